@@ -1,0 +1,65 @@
+/* Handle-based entry points of libmocha_b200.so for the B200 token loop.
+ *
+ * These run the reference host's whole token loop (src/minimind.cpp:110-182: prompt
+ * steps that only fill the KV cache, projection at the last prompt position,
+ * penalty + control mask + greedy or top-k/top-p/xorshift32 sampling, EOS stop) on
+ * the device, with an explicit device index so several replicas can run in one
+ * process.  They sit alongside the reference ABI (mocha_minimind.h), which stays
+ * the drop-in boundary; there is no reference counterpart for the handles
+ * themselves.  All functions return 0 on success and 1 on error (message on
+ * stderr). */
+#ifndef MOCHA_B200_H
+#define MOCHA_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mocha_q8 mocha_q8;
+
+/* Sampling settings with the reference CLI's meaning (mocha-llm:69-73):
+ * temperature 0 = greedy; top_k in [1,64] on the device path; top_p in (0,1];
+ * repeat_penalty >= 1 over the last 64 tokens; seed = xorshift32 start state. */
+typedef struct {
+    float temperature;
+    int top_k;
+    float top_p;
+    float repeat_penalty;
+    unsigned seed;
+} mocha_sampling;
+
+typedef struct {
+    double prefill_s;  /* prompt positions, measured with CUDA events */
+    double decode_s;   /* generated tokens after the first, CUDA events */
+    int generated;     /* tokens before EOS (EOS itself is not counted) */
+} mocha_timing;
+
+/* Number of visible CUDA devices with compute capability 10.x. */
+int mocha_b200_device_count(void);
+
+/* Upload a grouped-Q8 Qwen2.5-0.5B file (reference format) to `device`. */
+int mocha_q8_open(int device, const void *file, unsigned long long bytes, mocha_q8 **out);
+int mocha_q8_close(mocha_q8 *h);
+
+/* One step for `token` at `pos` (same as gpu_forward on a handle). */
+int mocha_q8_forward(mocha_q8 *h, int token, int pos, int project, float *logits);
+
+/* Run the token loop: n_prompt prompt tokens, then up to n_new sampled tokens,
+ * written to out_tokens (capacity n_new); *n_out = tokens before EOS.
+ * n_prompt + n_new <= 1024 as in the reference (src/minimind.cpp:98). */
+int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s,
+                      int *out_tokens, int *n_out, mocha_timing *timing);
+
+/* Device-timed decode: after the KV cache holds positions [0, pos0), run `warmup`
+ * then `steps` greedy steps with the token fed back on the device, starting at
+ * (token, pos0) and restarting at pos0 whenever the position reaches pos_end.
+ * *ms = CUDA-event time of the timed steps. */
+int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int warmup, int steps, float *ms);
+
+/* Number of this library's kernel launches per decode step (projection + sampling). */
+int mocha_q8_launches_per_step(mocha_q8 *h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

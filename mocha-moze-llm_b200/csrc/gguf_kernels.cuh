@@ -1,0 +1,51 @@
+// GGUF K-quant / Q8_0 weights on B200: device layout, repack, dequant and GEMV.
+//
+// Block formats are ggml's.  In HBM every block is stored so that all vector loads
+// are 16-byte aligned, with exactly the file's bytes per block:
+//   Q4_K: the 144-byte block unchanged (16-byte header d, dmin, 12 scale bytes,
+//         then 128 bytes of nibbles);
+//   Q6_K: a 208-byte body (ql 128, qh 64, int8 scales 16) per block in one array
+//         [rows][blocks][208] and the fp16 d in a second array [rows][blocks];
+//   Q8_0: int8 quants [rows][cols] and fp16 d [rows][cols/32].
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gguf {
+
+enum Type { Q8_0 = 8, Q4_K = 12, Q6_K = 14 };
+
+// Bytes of one file row, or 0 when type/cols are unsupported.
+inline unsigned row_bytes(int type, int cols)
+{
+    if (cols <= 0) return 0;
+    if (type == Q8_0) return cols % 32 ? 0 : (unsigned)(cols / 32) * 34u;
+    if (type == Q4_K) return cols % 256 ? 0 : (unsigned)(cols / 256) * 144u;
+    if (type == Q6_K) return cols % 256 ? 0 : (unsigned)(cols / 256) * 210u;
+    return 0;
+}
+
+// A weight matrix resident in the device layout above.
+struct DevMat {
+    int type;
+    int rows, cols;
+    const uint8_t *body;     // Q4_K blocks / Q6_K bodies / Q8_0 quants
+    const uint16_t *d;       // Q6_K and Q8_0 fp16 scales (null for Q4_K)
+};
+
+// Bytes of device storage for a matrix (same as the file's).
+inline size_t dev_bytes(int type, int rows, int cols) { return (size_t)row_bytes(type, cols) * rows; }
+
+// Repack `rows` file rows (raw, already on the device) into `dst` (dev_bytes long).
+int enqueue_repack(int type, const uint8_t *raw, int rows, int cols, uint8_t *dst, cudaStream_t s);
+DevMat make_devmat(int type, int rows, int cols, uint8_t *dst);
+
+// out[r*cols + c] = dequantised weight, exact (no fused multiply-add), for checking.
+int enqueue_dequant(const DevMat &m, float *out, cudaStream_t s);
+
+// y[v*y_stride_f + r] = sum_c W[r][c] * x[v*x_stride_f + c] for v < vectors (fp32
+// activations, fp32 accumulation); strides in floats.
+int enqueue_gemv(const DevMat &m, const float *x, int vectors, int x_stride_f, float *y, int y_stride_f,
+                 cudaStream_t s);
+
+}  // namespace gguf

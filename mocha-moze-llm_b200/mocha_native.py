@@ -1,0 +1,152 @@
+"""ctypes view of libmocha_b200.so (the C ABI in include/*.h) and of the build.
+
+The library is the product; this module only loads it and declares the argument
+types, mirroring the reference's C entry points (src/minimind.h:16-22,
+src/gguf-cuda.cu:110) and the handle API of include/mocha_b200.h.  It never falls
+back to anything: when the shared object is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(PKG_DIR, "libmocha_b200.so")
+INCLUDE_DIR = os.path.join(ROOT, "include")
+
+
+class MochaSampling(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("repeat_penalty", C.c_float), ("seed", C.c_uint)]
+
+
+class MochaTiming(C.Structure):
+    _fields_ = [("prefill_s", C.c_double), ("decode_s", C.c_double), ("generated", C.c_int)]
+
+
+_SIGS = {
+    # reference engine ABI
+    "gpu_init": (C.c_int, [C.c_void_p, C.c_uint]),
+    "gpu_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "gpu_finish": (C.c_int, []),
+    "gpu_head_init": (C.c_int, [C.c_void_p]),
+    "gpu_head_start": (C.c_int, [C.c_void_p, C.c_int]),
+    "gpu_head_finish": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "gpu_collect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_int]),
+    # reference GGUF bridge
+    "mocha_gguf_matmul": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_uint,
+                                    C.c_void_p, C.c_uint]),
+    "mocha_gguf_dequant": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    # handle API
+    "mocha_b200_device_count": (C.c_int, []),
+    "mocha_q8_open": (C.c_int, [C.c_int, C.c_void_p, C.c_ulonglong, C.POINTER(C.c_void_p)]),
+    "mocha_q8_close": (C.c_int, [C.c_void_p]),
+    "mocha_q8_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "mocha_q8_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(MochaSampling),
+                                    C.c_void_p, C.POINTER(C.c_int), C.POINTER(MochaTiming)]),
+    "mocha_q8_bench_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.POINTER(C.c_float)]),
+    "mocha_q8_launches_per_step": (C.c_int, [C.c_void_p]),
+}
+
+
+def build(verbose: bool = False) -> str:
+    """Compile libmocha_b200.so for sm_100a with the package Makefile."""
+    out = subprocess.run(["make", "-C", PKG_DIR, "-j", str(min(8, os.cpu_count() or 1))],
+                         capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("libmocha_b200 build failed:\n" + out.stdout[-4000:] + out.stderr[-4000:])
+    if verbose:
+        print(out.stdout)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Load the library (raises OSError when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise OSError(f"{path} missing: build it with `make -C {PKG_DIR}` (no fallback exists)")
+        lib = C.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def declared_functions() -> list[str]:
+    """Every function name declared in include/*.h."""
+    import re
+    names = []
+    for fn in sorted(os.listdir(INCLUDE_DIR)):
+        if fn.endswith(".h"):
+            text = open(os.path.join(INCLUDE_DIR, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"^\s*(?:int|void|float|unsigned)\s+\**(\w+)\s*\(", text, flags=re.M)
+    return names
+
+
+class Q8Handle:
+    """A grouped-Q8 model resident on one device (mocha_q8 handle)."""
+
+    def __init__(self, device: int, file_bytes, lib: C.CDLL | None = None):
+        self.lib = lib or load()
+        self._buf = file_bytes  # keep the host buffer alive while opening
+        ptr = C.c_void_p()
+        addr, size = _addr(file_bytes)
+        if self.lib.mocha_q8_open(device, addr, size, C.byref(ptr)) != 0:
+            raise RuntimeError("mocha_q8_open failed")
+        self.h = ptr
+
+    def close(self):
+        if self.h:
+            self.lib.mocha_q8_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, token: int, pos: int, project: bool = True):
+        import numpy as np
+        out = np.empty(151936, dtype=np.float32)
+        rc = self.lib.mocha_q8_forward(self.h, token, pos, int(project), out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError("mocha_q8_forward failed")
+        return out
+
+    def generate(self, prompt, n_new, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0, seed=42):
+        import numpy as np
+        p = np.asarray(prompt, dtype=np.int32)
+        out = np.zeros(n_new, dtype=np.int32)
+        n = C.c_int()
+        t = MochaTiming()
+        s = MochaSampling(temperature, top_k, top_p, penalty, seed)
+        rc = self.lib.mocha_q8_generate(self.h, p.ctypes.data, len(p), n_new, C.byref(s), out.ctypes.data,
+                                        C.byref(n), C.byref(t))
+        if rc != 0:
+            raise RuntimeError("mocha_q8_generate failed")
+        return out[:n.value].tolist(), t
+
+    def bench_decode(self, token, pos0, pos_end, warmup, steps) -> float:
+        ms = C.c_float()
+        rc = self.lib.mocha_q8_bench_decode(self.h, token, pos0, pos_end, warmup, steps, C.byref(ms))
+        if rc != 0:
+            raise RuntimeError("mocha_q8_bench_decode failed")
+        return ms.value
+
+
+def _addr(buf):
+    """(address, size) of a bytes-like / numpy / mmap buffer without copying."""
+    import numpy as np
+    arr = np.frombuffer(buf, dtype=np.uint8) if not isinstance(buf, np.ndarray) else buf
+    return arr.ctypes.data, arr.nbytes

@@ -1,0 +1,147 @@
+"""ctypes access to the CPU oracle (liboracle.so) -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+REF_DIR = os.path.join(HERE, "_ref")
+VOCAB = 151936
+DIM = 896
+
+
+def build(ref: bool = True) -> None:
+    """Build liboracle.so and, when the reference sources exist, oracle/_ref."""
+    subprocess.run(["make", "-C", HERE, "all"], check=True, capture_output=True)
+    if ref and os.path.isdir("/root/reference/src"):
+        subprocess.run(["make", "-C", HERE, "ref"], check=True, capture_output=True)
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build(ref=False)
+        L = C.CDLL(LIB)
+        L.q8o_create.restype = C.c_void_p
+        L.q8o_create.argtypes = [C.c_void_p, C.c_size_t]
+        L.q8o_destroy.argtypes = [C.c_void_p]
+        L.q8o_reset.argtypes = [C.c_void_p]
+        L.q8o_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        L.q8o_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_uint, C.c_uint, C.c_void_p, C.c_void_p, C.c_int,
+                                 C.c_uint]
+        L.q8o_rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p]
+        L.q8o_sample.restype = C.c_int
+        L.q8o_sample.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_float, C.c_int,
+                                 C.c_float, C.POINTER(C.c_uint32), C.c_int]
+        L.q8o_collect.restype = C.c_int
+        L.q8o_collect.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_int]
+        L.gguf_o_half.restype = C.c_float
+        L.gguf_o_half.argtypes = [C.c_uint16]
+        L.gguf_o_row_bytes.restype = C.c_uint
+        L.gguf_o_row_bytes.argtypes = [C.c_int, C.c_int]
+        L.gguf_o_dequant_row.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+        L.gguf_o_matmul.restype = C.c_int
+        L.gguf_o_matmul.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_uint,
+                                    C.c_void_p, C.c_uint]
+        _lib = L
+    return _lib
+
+
+class Q8Oracle:
+    """The reference CPU forward restated in C, with its own KV cache."""
+
+    def __init__(self, file_bytes):
+        self._arr = file_bytes if isinstance(file_bytes, np.ndarray) else np.frombuffer(file_bytes, dtype=np.uint8)
+        self.m = lib().q8o_create(self._arr.ctypes.data, self._arr.nbytes)
+        if not self.m:
+            raise ValueError("oracle rejected the model file")
+
+    def __del__(self):
+        if getattr(self, "m", None):
+            lib().q8o_destroy(self.m)
+            self.m = None
+
+    def reset(self):
+        lib().q8o_reset(self.m)
+
+    def forward(self, token: int, pos: int, project: bool = True, hidden_only: bool = False):
+        out = np.zeros(DIM if hidden_only else VOCAB, dtype=np.float32)
+        lib().q8o_forward(self.m, token, pos, int(project), int(hidden_only), out.ctypes.data)
+        return out
+
+    def generate(self, prompt, n, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0, seed=42, logits_at=()):
+        """Token loop of src/minimind.cpp:110-182 (cpu backend); returns tokens and
+        the raw logits at the requested decode steps."""
+        self.reset()
+        history = list(prompt)
+        token = prompt[0]
+        s = C.c_uint32(seed)
+        out, kept = [], {}
+        for pos in range(len(prompt) + n - 1):
+            project = pos + 1 >= len(prompt)
+            logits = self.forward(token, pos, project)
+            if pos + 1 < len(prompt):
+                token = prompt[pos + 1]
+                continue
+            step = len(out)
+            if step in logits_at:
+                kept[step] = logits.copy()
+            h = np.asarray(history, dtype=np.int32)
+            token = lib().q8o_sample(logits.ctypes.data, VOCAB, h.ctypes.data, len(h), penalty, temperature,
+                                     top_k, top_p, C.byref(s), 0)
+            if token == 151645:
+                break
+            out.append(token)
+            history.append(token)
+        return out, kept
+
+
+def sample(logits, history, temperature, top_k, top_p, penalty, seed, skip_penalty=False):
+    arr = np.array(logits, dtype=np.float32)
+    h = np.asarray(history, dtype=np.int32)
+    s = C.c_uint32(seed)
+    tok = lib().q8o_sample(arr.ctypes.data, len(arr), h.ctypes.data, len(h), penalty, temperature, top_k, top_p,
+                           C.byref(s), int(skip_penalty))
+    return tok, s.value, arr
+
+
+def collect(logits, recent, penalty, k, rows):
+    out = np.empty(rows, dtype=np.float32)
+    r = np.asarray(recent, dtype=np.int32)
+    rc = lib().q8o_collect(np.ascontiguousarray(logits, dtype=np.float32).ctypes.data, out.ctypes.data,
+                           r.ctypes.data, len(r), penalty, k, rows)
+    if rc:
+        raise ValueError("bad k/count")
+    return out
+
+
+def gguf_dequant(type_id: int, raw: bytes, rows: int, cols: int):
+    rb = lib().gguf_o_row_bytes(type_id, cols)
+    a = np.frombuffer(raw, dtype=np.uint8)
+    out = np.empty((rows, cols), dtype=np.float32)
+    for r in range(rows):
+        lib().gguf_o_dequant_row(type_id, a.ctypes.data + r * rb, cols, out[r].ctypes.data)
+    return out
+
+
+def gguf_matmul(type_id, raw, cols, rows, x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    v = x.shape[0]
+    y = np.empty((v, rows), dtype=np.float32)
+    a = np.frombuffer(raw, dtype=np.uint8)
+    rc = lib().gguf_o_matmul(type_id, a.ctypes.data, cols, rows, x.ctypes.data, v, cols * 4, y.ctypes.data,
+                             rows * 4)
+    if rc:
+        raise ValueError("gguf_o_matmul rejected the arguments")
+    return y
