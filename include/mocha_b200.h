@@ -50,6 +50,15 @@ int mocha_q8_forward(mocha_q8 *h, int token, int pos, int project, float *logits
 int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s,
                       int *out_tokens, int *n_out, mocha_timing *timing);
 
+/* Streaming form of mocha_q8_generate for hosts that print tokens as they come
+ * (the reference host prints one id per line, src/minimind.cpp:181).  begin enqueues
+ * the prompt steps and a few decode steps; each next returns the next sampled token
+ * (EOS included, once) and keeps a fixed number of steps in flight; *token = -1 once
+ * the stream has ended.  end waits for the steps still in flight. */
+int mocha_q8_stream_begin(mocha_q8 *h, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s);
+int mocha_q8_stream_next(mocha_q8 *h, int *token);
+int mocha_q8_stream_end(mocha_q8 *h);
+
 /* Device-timed decode: after the KV cache holds positions [0, pos0), run `warmup`
  * then `steps` greedy steps with the token fed back on the device, starting at
  * (token, pos0) and restarting at pos0 whenever the position reaches pos_end.
@@ -58,6 +67,10 @@ int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int war
 
 /* Number of this library's kernel launches per decode step (projection + sampling). */
 int mocha_q8_launches_per_step(mocha_q8 *h);
+
+/* Forward steps and kernel launches issued on this handle so far (the counters the
+ * reference prints at exit as CUDA_FORWARD_STEPS / CUDA_KERNEL_CALLS). */
+int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches);
 
 #ifdef __cplusplus
 }

@@ -83,7 +83,11 @@ struct mocha_q8 {
     int *d_hist = nullptr, *h_hist = nullptr;  // [64 ids][count]
     unsigned long long *d_scratch = nullptr, *d_keys = nullptr, *h_keys = nullptr;
     float *h_logits = nullptr;
-    int *d_prompt = nullptr, *d_out = nullptr, *d_out_count = nullptr, *h_pos0 = nullptr;
+    int *d_prompt = nullptr, *h_pos0 = nullptr;
+    int *h_out = nullptr, *h_out_count = nullptr;  // mapped pinned ring written by the sampler
+    int *d_out = nullptr, *d_out_count = nullptr;  // their device addresses
+    int stream_total = 0, stream_enqueued = 0, stream_read = 0;
+    bool stream_done = true;
     cudaGraphExec_t g_forward[2] = {nullptr, nullptr};
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
     cudaEvent_t ev[4] = {};
@@ -239,8 +243,11 @@ int open_full(mocha_q8 *h, int device, const void *file, size_t bytes)
     memset(h->h_state, 0, sizeof(q8::DecodeState));
     TRY(cudaMallocHost(&h->h_pos0, sizeof(int) * 2));
     TRY(cudaMalloc(&h->d_prompt, sizeof(int) * CONTEXT));
-    TRY(cudaMalloc(&h->d_out, sizeof(int) * (CONTEXT + 1)));
-    TRY(cudaMalloc(&h->d_out_count, sizeof(int)));
+    TRY(cudaHostAlloc(&h->h_out, sizeof(int) * sampling::kOutRing, cudaHostAllocMapped));
+    TRY(cudaHostAlloc(&h->h_out_count, sizeof(int), cudaHostAllocMapped));
+    TRY(cudaHostGetDevicePointer(&h->d_out, h->h_out, 0));
+    TRY(cudaHostGetDevicePointer(&h->d_out_count, h->h_out_count, 0));
+    *h->h_out_count = 0;
     if (capture(h, &h->g_forward[0], 0) || capture(h, &h->g_forward[1], 1) || capture(h, &h->g_prefill, 2) ||
         capture(h, &h->g_decode, 3))
         return 1;
@@ -261,10 +268,11 @@ void release(mocha_q8 *h)
         if (e) cudaEventDestroy(e);
     void *dev[] = {h->d_file, h->dm, h->b.x, h->b.q, h->b.kc, h->b.vc, h->b.partial, h->b.h, h->b.logits,
                    h->b.hidden, (void *)h->b.rope_cos, h->b.st, h->d_seq, h->d_params, h->d_hist,
-                   h->d_scratch, h->d_keys, h->d_prompt, h->d_out, h->d_out_count};
+                   h->d_scratch, h->d_keys, h->d_prompt};
     for (void *p : dev)
         if (p) cudaFree(p);
-    void *host[] = {h->h_state, h->h_params, h->h_hist, h->h_keys, h->h_logits, h->h_pos0};
+    void *host[] = {h->h_state, h->h_params, h->h_hist, h->h_keys, h->h_logits, h->h_pos0, h->h_out,
+                    h->h_out_count};
     for (void *p : host)
         if (p) cudaFreeHost(p);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -316,6 +324,7 @@ int forward_step(mocha_q8 *h, float *logits, int token, int pos, int project, in
 }
 
 mocha_q8 *g_engine = nullptr;  // the reference ABI's single per-process model
+constexpr int kStreamAhead = 8;  // decode steps kept enqueued ahead of the host reader
 
 int env_device()
 {
@@ -499,25 +508,37 @@ extern "C" int mocha_q8_forward(mocha_q8 *h, int token, int pos, int project, fl
     return forward_step(h, logits, token, pos, project, 1, false);
 }
 
+extern "C" int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches)
+{
+    if (!h) return 1;
+    if (steps) *steps = h->calls;
+    if (launches) *launches = h->kernel_calls;
+    return 0;
+}
+
 extern "C" int mocha_q8_launches_per_step(mocha_q8 *h)
 {
     (void)h;
     return q8::forward_launches(true) + 1 + 3;  // forward + step counter + top-k (2) + sample
 }
 
-extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s,
-                                 int *out_tokens, int *n_out, mocha_timing *timing)
+namespace {
+
+bool valid_sampling(const mocha_sampling *s)
 {
-    if (!h || h->head_only || !prompt || !s || !out_tokens || n_prompt < 1 || n_new < 1 ||
-        n_prompt + n_new > CONTEXT || !(s->temperature >= 0.f) || !(s->repeat_penalty >= 1.f) ||
-        (s->temperature > 0.f && (s->top_k < 1 || s->top_k > sampling::kMaxK)) || !(s->top_p > 0.f && s->top_p <= 1.f)) {
-        fprintf(stderr, "MOCHA_B200: mocha_q8_generate: invalid arguments\n");
-        return 1;
-    }
+    return s && s->temperature >= 0.f && s->temperature < 1e30f && s->repeat_penalty >= 1.f &&
+           s->repeat_penalty < 1e30f && (s->temperature == 0.f || (s->top_k >= 1 && s->top_k <= sampling::kMaxK)) &&
+           s->top_p > 0.f && s->top_p <= 1.f;
+}
+
+// Sequence set-up shared by generate and the stream: history ring = last <= 64
+// prompt tokens, xorshift seed, prompt upload, state at (prompt[0], 0), ring reset.
+int begin_sequence(mocha_q8 *h, const int *prompt, int n_prompt, const mocha_sampling *s)
+{
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= VOCAB) return 1;
     TRY(cudaSetDevice(h->device));
-    // sequence state: history ring = last <= 64 prompt tokens; xorshift seed
+    TRY(cudaStreamSynchronize(h->stream));
     sampling::SeqState seq;
     memset(&seq, 0, sizeof seq);
     const int first = n_prompt > sampling::kHistory ? n_prompt - sampling::kHistory : 0;
@@ -531,7 +552,22 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
     h->h_state->token = prompt[0];
     h->h_state->pos = 0;
     TRY(cudaMemcpyAsync(h->b.st, h->h_state, 2 * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    TRY(cudaMemsetAsync(h->d_out_count, 0, sizeof(int), h->stream));
+    TRY(cudaStreamSynchronize(h->stream));  // the seq copy above reads a stack buffer
+    __atomic_store_n(h->h_out_count, 0, __ATOMIC_SEQ_CST);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s,
+                                 int *out_tokens, int *n_out, mocha_timing *timing)
+{
+    if (!h || h->head_only || !prompt || !out_tokens || n_prompt < 1 || n_new < 1 || n_prompt + n_new > CONTEXT ||
+        !valid_sampling(s)) {
+        fprintf(stderr, "MOCHA_B200: mocha_q8_generate: invalid arguments\n");
+        return 1;
+    }
+    if (begin_sequence(h, prompt, n_prompt, s)) return 1;
     TRY(cudaEventRecord(h->ev[0], h->stream));
     for (int p = 0; p + 1 < n_prompt; p++) TRY(cudaGraphLaunch(h->g_prefill, h->stream));
     TRY(cudaEventRecord(h->ev[1], h->stream));
@@ -539,9 +575,9 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
     TRY(cudaEventRecord(h->ev[2], h->stream));
     for (int i = 1; i < n_new; i++) TRY(cudaGraphLaunch(h->g_decode, h->stream));
     TRY(cudaEventRecord(h->ev[3], h->stream));
-    TRY(cudaMemcpyAsync(out_tokens, h->d_out, sizeof(int) * n_new, cudaMemcpyDeviceToHost, h->stream));
     TRY(cudaStreamSynchronize(h->stream));
     int n = 0;
+    for (int i = 0; i < n_new; i++) out_tokens[i] = h->h_out[i];
     while (n < n_new && out_tokens[n] != q8::EOS) n++;
     if (n_out) *n_out = n;
     if (timing) {
@@ -553,6 +589,77 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
         timing->generated = n;
     }
     h->calls += n_prompt - 1 + n_new;
+    h->kernel_calls += (uint64_t)(n_prompt - 1) * (q8::forward_launches(false) + 1) +
+                       (uint64_t)n_new * mocha_q8_launches_per_step(h);
+    return 0;
+}
+
+extern "C" int mocha_q8_stream_begin(mocha_q8 *h, const int *prompt, int n_prompt, int n_new,
+                                     const mocha_sampling *s)
+{
+    if (!h || h->head_only || !prompt || n_prompt < 1 || n_new < 1 || n_prompt + n_new > CONTEXT ||
+        !valid_sampling(s)) {
+        fprintf(stderr, "MOCHA_B200: mocha_q8_stream_begin: invalid arguments\n");
+        return 1;
+    }
+    if (begin_sequence(h, prompt, n_prompt, s)) return 1;
+    for (int p = 0; p + 1 < n_prompt; p++) TRY(cudaGraphLaunch(h->g_prefill, h->stream));
+    h->stream_total = n_new;
+    h->stream_read = 0;
+    h->stream_enqueued = 0;
+    h->stream_done = false;
+    const int ahead = n_new < kStreamAhead ? n_new : kStreamAhead;
+    for (int i = 0; i < ahead; i++) TRY(cudaGraphLaunch(h->g_decode, h->stream));
+    h->stream_enqueued = ahead;
+    h->calls += n_prompt - 1;
+    h->kernel_calls += (uint64_t)(n_prompt - 1) * (q8::forward_launches(false) + 1);
+    return 0;
+}
+
+extern "C" int mocha_q8_stream_next(mocha_q8 *h, int *token)
+{
+    if (!h || !token) return 1;
+    if (h->stream_done || h->stream_read >= h->stream_total) {
+        *token = -1;
+        return 0;
+    }
+    // wait for the sampler's write to the mapped ring; poll the stream for errors
+    long spins = 0;
+    while (__atomic_load_n(h->h_out_count, __ATOMIC_ACQUIRE) <= h->stream_read) {
+        if (++spins % 4096 == 0) {
+            const cudaError_t e = cudaStreamQuery(h->stream);
+            if (e != cudaSuccess && e != cudaErrorNotReady) {
+                fprintf(stderr, "CUDA decode stream: %d %s\n", (int)e, cudaGetErrorString(e));
+                h->stream_done = true;
+                return 1;
+            }
+            if (e == cudaSuccess && __atomic_load_n(h->h_out_count, __ATOMIC_ACQUIRE) <= h->stream_read) {
+                fprintf(stderr, "MOCHA_B200: decode stream idle without a token\n");
+                h->stream_done = true;
+                return 1;
+            }
+        }
+    }
+    const int t = h->h_out[h->stream_read % sampling::kOutRing];
+    h->stream_read++;
+    h->calls++;
+    h->kernel_calls += mocha_q8_launches_per_step(h);
+    if (t == q8::EOS || h->stream_read >= h->stream_total) {
+        h->stream_done = true;
+    } else if (h->stream_enqueued < h->stream_total) {
+        TRY(cudaGraphLaunch(h->g_decode, h->stream));
+        h->stream_enqueued++;
+    }
+    *token = t;
+    return 0;
+}
+
+extern "C" int mocha_q8_stream_end(mocha_q8 *h)
+{
+    if (!h) return 1;
+    h->stream_done = true;
+    TRY(cudaSetDevice(h->device));
+    TRY(cudaStreamSynchronize(h->stream));
     return 0;
 }
 
@@ -566,13 +673,11 @@ extern "C" int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_e
     h->h_pos0[0] = token;
     h->h_pos0[1] = pos0;
     TRY(cudaMemcpyAsync(h->b.st, h->h_pos0, 2 * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    TRY(cudaMemsetAsync(h->d_out_count, 0, sizeof(int), h->stream));
     int pos = pos0;
     for (int i = 0; i < warmup + steps; i++) {
         if (i == warmup) TRY(cudaEventRecord(h->ev[0], h->stream));
         if (pos == pos_end) {
             TRY(cudaMemcpyAsync(&h->b.st->pos, h->h_pos0 + 1, sizeof(int), cudaMemcpyHostToDevice, h->stream));
-            TRY(cudaMemsetAsync(h->d_out_count, 0, sizeof(int), h->stream));
             pos = pos0;
         }
         TRY(cudaGraphLaunch(h->g_decode, h->stream));

@@ -180,7 +180,13 @@ __global__ void k_sample(const unsigned long long *__restrict__ keys, const Para
     if (token == p.eos) st->finished = 1;
     *token_out = token;
     if (pos_inout) (*pos_inout)++;
-    if (out_ring) out_ring[(*out_count)++] = token;
+    if (out_ring) {
+        const int n = st->n_out;
+        out_ring[n % kOutRing] = token;
+        st->n_out = n + 1;
+        __threadfence_system();
+        *(volatile int *)out_count = n + 1;
+    }
 }
 
 }  // namespace

@@ -27,7 +27,10 @@ struct SeqState {
     uint32_t seed;          // xorshift32 state
     int last_token;         // token sampled by the last step
     int finished;           // EOS seen
+    int n_out;              // tokens written to the output ring
 };
+
+constexpr int kOutRing = 1024;  // output ring entries (index = n_out % kOutRing)
 
 // Top-k candidate keys of logits[0..rows) after penalty (on the distinct ids of
 // history[0..*count), device memory, order irrelevant) and mask.  keys_out receives k keys, best first.
@@ -38,7 +41,9 @@ int enqueue_topk(const float *logits, int rows, const int *history, const int *c
 
 // Draw the next token from the sorted candidate keys (greedy when temperature == 0),
 // exactly as the reference host sampler does (src/minimind.cpp:171-179), then push it
-// into the history ring and write it to *token_out (and out_ring[*out_count] if given).
+// into the history ring, write it to *token_out and, when out_ring is given, to
+// out_ring[n_out % kOutRing] followed (after a system fence) by *out_count = n_out + 1;
+// the ring may live in mapped host memory so a host thread can stream tokens.
 int enqueue_sample(const unsigned long long *keys, const Params *p, SeqState *st, int *token_out,
                    int *pos_inout, int *out_ring, int *out_count, cudaStream_t stream);
 

@@ -140,3 +140,37 @@ def test_reference_host_drop_in(golden_q8, q8_model_path):
                          s["top_k"], s["top_p"])
     assert p.returncode == 0, p.stderr[-2000:]
     assert [int(t) for t in p.stdout.split()] == s["tokens"]
+
+
+def test_stream_api_matches_generate(native, handle, golden_q8):
+    lib = native.load()
+    c = golden_q8["cases"]["sampled64"]
+    p = np.asarray(c["prompt"], np.int32)
+    s = native.MochaSampling(c["temperature"], c["top_k"], c["top_p"], c["penalty"], c["seed"])
+    assert lib.mocha_q8_stream_begin(handle.h, p.ctypes.data, len(p), c["n"], ctypes.byref(s)) == 0
+    got, t = [], ctypes.c_int()
+    while True:
+        assert lib.mocha_q8_stream_next(handle.h, ctypes.byref(t)) == 0
+        if t.value < 0 or t.value == 151645:
+            break
+        got.append(t.value)
+    assert lib.mocha_q8_stream_end(handle.h) == 0
+    assert got == c["tokens"]
+
+
+def test_engine_binary_matches_reference(golden_q8, q8_model_path):
+    """mocha-qwen-engine keeps the reference engine's argv protocol and output lines."""
+    binary = os.path.join(ROOT, "mocha-moze-llm_b200", "bin", "mocha-qwen-engine")
+    for case in ("greedy256", "sampled64"):
+        c = golden_q8["cases"][case]
+        p, m = _run_ref_host(binary, q8_model_path, c["prompt"], c["n"], "cuda", 0, c["penalty"], c["temperature"],
+                             c["top_k"], c["top_p"])
+        assert p.returncode == 0, p.stderr[-2000:]
+        assert [int(t) for t in p.stdout.split()] == c["tokens"]
+        assert int(m["GENERATED"]) == len(c["tokens"]) and float(m["DECODE_TPS"]) > 0
+        assert "CUDA_FORWARD_STEPS" in m
+    # argument errors keep the reference's exit code 2
+    p, _ = _run_ref_host(binary, q8_model_path, [1, 2], 2000, "cuda", 0)
+    assert p.returncode == 2
+    p, _ = _run_ref_host(binary, q8_model_path, [1, 2], 4, "cuda", 1)
+    assert p.returncode == 2
