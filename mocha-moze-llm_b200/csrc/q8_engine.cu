@@ -16,6 +16,7 @@
 #include "mocha_b200.h"
 #include "mocha_minimind.h"
 #include "q8_decode.cuh"
+#include "q8_persistent.cuh"
 #include "sampling.cuh"
 
 namespace {
@@ -91,6 +92,16 @@ struct mocha_q8 {
     cudaGraphExec_t g_forward[2] = {nullptr, nullptr};
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
     cudaEvent_t ev[4] = {};
+    // persistent one-launch-per-token path (default) and its state
+    bool persistent = true;
+    q8p::Plan hplan{};
+    q8p::Plan *dplan = nullptr;
+    q8p::Chunk *dchunks = nullptr;
+    uint8_t *dstream = nullptr;
+    size_t stream_bytes = 0;
+    q8p::Sync *dsync = nullptr;
+    q8p::Scratch scr{};
+    unsigned *h_err = nullptr, *d_err = nullptr;  // mapped error word of the bounded waits
     unsigned long long calls = 0, kernel_calls = 0;
     double transformer_s = 0, head_s = 0, copy_s = 0;
 };
@@ -134,7 +145,11 @@ int capture(mocha_q8 *h, cudaGraphExec_t *out, int kind)
     cudaGraph_t g = nullptr;
     TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     int rc = 0;
-    if (kind == 0 || kind == 1) {  // bare forward without / with projection
+    if (h->persistent) {
+        static const int modes[4] = {q8p::FORWARD, q8p::FORWARD_PROJECT, q8p::PREFILL, q8p::DECODE};
+        rc = q8p::enqueue_step(h->dm, h->dplan, h->b, h->dsync, h->scr, modes[kind], h->d_params, h->d_seq, h->d_out,
+                               h->d_out_count, h->d_prompt, h->d_err, h->stream);
+    } else if (kind == 0 || kind == 1) {  // bare forward without / with projection
         rc = q8::enqueue_forward(h->dm, h->hm, h->b, kind == 1, h->stream);
         if (!rc) k_count_step<<<1, 1, 0, h->stream>>>(h->b.st);
     } else if (kind == 2) {  // prompt step: fill KV, advance to the next prompt token
@@ -248,6 +263,25 @@ int open_full(mocha_q8 *h, int device, const void *file, size_t bytes)
     TRY(cudaHostGetDevicePointer(&h->d_out, h->h_out, 0));
     TRY(cudaHostGetDevicePointer(&h->d_out_count, h->h_out_count, 0));
     *h->h_out_count = 0;
+    const char *mode = getenv("MOCHA_B200_DECODE");
+    h->persistent = !(mode && strcmp(mode, "graph") == 0);
+    if (h->persistent) {
+        if (q8p::init_device()) return 1;
+        if (q8p::build_plan(hd, (const unsigned char *)file, &h->hplan, &h->dchunks, &h->dstream, &h->stream_bytes,
+                            h->stream))
+            return 1;
+        TRY(cudaMalloc(&h->dplan, sizeof(q8p::Plan)));
+        TRY(cudaMemcpy(h->dplan, &h->hplan, sizeof(q8p::Plan), cudaMemcpyHostToDevice));
+        TRY(cudaMalloc(&h->dsync, sizeof(q8p::Sync)));
+        TRY(cudaMemset(h->dsync, 0, sizeof(q8p::Sync)));
+        TRY(cudaMalloc(&h->scr.o, sizeof(float) * DIM));
+        TRY(cudaMalloc(&h->scr.partial, sizeof(float) * q8::KV_HEADS * (CONTEXT / q8p::kAttnChunk) * q8::GQA *
+                                            q8::ATTN_PARTIAL));
+        TRY(cudaMalloc(&h->scr.cand, sizeof(unsigned long long) * q8p::kCTAs * sampling::kMaxK));
+    }
+    TRY(cudaHostAlloc(&h->h_err, sizeof(unsigned), cudaHostAllocMapped));
+    TRY(cudaHostGetDevicePointer(&h->d_err, h->h_err, 0));
+    *h->h_err = 0;
     if (capture(h, &h->g_forward[0], 0) || capture(h, &h->g_forward[1], 1) || capture(h, &h->g_prefill, 2) ||
         capture(h, &h->g_decode, 3))
         return 1;
@@ -268,11 +302,12 @@ void release(mocha_q8 *h)
         if (e) cudaEventDestroy(e);
     void *dev[] = {h->d_file, h->dm, h->b.x, h->b.q, h->b.kc, h->b.vc, h->b.partial, h->b.h, h->b.logits,
                    h->b.hidden, (void *)h->b.rope_cos, h->b.st, h->d_seq, h->d_params, h->d_hist,
-                   h->d_scratch, h->d_keys, h->d_prompt};
+                   h->d_scratch, h->d_keys, h->d_prompt, h->dplan, h->dchunks, h->dstream, h->dsync, h->scr.o,
+                   h->scr.partial, h->scr.cand};
     for (void *p : dev)
         if (p) cudaFree(p);
     void *host[] = {h->h_state, h->h_params, h->h_hist, h->h_keys, h->h_logits, h->h_pos0, h->h_out,
-                    h->h_out_count};
+                    h->h_out_count, h->h_err};
     for (void *p : host)
         if (p) cudaFreeHost(p);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -293,6 +328,25 @@ int set_params(mocha_q8 *h, float penalty, float temperature, int top_k, float t
     return 0;
 }
 
+// A bounded wait inside the persistent kernel expired: report it, clear the
+// synchronisation words so the next step starts from a clean state, and fail.
+int check_device_error(mocha_q8 *h)
+{
+    if (!h->h_err) return 0;
+    const unsigned code = __atomic_load_n(h->h_err, __ATOMIC_ACQUIRE);
+    if (!code) return 0;
+    fprintf(stderr, "MOCHA_B200: persistent decode step aborted (wait expired, code %u)\n", code);
+    cudaStreamSynchronize(h->stream);
+    if (h->dsync) cudaMemset(h->dsync, 0, sizeof(q8p::Sync));
+    __atomic_store_n(h->h_err, 0u, __ATOMIC_RELEASE);
+    return 1;
+}
+
+int launches_per_forward(const mocha_q8 *h, bool project)
+{
+    return h->persistent ? 1 : q8::forward_launches(project) + 1;
+}
+
 int forward_step(mocha_q8 *h, float *logits, int token, int pos, int project, int readback, bool profile)
 {
     if (token < 0 || token >= VOCAB || pos < 0 || pos >= CONTEXT) {
@@ -308,6 +362,7 @@ int forward_step(mocha_q8 *h, float *logits, int token, int pos, int project, in
     const bool copy = project && readback && logits;
     if (copy) TRY(cudaMemcpyAsync(h->h_logits, h->b.logits, sizeof(float) * VOCAB, cudaMemcpyDeviceToHost, h->stream));
     TRY(cudaStreamSynchronize(h->stream));
+    if (check_device_error(h)) return 1;
     if (profile) {
         float ms = 0.f;
         TRY(cudaEventElapsedTime(&ms, h->ev[0], h->ev[1]));
@@ -319,7 +374,7 @@ int forward_step(mocha_q8 *h, float *logits, int token, int pos, int project, in
         h->copy_s += now_s() - t0;
     }
     h->calls++;
-    h->kernel_calls += q8::forward_launches(project) + 1;
+    h->kernel_calls += launches_per_forward(h, project);
     return 0;
 }
 
@@ -518,8 +573,9 @@ extern "C" int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigne
 
 extern "C" int mocha_q8_launches_per_step(mocha_q8 *h)
 {
-    (void)h;
-    return q8::forward_launches(true) + 1 + 3;  // forward + step counter + top-k (2) + sample
+    if (!h) return 0;
+    // persistent: one kernel; graph path: forward + step counter + top-k (2) + sample
+    return h->persistent ? 1 : q8::forward_launches(true) + 1 + 3;
 }
 
 namespace {
@@ -576,6 +632,7 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
     for (int i = 1; i < n_new; i++) TRY(cudaGraphLaunch(h->g_decode, h->stream));
     TRY(cudaEventRecord(h->ev[3], h->stream));
     TRY(cudaStreamSynchronize(h->stream));
+    if (check_device_error(h)) return 1;
     int n = 0;
     for (int i = 0; i < n_new; i++) out_tokens[i] = h->h_out[i];
     while (n < n_new && out_tokens[n] != q8::EOS) n++;
@@ -589,7 +646,7 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
         timing->generated = n;
     }
     h->calls += n_prompt - 1 + n_new;
-    h->kernel_calls += (uint64_t)(n_prompt - 1) * (q8::forward_launches(false) + 1) +
+    h->kernel_calls += (uint64_t)(n_prompt - 1) * launches_per_forward(h, false) +
                        (uint64_t)n_new * mocha_q8_launches_per_step(h);
     return 0;
 }
@@ -612,7 +669,7 @@ extern "C" int mocha_q8_stream_begin(mocha_q8 *h, const int *prompt, int n_promp
     for (int i = 0; i < ahead; i++) TRY(cudaGraphLaunch(h->g_decode, h->stream));
     h->stream_enqueued = ahead;
     h->calls += n_prompt - 1;
-    h->kernel_calls += (uint64_t)(n_prompt - 1) * (q8::forward_launches(false) + 1);
+    h->kernel_calls += (uint64_t)(n_prompt - 1) * launches_per_forward(h, false);
     return 0;
 }
 
@@ -627,6 +684,10 @@ extern "C" int mocha_q8_stream_next(mocha_q8 *h, int *token)
     long spins = 0;
     while (__atomic_load_n(h->h_out_count, __ATOMIC_ACQUIRE) <= h->stream_read) {
         if (++spins % 4096 == 0) {
+            if (check_device_error(h)) {
+                h->stream_done = true;
+                return 1;
+            }
             const cudaError_t e = cudaStreamQuery(h->stream);
             if (e != cudaSuccess && e != cudaErrorNotReady) {
                 fprintf(stderr, "CUDA decode stream: %d %s\n", (int)e, cudaGetErrorString(e));
@@ -660,7 +721,7 @@ extern "C" int mocha_q8_stream_end(mocha_q8 *h)
     h->stream_done = true;
     TRY(cudaSetDevice(h->device));
     TRY(cudaStreamSynchronize(h->stream));
-    return 0;
+    return check_device_error(h);
 }
 
 extern "C" int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int warmup, int steps, float *ms)
@@ -685,6 +746,7 @@ extern "C" int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_e
     }
     TRY(cudaEventRecord(h->ev[1], h->stream));
     TRY(cudaStreamSynchronize(h->stream));
+    if (check_device_error(h)) return 1;
     TRY(cudaEventElapsedTime(ms, h->ev[0], h->ev[1]));
     h->calls += warmup + steps;
     return 0;

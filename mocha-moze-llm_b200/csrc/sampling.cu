@@ -16,6 +16,7 @@
 
 #include "mb_common.cuh"
 #include "sampling.cuh"
+#include "sampling_dev.cuh"
 
 namespace sampling {
 namespace {
@@ -140,53 +141,13 @@ __global__ void k_sample(const unsigned long long *__restrict__ keys, const Para
 {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const Params p = *prm;
-    int token;
-    if (p.temperature == 0.f) {
-        token = mb::key_id(keys[0]);
-    } else {
-        float prob[kMaxK];
-        int ids[kMaxK];
-        const int k = min(max(p.top_k, 1), kMaxK);
-        const float largest = mb::key_value(keys[0]);
-        float sum = 0.f;
-        for (int j = 0; j < k; j++) {
-            ids[j] = mb::key_id(keys[j]);
-            prob[j] = expf((mb::key_value(keys[j]) - largest) / p.temperature);
-            sum += prob[j];
-        }
-        float cutoff = 0.f;
-        int kept = 0;
-        while (kept < k && cutoff < sum * p.top_p) cutoff += prob[kept++];
-        uint32_t s = st->seed;
-        s ^= s << 13;
-        s ^= s >> 17;
-        s ^= s << 5;
-        st->seed = s;
-        float r = (float)((s / 4294967296.0) * (double)cutoff);
-        token = ids[kept - 1];
-        for (int j = 0; j < kept; j++) {
-            r -= prob[j];
-            if (r <= 0.f) {
-                token = ids[j];
-                break;
-            }
-        }
-    }
+    uint32_t seed = st->seed;
+    int token = draw_token(keys, p, seed);
+    st->seed = seed;
     if (token < 0 || token >= p.vocab) token = p.eos;  // never index past the embedding
-    st->history[st->history_head] = token;
-    st->history_head = (st->history_head + 1) % kHistory;
-    if (st->history_count < kHistory) st->history_count++;
-    st->last_token = token;
-    if (token == p.eos) st->finished = 1;
+    record_token(token, p, st, out_ring, out_count);
     *token_out = token;
     if (pos_inout) (*pos_inout)++;
-    if (out_ring) {
-        const int n = st->n_out;
-        out_ring[n % kOutRing] = token;
-        st->n_out = n + 1;
-        __threadfence_system();
-        *(volatile int *)out_count = n + 1;
-    }
 }
 
 }  // namespace

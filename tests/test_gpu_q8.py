@@ -20,9 +20,18 @@ def masked_choice(logits):
     return int(np.argmax(l))
 
 
-@pytest.fixture(scope="module")
-def handle(native, q8_model_bytes):
-    h = native.Q8Handle(0, q8_model_bytes)
+@pytest.fixture(scope="module", params=["persistent", "graph"])
+def handle(request, native, q8_model_bytes):
+    """Both decode paths: one persistent launch per token, or the per-phase graph."""
+    old = os.environ.pop("MOCHA_B200_DECODE", None)
+    if request.param == "graph":
+        os.environ["MOCHA_B200_DECODE"] = "graph"
+    try:
+        h = native.Q8Handle(0, q8_model_bytes)
+    finally:
+        os.environ.pop("MOCHA_B200_DECODE", None)
+        if old is not None:
+            os.environ["MOCHA_B200_DECODE"] = old
     yield h
     h.close()
 
