@@ -68,6 +68,11 @@ int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int war
 /* Number of this library's kernel launches per decode step (projection + sampling). */
 int mocha_q8_launches_per_step(mocha_q8 *h);
 
+/* Diagnostic: one persistent step (forward + projection) for `token` at `pos` that
+ * records %globaltimer stamps at every phase boundary of every CTA into
+ * stamps[148][256] (0 = not reached).  Fails on the per-phase graph path. */
+int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps);
+
 /* Forward steps and kernel launches issued on this handle so far (the counters the
  * reference prints at exit as CUDA_FORWARD_STEPS / CUDA_KERNEL_CALLS). */
 int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches);

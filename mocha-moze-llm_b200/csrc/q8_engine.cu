@@ -101,6 +101,7 @@ struct mocha_q8 {
     size_t stream_bytes = 0;
     q8p::Sync *dsync = nullptr;
     q8p::Scratch scr{};
+    unsigned long long *dwords = nullptr;  // data words exchanged between CTAs
     unsigned *h_err = nullptr, *d_err = nullptr;  // mapped error word of the bounded waits
     unsigned long long calls = 0, kernel_calls = 0;
     double transformer_s = 0, head_s = 0, copy_s = 0;
@@ -116,6 +117,8 @@ namespace {
             return 1;                                                                            \
         }                                                                                        \
     } while (0)
+
+int reset_persistent(mocha_q8 *h);
 
 int check_device(int device, cudaDeviceProp *p)
 {
@@ -267,17 +270,16 @@ int open_full(mocha_q8 *h, int device, const void *file, size_t bytes)
     h->persistent = !(mode && strcmp(mode, "graph") == 0);
     if (h->persistent) {
         if (q8p::init_device()) return 1;
-        if (q8p::build_plan(hd, (const unsigned char *)file, &h->hplan, &h->dchunks, &h->dstream, &h->stream_bytes,
-                            h->stream))
+        if (q8p::build_plan(hd, (const unsigned char *)file, h->d_file, &h->hplan, &h->dchunks, &h->dstream,
+                            &h->stream_bytes, h->stream))
             return 1;
         TRY(cudaMalloc(&h->dplan, sizeof(q8p::Plan)));
         TRY(cudaMemcpy(h->dplan, &h->hplan, sizeof(q8p::Plan), cudaMemcpyHostToDevice));
         TRY(cudaMalloc(&h->dsync, sizeof(q8p::Sync)));
-        TRY(cudaMemset(h->dsync, 0, sizeof(q8p::Sync)));
-        TRY(cudaMalloc(&h->scr.o, sizeof(float) * DIM));
-        TRY(cudaMalloc(&h->scr.partial, sizeof(float) * q8::KV_HEADS * (CONTEXT / q8p::kAttnChunk) * q8::GQA *
-                                            q8::ATTN_PARTIAL));
+        TRY(cudaMalloc(&h->dwords, sizeof(unsigned long long) * q8p::scratch_words()));
+        q8p::carve_scratch(h->dwords, &h->scr);
         TRY(cudaMalloc(&h->scr.cand, sizeof(unsigned long long) * q8p::kCTAs * sampling::kMaxK));
+        if (reset_persistent(h)) return 1;
     }
     TRY(cudaHostAlloc(&h->h_err, sizeof(unsigned), cudaHostAllocMapped));
     TRY(cudaHostGetDevicePointer(&h->d_err, h->h_err, 0));
@@ -302,8 +304,8 @@ void release(mocha_q8 *h)
         if (e) cudaEventDestroy(e);
     void *dev[] = {h->d_file, h->dm, h->b.x, h->b.q, h->b.kc, h->b.vc, h->b.partial, h->b.h, h->b.logits,
                    h->b.hidden, (void *)h->b.rope_cos, h->b.st, h->d_seq, h->d_params, h->d_hist,
-                   h->d_scratch, h->d_keys, h->d_prompt, h->dplan, h->dchunks, h->dstream, h->dsync, h->scr.o,
-                   h->scr.partial, h->scr.cand};
+                   h->d_scratch, h->d_keys, h->d_prompt, h->dplan, h->dchunks, h->dstream, h->dsync, h->dwords,
+                   h->scr.cand};
     for (void *p : dev)
         if (p) cudaFree(p);
     void *host[] = {h->h_state, h->h_params, h->h_hist, h->h_keys, h->h_logits, h->h_pos0, h->h_out,
@@ -328,6 +330,16 @@ int set_params(mocha_q8 *h, float penalty, float temperature, int top_k, float t
     return 0;
 }
 
+// Synchronisation words to their start state: epoch 1 (tag 0 never matches), data
+// words cleared so no stale tag can be mistaken for this step's.
+int reset_persistent(mocha_q8 *h)
+{
+    q8p::Sync s{1u, 0u, 0u};
+    TRY(cudaMemcpy(h->dsync, &s, sizeof s, cudaMemcpyHostToDevice));
+    TRY(cudaMemset(h->dwords, 0, sizeof(unsigned long long) * q8p::scratch_words()));
+    return 0;
+}
+
 // A bounded wait inside the persistent kernel expired: report it, clear the
 // synchronisation words so the next step starts from a clean state, and fail.
 int check_device_error(mocha_q8 *h)
@@ -337,7 +349,7 @@ int check_device_error(mocha_q8 *h)
     if (!code) return 0;
     fprintf(stderr, "MOCHA_B200: persistent decode step aborted (wait expired, code %u)\n", code);
     cudaStreamSynchronize(h->stream);
-    if (h->dsync) cudaMemset(h->dsync, 0, sizeof(q8p::Sync));
+    if (h->dsync) reset_persistent(h);
     __atomic_store_n(h->h_err, 0u, __ATOMIC_RELEASE);
     return 1;
 }
@@ -561,6 +573,28 @@ extern "C" int mocha_q8_forward(mocha_q8 *h, int token, int pos, int project, fl
     if (!h || h->head_only) return 1;
     TRY(cudaSetDevice(h->device));
     return forward_step(h, logits, token, pos, project, 1, false);
+}
+
+extern "C" int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps)
+{
+    if (!h || !h->persistent || !stamps || token < 0 || token >= VOCAB || pos < 0 || pos >= CONTEXT) return 1;
+    TRY(cudaSetDevice(h->device));
+    const size_t n = (size_t)q8p::kCTAs * q8p::kTraceStamps;
+    unsigned long long *d = nullptr;
+    TRY(cudaMalloc(&d, n * sizeof(unsigned long long)));
+    int rc = cudaMemsetAsync(d, 0, n * sizeof(unsigned long long), h->stream) != cudaSuccess;
+    h->h_state->token = token;
+    h->h_state->pos = pos;
+    rc = rc || cudaMemcpyAsync(h->b.st, h->h_state, 2 * sizeof(int), cudaMemcpyHostToDevice, h->stream) != cudaSuccess;
+    rc = rc || q8p::enqueue_step(h->dm, h->dplan, h->b, h->dsync, h->scr, q8p::FORWARD_PROJECT, h->d_params,
+                                 h->d_seq, h->d_out, h->d_out_count, h->d_prompt, h->d_err, h->stream, d);
+    rc = rc || cudaMemcpyAsync(stamps, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, h->stream) !=
+                   cudaSuccess;
+    rc = rc || cudaStreamSynchronize(h->stream) != cudaSuccess;
+    cudaFree(d);
+    if (rc || check_device_error(h)) return 1;
+    h->calls++;
+    return 0;
 }
 
 extern "C" int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches)

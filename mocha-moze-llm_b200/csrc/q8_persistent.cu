@@ -1,18 +1,28 @@
 // Persistent batch-1 decode step for the grouped-Q8 model on B200.
 //
-// One cooperative launch of 148 CTAs (one per SM) runs the whole token:
-//   * warp 0 of every CTA streams that CTA's weights -- laid out at set-up as one
-//     contiguous region per CTA, in the order the CTA consumes them -- through a
-//     5-slot shared-memory ring with cp.async.bulk copies completed on mbarriers.
-//     Weights do not depend on activations, so the stream runs ahead of the
-//     dependency chain by up to the ring depth (~1.7 layers).
-//   * warps 1..8 walk the token's phases: per layer QKV(+bias, RoPE, KV write),
-//     split-K attention (last unit per KV head combines), O + residual,
-//     RMSNorm -> gate/up + SwiGLU, down + residual; then the final norm, the tied
-//     vocabulary head fused with the repetition penalty, control mask and per-CTA
-//     top-k, and -- in the last CTA to finish -- the merge and the token draw.
-//   * phases are separated by epoch-tagged global counters; every wait is bounded
-//     (about two seconds of clock cycles) and sets an error word instead of hanging.
+// One cooperative launch of 148 CTAs (one per SM) runs the whole token.
+//
+// Weights: warp 0 of every CTA streams that CTA's weights -- laid out at set-up as
+// one contiguous region per CTA, in consumption order -- through a 4-slot
+// shared-memory ring with cp.async.bulk copies completed on mbarriers.  Each chunk
+// carries a 16-byte header (kind, layer, row range) and its rows' biases; chunks that
+// start a normalised phase also receive the RMSNorm gain by a second bulk copy (an
+// L2 hit: every CTA reads the same gain).  Weights do not depend on activations, so
+// the stream runs ahead of the dependency chain by up to the ring depth.
+//
+// Activations: the 16 consumer warps exchange every cross-CTA value as a 64-bit data
+// word (float | tag << 32, tag = epoch << 8 | layer << 3 | phase) written with one
+// relaxed store and polled directly by its readers.  There are no counters, fences or
+// second loads between phases; each reader waits exactly for the words it needs.
+// Per layer: QKV (+bias, split-half RoPE, KV write) -> attention split over the
+// positions of each query head (K/V of past positions are prefetched with cp.async
+// before the query exists) -> O + residual -> RMSNorm -> gate/up + SwiGLU ->
+// down + residual.  The vocabulary head is fused with the repetition penalty, the
+// control mask and a per-CTA top-k; the last CTA to finish (one atomic ticket)
+// merges the candidates, draws the token and advances the epoch.
+//
+// Every wait is bounded (~2 s of clock cycles); on expiry the kernel records an
+// error word (device and mapped host memory), drains its own bulk copies and exits.
 // The arithmetic is the reference's (src/minimind.cu:67-123, src/minimind.cpp:51-82):
 // fp32 activations, int8 weights widened exactly, one fp32 scale per 64 weights.
 #include <float.h>
@@ -30,30 +40,37 @@ namespace q8p {
 namespace {
 
 using namespace q8;
-constexpr int kNT = kConsumerWarps * 32;
+constexpr int kNT = kConsumerWarps * 32;  // consumer threads
 constexpr long long kTimeoutCycles = 4000000000LL;
-constexpr int kMaxChunks = CONTEXT / kAttnChunk;
 constexpr int kQkvPairs = (DIM + 2 * KV) / 2;  // 576
-constexpr int kGateupPerChunk = 19;            // pairs (38 rows of 896)
-constexpr int kHeadPerChunk = 38;              // rows
+constexpr int kGateupPerChunk = 17;            // pairs: 34 rows of 896 + header < kGainOff
+constexpr int kHeadPerChunk = 34;              // rows
 constexpr int kHeadSlice = 1040;               // >= ceil(VOCAB / kCTAs)
+constexpr int kPartWords = HEADS * kMaxSplit * ATTN_PARTIAL;
+
+enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_H = 3, PH_X = 4 };
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
-    __align__(16) float xs[DIM];
-    __align__(16) float ns[DIM];
+    __align__(16) float xs[DIM];  // residual (x_in, then x_mid) of the current layer
+    __align__(16) float ns[DIM];  // normalised input / attention output
     union __align__(16) {
-        float hs[HIDDEN];
+        float hs[HIDDEN];          // down-projection input
+        float part[kPartWords];    // gathered attention partials
         struct {
-            float q[GQA][HEAD_DIM];
-            float k[kAttnChunk][HEAD_DIM + 1];
-            float v[kAttnChunk][HEAD_DIM];
+            float k[kAttnLenMax][HEAD_DIM];
+            float v[kAttnLenMax][HEAD_DIM];
+            float q[HEAD_DIM];
+            float e[kAttnLenMax + 1];
         } att;
-        float hl[kHeadSlice];
+        float hl[kHeadSlice];      // this CTA's slice of the logits
     } u;
     float red[kConsumerWarps][8];
+    float rc[HEAD_DIM / 2], rs[HEAD_DIM / 2];  // RoPE cos/sin at pos
+    Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors (producer)
     unsigned long long full[kSlots], empty[kSlots];
     int flag;
+    int iters;  // poll iterations of the last traced gather
     int token, pos;
     volatile int issued;         // chunks the producer has started copying
     volatile int producer_done;  // the producer has left its loop
@@ -64,6 +81,21 @@ struct Smem {
 MB_DEV uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 MB_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kNT) : "memory"); }
+
+// consumer barrier that also ANDs a predicate over the consumer threads
+MB_DEV int cbar_and(int v)
+{
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(v), "n"(kNT)
+        : "memory");
+    return r;
+}
 
 MB_DEV void mbar_init(unsigned long long *bar, uint32_t count)
 {
@@ -94,13 +126,6 @@ MB_DEV bool mbar_test(unsigned long long *bar, uint32_t parity)
     return ok != 0;
 }
 
-MB_DEV unsigned ld_acquire(const unsigned *p)
-{
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 MB_DEV unsigned ld_volatile(const unsigned *p) { return *(const volatile unsigned *)p; }
 
 MB_DEV void fail(Sync *sy, unsigned *host_error, unsigned code)
@@ -110,8 +135,6 @@ MB_DEV void fail(Sync *sy, unsigned *host_error, unsigned code)
     __threadfence_system();
 }
 
-// Bounded wait on an mbarrier phase; false (and the error word set) on timeout or
-// when another CTA already failed.
 MB_DEV bool mbar_wait(unsigned long long *bar, uint32_t parity, Sync *sy, unsigned *host_error)
 {
     if (mbar_test(bar, parity)) return true;
@@ -126,13 +149,43 @@ MB_DEV bool mbar_wait(unsigned long long *bar, uint32_t parity, Sync *sy, unsign
     }
 }
 
-MB_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar)
+MB_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar, uint64_t policy)
 {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-        ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(mb::evict_first_policy())
+        ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
 }
+
+MB_DEV void bulk_load_plain(void *dst, const void *src, uint32_t bytes, unsigned long long *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+MB_DEV void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+MB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// data words
+MB_DEV void dw_store(unsigned long long *p, float v, uint32_t tag)
+{
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+MB_DEV unsigned long long dw_load(const unsigned long long *p)
+{
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+MB_DEV uint32_t make_tag(uint32_t epoch, int layer, int phase) { return (epoch << 8) | (layer << 3) | phase; }
 
 // ---- consumer-side helpers --------------------------------------------------
 
@@ -141,44 +194,83 @@ struct Ctx {
     Sync *sy;
     unsigned *host_error;
     int ct, cw, lane;
-    unsigned target;
 };
 
-// all consumer threads return the same verdict
-MB_DEV bool gwait(Ctx &c, const unsigned *cnt)
+// 32-byte relaxed load of four data words (one L2 request instead of four)
+MB_DEV void dw_load4(const unsigned long long *p, unsigned long long (&v)[4])
 {
-    if (c.ct == 0) {
-        int ok = 1;
-        if (ld_acquire(cnt) < c.target) {
-            const long long t0 = clock64();
-            while (ld_acquire(cnt) < c.target) {
-                if (ld_volatile(&c.sy->error)) { ok = 0; break; }
-                if (clock64() - t0 > kTimeoutCycles) {
-                    fail(c.sy, c.host_error, 1);
-                    ok = 0;
-                    break;
+    asm volatile("ld.relaxed.gpu.global.v4.u64 {%0,%1,%2,%3}, [%4];"
+                 : "=l"(v[0]), "=l"(v[1]), "=l"(v[2]), "=l"(v[3])
+                 : "l"(p)
+                 : "memory");
+}
+
+// Poll the data words src[0..n) (n a multiple of 4, src 32-byte aligned) that `want`
+// selects until each carries `tag`, storing their floats to dst.  Thread ct owns the
+// 4-word groups ct, ct+kNT, ...; each request covers a whole group, only groups with
+// missing words are polled again, and a short sleep between rounds keeps 148 CTAs
+// from saturating the L2 slices that hold the words.  Every consumer thread returns
+// the same verdict.
+template <int E, typename Want>
+MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, Want want,
+                      int *iters = nullptr)
+{
+    const int ng = n >> 2;
+    unsigned need[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        const int g = c.ct + e * kNT;
+        need[e] = 0;
+        if (g < ng)
+#pragma unroll
+            for (int j = 0; j < 4; j++) need[e] |= want(4 * g + j) ? (1u << j) : 0u;
+    }
+    int ok = 1, it = 0;
+    long long t0 = 0;
+    for (;;) {
+        unsigned missing = 0;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            if (!need[e]) continue;
+            const int g = c.ct + e * kNT;
+            unsigned long long v[4];
+            dw_load4(src + 4 * g, v);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if ((need[e] >> j & 1u) && (uint32_t)(v[j] >> 32) == tag) {
+                    dst[4 * g + j] = __uint_as_float((uint32_t)v[j]);
+                    need[e] &= ~(1u << j);
                 }
             }
+            missing |= need[e];
         }
-        c.S.flag = ok;
+        if (!missing) break;
+        it++;
+        if (t0 == 0) {
+            t0 = clock64();
+        } else if (clock64() - t0 > kTimeoutCycles) {
+            fail(c.sy, c.host_error, 1);
+            ok = 0;
+            break;
+        }
+        if (ld_volatile(&c.sy->error)) {
+            ok = 0;
+            break;
+        }
+        __nanosleep(64);
     }
-    cbar();
-    return c.S.flag != 0;
+    if (iters) atomicMax(iters, it);
+    return cbar_and(ok) != 0;
 }
 
-MB_DEV void gsignal(Ctx &c, unsigned *cnt)
-{
-    cbar();
-    if (c.ct == 0) {
-        __threadfence();
-        atomicAdd(cnt, 1u);
-    }
-}
+struct All {
+    MB_DEV bool operator()(int) const { return true; }
+};
 
-MB_DEV void load_vec_cg(float *dst, const float *src, int n, int ct)
+template <int E>
+MB_DEV bool gather(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, int *iters = nullptr)
 {
-    for (int i = ct * 4; i < n; i += kNT * 4)
-        *reinterpret_cast<float4 *>(dst + i) = __ldcg(reinterpret_cast<const float4 *>(src + i));
+    return gather_if<E>(c, src, n, tag, dst, All{}, iters);
 }
 
 // y = (x * s) * g, s = 1/sqrt(sum(x^2)/DIM + eps); identical bits in every CTA
@@ -193,34 +285,47 @@ MB_DEV void rmsnorm(Ctx &c, const float *xs, const float *gain, float *ns)
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; w++) sum += c.S.red[w][0];
     const float s = 1.0f / sqrtf(sum / DIM + RMS_EPS);
-    for (int i = c.ct; i < DIM; i += kNT) ns[i] = xs[i] * s * __ldg(gain + i);
+    for (int i = c.ct; i < DIM; i += kNT) ns[i] = xs[i] * s * gain[i];
     cbar();
 }
 
-// 16 int8 weights (smem) . 16 fp32 inputs held in registers
+// 16 int8 weights . 16 fp32 inputs held in registers (two accumulation chains)
 MB_DEV float dot16r(const int4 w, const float *xr)
 {
     const uint32_t u[4] = {(uint32_t)w.x ^ 0x80808080u, (uint32_t)w.y ^ 0x80808080u, (uint32_t)w.z ^ 0x80808080u,
                            (uint32_t)w.w ^ 0x80808080u};
-    float acc = 0.f;
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        acc = fmaf(mb::s8_lane(u[i], 0x7540), xr[4 * i + 0], acc);
-        acc = fmaf(mb::s8_lane(u[i], 0x7541), xr[4 * i + 1], acc);
-        acc = fmaf(mb::s8_lane(u[i], 0x7542), xr[4 * i + 2], acc);
-        acc = fmaf(mb::s8_lane(u[i], 0x7543), xr[4 * i + 3], acc);
+        a0 = fmaf(mb::s8_lane(u[i], 0x7540), xr[4 * i + 0], a0);
+        a1 = fmaf(mb::s8_lane(u[i], 0x7541), xr[4 * i + 1], a1);
+        a0 = fmaf(mb::s8_lane(u[i], 0x7542), xr[4 * i + 2], a0);
+        a1 = fmaf(mb::s8_lane(u[i], 0x7543), xr[4 * i + 3], a1);
     }
-    return acc;
+    return a0 + a1;
 }
 
 // A 896-wide row: lane owns 16-weight chunks lane and lane+32 (< 56); its 32 inputs
 // live in registers for every row of the phase.
 MB_DEV void load_x896(const float *ns, int lane, float *xr)
 {
+    const float4 *n4 = reinterpret_cast<const float4 *>(ns);
 #pragma unroll
-    for (int i = 0; i < 16; i++) xr[i] = ns[lane * 16 + i];
+    for (int i = 0; i < 4; i++) {
+        const float4 v = n4[lane * 4 + i];
+        xr[4 * i] = v.x;
+        xr[4 * i + 1] = v.y;
+        xr[4 * i + 2] = v.z;
+        xr[4 * i + 3] = v.w;
+    }
 #pragma unroll
-    for (int i = 0; i < 16; i++) xr[16 + i] = lane < 24 ? ns[(lane + 32) * 16 + i] : 0.f;
+    for (int i = 0; i < 4; i++) {
+        const float4 v = lane < 24 ? n4[(lane + 32) * 4 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        xr[16 + 4 * i] = v.x;
+        xr[16 + 4 * i + 1] = v.y;
+        xr[16 + 4 * i + 2] = v.z;
+        xr[16 + 4 * i + 3] = v.w;
+    }
 }
 
 MB_DEV float row896(const uint8_t *w_row, const float *s_row, const float *xr, int lane)
@@ -253,109 +358,75 @@ struct Args {
     int *out_ring, *out_count;
     const int *prompt;
     unsigned *host_error;
+    unsigned long long *trace;  // optional [kCTAs][kTraceStamps] %globaltimer stamps
 };
+
+MB_DEV void stamp(const Args &a, int cta, int ct, int point)
+{
+    if (a.trace && ct == 0 && point < kTraceStamps) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.trace[cta * kTraceStamps + point] = t;
+    }
+}
+
+MB_DEV void stamp_value(const Args &a, int cta, int ct, int point, unsigned long long v)
+{
+    if (a.trace && ct == 0 && point < kTraceStamps) a.trace[cta * kTraceStamps + point] = v;
+}
 
 struct Cursor {
-    uint32_t i, end, k;
+    uint32_t k;  // chunks consumed
 };
 
-// Wait for the next chunk of the stream; returns its slot data or null on failure.
-MB_DEV const uint8_t *take(Ctx &c, const Args &a, Cursor &cur, uint32_t kind, const Chunk *&ch)
+// Wait for the next chunk; returns the slot (header first) or null on failure.
+MB_DEV const uint8_t *take(Ctx &c, Cursor &cur, uint32_t kind)
 {
-    if (cur.i >= cur.end) {
-        if (c.ct == 0) fail(c.sy, c.host_error, 3);
-        return nullptr;
-    }
-    ch = &a.P->chunks[cur.i];
-    if (ch->kind != kind) {
+    const uint32_t slot = cur.k % kSlots, use = cur.k / kSlots;
+    if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return nullptr;
+    const uint8_t *w = c.S.ring[slot];
+    if (reinterpret_cast<const ChunkHdr *>(w)->kind != kind) {
         if (c.ct == 0) fail(c.sy, c.host_error, 4);
         return nullptr;
     }
-    const uint32_t slot = cur.k % kSlots, use = cur.k / kSlots;
-    if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return nullptr;
-    return c.S.ring[slot];
+    return w;
 }
 
 MB_DEV void give_back(Ctx &c, Cursor &cur)
 {
     cbar();
     if (c.ct == 0) mbar_arrive(&c.S.empty[cur.k % kSlots]);
-    cur.i++;
     cur.k++;
 }
 
-MB_DEV bool next_is(const Args &a, const Cursor &cur, uint32_t kind, uint32_t layer)
+// Is the next chunk of `kind` in `layer`?  (waits for it to land, then reads its
+// header; -1 on failure)
+MB_DEV int next_is(Ctx &c, const Cursor &cur, int remaining, uint32_t kind, uint32_t layer)
 {
-    if (cur.i >= cur.end) return false;
-    const Chunk &ch = a.P->chunks[cur.i];
-    return ch.kind == kind && ch.layer == layer;
+    if (remaining <= 0) return 0;
+    const uint32_t slot = cur.k % kSlots, use = cur.k / kSlots;
+    if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return -1;
+    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(c.S.ring[slot]);
+    return h->kind == kind && h->layer == layer ? 1 : 0;
 }
 
-MB_DEV void attention_unit(Ctx &c, const Args &a, int layer, int pos, int nch, int unit)
+// Error exit of the consumers: wait (bounded) until the producer has stopped and
+// every bulk copy it started into this CTA's ring has landed, so no copy is still
+// writing shared memory when the CTA exits.
+MB_DEV void drain(Ctx &c, const Cursor &cur)
 {
-    Smem &S = c.S;
-    const int kvh = unit / nch, ch = unit % nch;
-    const int p0 = ch * kAttnChunk, np = min(kAttnChunk, pos + 1 - p0);
-    const float *kb = a.b.kc + kv_index(layer, kvh, p0);
-    const float *vb = a.b.vc + kv_index(layer, kvh, p0);
-    for (int i = c.ct; i < GQA * HEAD_DIM; i += kNT)
-        S.u.att.q[i / HEAD_DIM][i % HEAD_DIM] = __ldcg(a.b.q + kvh * GQA * HEAD_DIM + i);
-    for (int i = c.ct; i < np * HEAD_DIM; i += kNT) {
-        S.u.att.k[i / HEAD_DIM][i % HEAD_DIM] = __ldcg(kb + i);
-        S.u.att.v[i / HEAD_DIM][i % HEAD_DIM] = __ldcg(vb + i);
-    }
-    cbar();
-    if (c.cw < GQA) {
-        const int j = c.cw, lane = c.lane;
-        float s = -INFINITY;
-        if (lane < np) {
-            float z = 0.f;
-#pragma unroll 16
-            for (int i = 0; i < HEAD_DIM; i++) z = fmaf(S.u.att.q[j][i], S.u.att.k[lane][i], z);
-            s = z * 0.125f;
-        }
-        const float m = mb::warp_max(s);
-        const float e = lane < np ? expf(s - m) : 0.f;
-        const float l = mb::warp_sum(e);
-        float a0 = 0.f, a1 = 0.f;
-        for (int p = 0; p < np; p++) {
-            const float w = __shfl_sync(0xffffffffu, e, p);
-            a0 = fmaf(w, S.u.att.v[p][lane], a0);
-            a1 = fmaf(w, S.u.att.v[p][lane + 32], a1);
-        }
-        float *out = a.scr.partial + ((size_t)(kvh * kMaxChunks + ch) * GQA + j) * ATTN_PARTIAL;
-        if (lane == 0) {
-            out[0] = m;
-            out[1] = l;
-        }
-        out[2 + lane] = a0;
-        out[2 + lane + 32] = a1;
-    }
-    cbar();
     if (c.ct == 0) {
-        __threadfence();
-        const unsigned t = atomicAdd(&c.sy->tickets[layer][kvh], 1u);
-        S.flag = t == (unsigned)(nch - 1);
-        if (S.flag) atomicExch(&c.sy->tickets[layer][kvh], 0u);
-    }
-    cbar();
-    if (S.flag) {
-        __threadfence();
-        constexpr int cstride = GQA * ATTN_PARTIAL;
-        for (int idx = c.ct; idx < GQA * HEAD_DIM; idx += kNT) {
-            const int j = idx / HEAD_DIM, d = idx % HEAD_DIM;
-            const float *p = a.scr.partial + ((size_t)kvh * kMaxChunks * GQA + j) * ATTN_PARTIAL;
-            float mx = -INFINITY;
-            for (int q = 0; q < nch; q++) mx = fmaxf(mx, __ldcg(p + q * cstride));
-            float lsum = 0.f, acc = 0.f;
-            for (int q = 0; q < nch; q++) {
-                const float w = expf(__ldcg(p + q * cstride) - mx);
-                lsum = fmaf(w, __ldcg(p + q * cstride + 1), lsum);
-                acc = fmaf(w, __ldcg(p + q * cstride + 2 + d), acc);
+        const long long t0 = clock64();
+        while (!c.S.producer_done && clock64() - t0 < kTimeoutCycles) {
+        }
+        const int issued = c.S.issued;
+        for (int k = (int)cur.k; k < issued; k++) {
+            const long long t1 = clock64();
+            while (!mbar_test(&c.S.full[k % kSlots], (k / kSlots) & 1) && clock64() - t1 < kTimeoutCycles) {
             }
-            a.scr.o[kvh * GQA * HEAD_DIM + idx] = acc / lsum;
         }
     }
+    cp_async_wait_all();
     cbar();
 }
 
@@ -394,24 +465,15 @@ MB_DEV unsigned long long block_max(Ctx &c, unsigned long long v)
     return best;
 }
 
-// Error exit of the consumers: wait (bounded) until the producer has stopped and
-// every bulk copy it started into this CTA's ring has landed, so no copy is still
-// writing shared memory when the CTA exits.
-MB_DEV void drain(Ctx &c, const Cursor &cur)
-{
-    if (c.ct == 0) {
-        const long long t0 = clock64();
-        while (!c.S.producer_done && clock64() - t0 < kTimeoutCycles) {
-        }
-        const int issued = c.S.issued;
-        for (int k = (int)cur.k; k < issued; k++) {
-            const long long t1 = clock64();
-            while (!mbar_test(&c.S.full[k % kSlots], (k / kSlots) & 1) && clock64() - t1 < kTimeoutCycles) {
-            }
-        }
-    }
-    cbar();
-}
+// attention split of one query head: positions [p0, p0+np)
+struct AttnUnit {
+    int head, split, p0, np;
+};
+
+struct UsedSplit {
+    int splits;
+    MB_DEV bool operator()(int i) const { return (i / ATTN_PARTIAL) % kMaxSplit < splits; }
+};
 
 __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 {
@@ -432,8 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         S.issued = 0;
         S.producer_done = 0;
         S.flag = 0;
-        const bool bad = S.token < 0 || S.token >= VOCAB || S.pos < 0 || S.pos >= CONTEXT ||
-                         (a.mode == PREFILL && S.pos + 1 >= CONTEXT);
+        const bool bad = S.token < 0 || S.token >= VOCAB || S.pos < 0 || S.pos >= CONTEXT || epoch == 0 ||
+                         epoch >= (1u << 24) || (a.mode == PREFILL && S.pos + 1 >= CONTEXT) ||
+                         a.P->chunk_begin[cta + 1] - a.P->chunk_begin[cta] > (uint32_t)kMaxChunksPerCta;
         if (bad) {
             fail(a.sy, a.host_error, 5);
             S.flag = -1;
@@ -443,17 +506,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     if (S.flag < 0) return;  // invalid token / position: nothing was issued
     const uint32_t c0 = a.P->chunk_begin[cta], c1 = a.P->chunk_begin[cta + 1];
 
+    const uint32_t c_end = project ? c1 : a.P->head_begin[cta];  // head chunks only when projecting
     if (threadIdx.x < 32) {  // ---- producer warp: stream this CTA's weights
+        for (uint32_t j = threadIdx.x; j < c_end - c0 && j < (uint32_t)kMaxChunksPerCta; j += 32)
+            S.desc[j] = a.P->chunks[c0 + j];
+        __syncwarp();
         if (threadIdx.x == 0) {
+            const uint64_t policy = mb::evict_first_policy();
             uint32_t k = 0;
-            for (uint32_t i = c0; i < c1 && S.flag >= 0; i++) {
-                const Chunk ch = a.P->chunks[i];
-                if (ch.kind == HEAD && !project) continue;
+            for (uint32_t i = 0; i < c_end - c0; i++) {
+                const Chunk ch = S.desc[i];
                 const uint32_t slot = k % kSlots, use = k / kSlots;
                 if (use > 0 && !mbar_wait(&S.empty[slot], (use - 1) & 1, a.sy, a.host_error)) break;
                 if (ld_volatile(&a.sy->error)) break;
-                mbar_expect_tx(&S.full[slot], ch.bytes);
-                bulk_load(S.ring[slot], a.P->stream + ch.off, ch.bytes, &S.full[slot]);
+                mbar_expect_tx(&S.full[slot], ch.bytes + (ch.gain_off ? kGainBytes : 0));
+                bulk_load(S.ring[slot], a.P->stream + ch.off, ch.bytes, &S.full[slot], policy);
+                if (ch.gain_off)
+                    bulk_load_plain(S.ring[slot] + kGainOff, a.P->blob + ch.gain_off, kGainBytes, &S.full[slot]);
                 k++;
                 S.issued = (int)k;
             }
@@ -463,143 +532,287 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         return;
     }
 
-    Ctx c{S, a.sy, a.host_error, (int)threadIdx.x - 32, ((int)threadIdx.x - 32) >> 5, (int)threadIdx.x & 31,
-          (epoch + 1) * kCTAs};
+    Ctx c{S, a.sy, a.host_error, (int)threadIdx.x - 32, ((int)threadIdx.x - 32) >> 5, (int)threadIdx.x & 31};
     const int pos = S.pos;
-    Cursor cur{c0, c1, 0};
+    Cursor cur{0};
+    int remaining = (int)(c_end - c0);  // chunks this CTA still has to take
     const Model *M = a.M;
+    const Scratch &scr = a.scr;
     float xr[32];
+    stamp(a, cta, c.ct, 0);
+
+    // per-step constants: RoPE at pos, the attention split owned by this CTA
+    if (c.ct < HEAD_DIM / 2) {
+        S.rc[c.ct] = __ldg(a.b.rope_cos + pos * 32 + c.ct);
+        S.rs[c.ct] = __ldg(a.b.rope_sin + pos * 32 + c.ct);
+    }
+    const int splits = min(kMaxSplit, (pos + kAttnTarget) / kAttnTarget);
+    const int span = (pos + splits) / splits;  // ceil((pos+1)/splits) <= kAttnLenMax
+    AttnUnit unit{-1, 0, 0, 0};
+    if (cta < HEADS * splits) {
+        unit.head = cta / splits;
+        unit.split = cta % splits;
+        unit.p0 = unit.split * span;
+        unit.np = min(span, pos + 1 - unit.p0);
+    }
+    // layer-0 input: the token's embedding row (src/minimind.cu:70)
+    {
+        const int8_t *e = M->embed.w + (size_t)S.token * DIM;
+        const float *es = M->embed.s + (size_t)S.token * (DIM / GROUP);
+        for (int i = c.ct; i < DIM; i += kNT) S.xs[i] = (float)e[i] * __ldg(es + i / GROUP);
+    }
+    cbar();
 
     for (int l = 0; l < LAYERS; l++) {
-        const Layer &L = M->layer[l];
-        // ---- QKV + bias + RoPE + KV write
-        if (l == 0) {
-            const int token = S.token;
-            const int8_t *e = M->embed.w + (size_t)token * DIM;
-            const float *es = M->embed.s + (size_t)token * (DIM / GROUP);
-            for (int i = c.ct; i < DIM; i += kNT) {
-                const float v = (float)e[i] * __ldg(es + i / GROUP);
-                S.xs[i] = v;
-                if (cta == 0) a.b.x[i] = v;
+        // K/V of past positions for this CTA's attention split: no dependency on this
+        // step, copied asynchronously while the QKV phase runs
+        if (unit.head >= 0) {
+            const int kvh = unit.head / GQA;
+            const int past = min(unit.np, pos - unit.p0);  // rows < pos
+            const float *kb = a.b.kc + kv_index(l, kvh, unit.p0);
+            const float *vb = a.b.vc + kv_index(l, kvh, unit.p0);
+            for (int i = c.ct; i < past * (HEAD_DIM / 4); i += kNT) {
+                const int p = i / (HEAD_DIM / 4), q4 = i % (HEAD_DIM / 4);
+                cp_async16(&S.u.att.k[p][q4 * 4], kb + p * HEAD_DIM + q4 * 4);
+                cp_async16(&S.u.att.v[p][q4 * 4], vb + p * HEAD_DIM + q4 * 4);
             }
-        } else {
-            if (!gwait(c, &a.sy->counters[l - 1][PH_DOWN])) return drain(c, cur);
-            load_vec_cg(S.xs, a.b.x, DIM, c.ct);
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
-        cbar();
-        rmsnorm(c, S.xs, L.attn_norm, S.ns);
+        // ---- QKV + bias + RoPE + KV write
+        if (l > 0 && !gather<1>(c, scr.xin, DIM, make_tag(epoch, l - 1, PH_X), S.xs)) return drain(c, cur);
+        stamp(a, cta, c.ct, 2 + l * 12 + 0);
         {
-            const Chunk *ch;
-            const uint8_t *w = take(c, a, cur, QKV, ch);
+            const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
-            const int npair = ch->count;
-            const float *sc = reinterpret_cast<const float *>(w + (size_t)2 * npair * DIM);
+            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
+            rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
+            const int npair = hd.count;
+            const uint8_t *rows = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(rows + (size_t)2 * npair * DIM);
+            const float *bias = sc + 2 * npair * (DIM / GROUP);
             if (c.cw < npair) {
                 load_x896(S.ns, c.lane, xr);
-                const int pair = ch->first + c.cw;
-                const float d0 = row896(w + (size_t)(2 * c.cw) * DIM, sc + (2 * c.cw) * 14, xr, c.lane);
-                const float d1 = row896(w + (size_t)(2 * c.cw + 1) * DIM, sc + (2 * c.cw + 1) * 14, xr, c.lane);
+                const int pair = hd.first + c.cw;
+                const float d0 = row896(rows + (size_t)(2 * c.cw) * DIM, sc + (2 * c.cw) * 14, xr, c.lane);
+                const float d1 = row896(rows + (size_t)(2 * c.cw + 1) * DIM, sc + (2 * c.cw + 1) * 14, xr, c.lane);
                 if (c.lane == 0) {
+                    const uint32_t tag = make_tag(epoch, l, PH_QKV);
                     int kind, t;
-                    const float *bias;
-                    if (pair < DIM / 2) { kind = 0; t = pair; bias = L.bq; }
-                    else if (pair < DIM / 2 + KV / 2) { kind = 1; t = pair - DIM / 2; bias = L.bk; }
-                    else { kind = 2; t = pair - DIM / 2 - KV / 2; bias = L.bv; }
+                    if (pair < DIM / 2) { kind = 0; t = pair; }
+                    else if (pair < DIM / 2 + KV / 2) { kind = 1; t = pair - DIM / 2; }
+                    else { kind = 2; t = pair - DIM / 2 - KV / 2; }
                     const int head = t / 32, i = t % 32, r0 = head * HEAD_DIM + i;
-                    const float v0 = d0 + __ldg(bias + r0), v1 = d1 + __ldg(bias + r0 + 32);
+                    const float v0 = d0 + bias[2 * c.cw], v1 = d1 + bias[2 * c.cw + 1];
                     if (kind == 2) {
                         float *v = a.b.vc + kv_index(l, head, pos);
                         v[i] = v0;
                         v[i + 32] = v1;
+                        dw_store(scr.kv + (head * 2 + 1) * HEAD_DIM + i, v0, tag);
+                        dw_store(scr.kv + (head * 2 + 1) * HEAD_DIM + i + 32, v1, tag);
                     } else {
-                        const float cs = __ldg(a.b.rope_cos + pos * 32 + i), sn = __ldg(a.b.rope_sin + pos * 32 + i);
+                        const float cs = S.rc[i], sn = S.rs[i];
+                        // unfused products, as the reference CPU evaluates them (src/minimind.cpp:64-66)
                         const float lo = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
                         const float hi = __fadd_rn(__fmul_rn(v1, cs), __fmul_rn(v0, sn));
                         if (kind == 0) {
-                            a.b.q[r0] = lo;
-                            a.b.q[r0 + 32] = hi;
+                            dw_store(scr.q + r0, lo, tag);
+                            dw_store(scr.q + r0 + 32, hi, tag);
                         } else {
                             float *k = a.b.kc + kv_index(l, head, pos);
                             k[i] = lo;
                             k[i + 32] = hi;
+                            dw_store(scr.kv + (head * 2) * HEAD_DIM + i, lo, tag);
+                            dw_store(scr.kv + (head * 2) * HEAD_DIM + i + 32, hi, tag);
                         }
                     }
                 }
             }
             give_back(c, cur);
+            remaining--;
         }
-        gsignal(c, &a.sy->counters[l][PH_QKV]);
+        stamp(a, cta, c.ct, 2 + l * 12 + 1);
 
-        // ---- split-K attention; the last unit of each KV head combines
-        if (!gwait(c, &a.sy->counters[l][PH_QKV])) return drain(c, cur);
-        {
-            const int nch = pos / kAttnChunk + 1;
-            if (cta < KV_HEADS * nch) attention_unit(c, a, l, pos, nch, cta);
+        // ---- attention: one split of one query head per CTA
+        if (unit.head >= 0) {
+            const uint32_t tag = make_tag(epoch, l, PH_QKV);
+            const int h = unit.head, kvh = h / GQA, np = unit.np;
+            const bool has_cur = unit.p0 + np == pos + 1;
+            const unsigned long long ready = (unsigned long long)tag << 32;
+            // the query of this head, and this position's K/V when the split holds it
+            int ok = 1;
+            if (c.ct < HEAD_DIM) {
+                const unsigned long long *qa = scr.q + h * HEAD_DIM + c.ct;
+                const unsigned long long *ka = scr.kv + (kvh * 2) * HEAD_DIM + c.ct;
+                const unsigned long long *va = scr.kv + (kvh * 2 + 1) * HEAD_DIM + c.ct;
+                unsigned long long w = dw_load(qa);
+                unsigned long long wk = has_cur ? dw_load(ka) : ready;
+                unsigned long long wv = has_cur ? dw_load(va) : ready;
+                const long long t0 = clock64();
+                while ((uint32_t)(w >> 32) != tag || (uint32_t)(wk >> 32) != tag || (uint32_t)(wv >> 32) != tag) {
+                    if ((uint32_t)(w >> 32) != tag) w = dw_load(qa);
+                    if ((uint32_t)(wk >> 32) != tag) wk = dw_load(ka);
+                    if ((uint32_t)(wv >> 32) != tag) wv = dw_load(va);
+                    if (ld_volatile(&c.sy->error)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (clock64() - t0 > kTimeoutCycles) {
+                        fail(c.sy, c.host_error, 1);
+                        ok = 0;
+                        break;
+                    }
+                }
+                S.u.att.q[c.ct] = __uint_as_float((uint32_t)w);
+                if (has_cur) {
+                    S.u.att.k[np - 1][c.ct] = __uint_as_float((uint32_t)wk);
+                    S.u.att.v[np - 1][c.ct] = __uint_as_float((uint32_t)wv);
+                }
+            }
+            cp_async_wait_all();
+            if (!cbar_and(ok)) return drain(c, cur);
+            // scores: warp per position, lanes over the 64 dims
+            for (int p = c.cw; p < np; p += kConsumerWarps) {
+                float z = S.u.att.q[c.lane] * S.u.att.k[p][c.lane];
+                z = fmaf(S.u.att.q[c.lane + 32], S.u.att.k[p][c.lane + 32], z);
+                z = mb::warp_sum(z);
+                if (c.lane == 0) S.u.att.e[p] = z * 0.125f;
+            }
+            cbar();
+            if (c.cw == 0) {
+                float m = -INFINITY;
+                for (int p = c.lane; p < np; p += 32) m = fmaxf(m, S.u.att.e[p]);
+                m = mb::warp_max(m);
+                float lsum = 0.f;
+                for (int p = c.lane; p < np; p += 32) {
+                    const float e = expf(S.u.att.e[p] - m);
+                    S.u.att.e[p] = e;
+                    lsum += e;
+                }
+                lsum = mb::warp_sum(lsum);
+                if (c.lane == 0) {
+                    S.red[0][0] = m;
+                    S.red[0][1] = lsum;
+                }
+            }
+            cbar();
+            if (c.ct < HEAD_DIM) {
+                float acc = 0.f;
+                for (int p = 0; p < np; p++) acc = fmaf(S.u.att.e[p], S.u.att.v[p][c.ct], acc);
+                const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
+                unsigned long long *out = scr.part + ((size_t)h * kMaxSplit + unit.split) * ATTN_PARTIAL;
+                dw_store(out + 2 + c.ct, acc, ptag);
+                if (c.ct == 0) {
+                    dw_store(out, S.red[0][0], ptag);
+                    dw_store(out + 1, S.red[0][1], ptag);
+                }
+            }
+            cbar();
         }
-        gsignal(c, &a.sy->counters[l][PH_ATTN]);
+        stamp(a, cta, c.ct, 2 + l * 12 + 2);
 
-        // ---- O projection + residual
-        if (!gwait(c, &a.sy->counters[l][PH_ATTN])) return drain(c, cur);
-        load_vec_cg(S.ns, a.scr.o, DIM, c.ct);
+        // ---- O projection + residual: combine every head's splits, then the rows
+        if (!gather_if<(kPartWords / 4 + kNT - 1) / kNT>(c, scr.part, kPartWords, make_tag(epoch, l, PH_ATTN), S.u.part,
+                                                       UsedSplit{splits}))
+            return drain(c, cur);
+        for (int idx = c.ct; idx < DIM; idx += kNT) {
+            const int h = idx / HEAD_DIM, d = idx % HEAD_DIM;
+            const float *p = S.u.part + (size_t)h * kMaxSplit * ATTN_PARTIAL;
+            float mx = -INFINITY;
+            for (int s = 0; s < splits; s++) mx = fmaxf(mx, p[s * ATTN_PARTIAL]);
+            float lsum = 0.f, acc = 0.f;
+            for (int s = 0; s < splits; s++) {
+                const float wgt = expf(p[s * ATTN_PARTIAL] - mx);
+                lsum = fmaf(wgt, p[s * ATTN_PARTIAL + 1], lsum);
+                acc = fmaf(wgt, p[s * ATTN_PARTIAL + 2 + d], acc);
+            }
+            S.ns[idx] = acc / lsum;
+        }
         cbar();
+        stamp(a, cta, c.ct, 2 + l * 12 + 3);
         {
-            const Chunk *ch;
-            const uint8_t *w = take(c, a, cur, OPROJ, ch);
+            const uint8_t *w = take(c, cur, OPROJ);
             if (!w) return drain(c, cur);
-            const int nrow = ch->count;
-            const float *sc = reinterpret_cast<const float *>(w + (size_t)nrow * DIM);
+            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
+            const int nrow = hd.count;
+            const uint8_t *rows = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * DIM);
             if (c.cw < nrow) {
                 load_x896(S.ns, c.lane, xr);
-                const int row = ch->first + c.cw;
-                const float d = row896(w + (size_t)c.cw * DIM, sc + c.cw * 14, xr, c.lane);
-                if (c.lane == 0) a.b.x[row] = __ldcg(a.b.x + row) + d;
+                const int row = hd.first + c.cw;
+                const float d = row896(rows + (size_t)c.cw * DIM, sc + c.cw * 14, xr, c.lane);
+                if (c.lane == 0) dw_store(scr.xmid + row, S.xs[row] + d, make_tag(epoch, l, PH_O));
             }
             give_back(c, cur);
+            remaining--;
         }
-        gsignal(c, &a.sy->counters[l][PH_O]);
+        stamp(a, cta, c.ct, 2 + l * 12 + 4);
 
         // ---- RMSNorm -> gate/up -> SwiGLU
-        if (!gwait(c, &a.sy->counters[l][PH_O])) return drain(c, cur);
-        load_vec_cg(S.xs, a.b.x, DIM, c.ct);
+        if (c.ct == 0) S.iters = 0;
         cbar();
-        rmsnorm(c, S.xs, L.ffn_norm, S.ns);
-        load_x896(S.ns, c.lane, xr);
-        while (next_is(a, cur, GATEUP, l)) {
-            const Chunk *ch;
-            const uint8_t *w = take(c, a, cur, GATEUP, ch);
-            if (!w) return drain(c, cur);
-            const int npair = ch->count;
-            const float *sc = reinterpret_cast<const float *>(w + (size_t)2 * npair * DIM);
-            for (int p = c.cw; p < npair; p += kConsumerWarps) {
-                const float g = row896(w + (size_t)(2 * p) * DIM, sc + (2 * p) * 14, xr, c.lane);
-                const float u = row896(w + (size_t)(2 * p + 1) * DIM, sc + (2 * p + 1) * 14, xr, c.lane);
-                if (c.lane == 0) a.b.h[ch->first + p] = (g / (1.0f + expf(-g))) * u;
+        if (!gather<1>(c, scr.xmid, DIM, make_tag(epoch, l, PH_O), S.xs, &S.iters)) return drain(c, cur);
+        stamp(a, cta, c.ct, 2 + l * 12 + 5);
+        stamp_value(a, cta, c.ct, 2 + l * 12 + 11, (unsigned long long)S.iters);
+        {
+            bool first = true;
+            for (;;) {
+                const int more = next_is(c, cur, remaining, GATEUP, l);
+                if (more < 0) return drain(c, cur);
+                if (!more) break;
+                const uint8_t *w = take(c, cur, GATEUP);
+                if (!w) return drain(c, cur);
+                if (first) {
+                    stamp(a, cta, c.ct, 2 + l * 12 + 9);
+                    rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
+                    load_x896(S.ns, c.lane, xr);
+                    first = false;
+                    stamp(a, cta, c.ct, 2 + l * 12 + 10);
+                }
+                const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
+                const int npair = hd.count;
+                const uint8_t *rows = w + sizeof(ChunkHdr);
+                const float *sc = reinterpret_cast<const float *>(rows + (size_t)2 * npair * DIM);
+                const uint32_t tag = make_tag(epoch, l, PH_H);
+                for (int p = c.cw; p < npair; p += kConsumerWarps) {
+                    const float g = row896(rows + (size_t)(2 * p) * DIM, sc + (2 * p) * 14, xr, c.lane);
+                    const float u = row896(rows + (size_t)(2 * p + 1) * DIM, sc + (2 * p + 1) * 14, xr, c.lane);
+                    if (c.lane == 0) dw_store(scr.h + hd.first + p, (g / (1.0f + expf(-g))) * u, tag);
+                }
+                give_back(c, cur);
+                remaining--;
             }
-            give_back(c, cur);
         }
-        gsignal(c, &a.sy->counters[l][PH_GATEUP]);
+        stamp(a, cta, c.ct, 2 + l * 12 + 6);
 
         // ---- down + residual: the CTA's threads own column chunks, rows reduced
-        if (!gwait(c, &a.sy->counters[l][PH_GATEUP])) return drain(c, cur);
-        load_vec_cg(S.u.hs, a.b.h, HIDDEN, c.ct);
-        cbar();
+        if (!gather<(HIDDEN / 4 + kNT - 1) / kNT>(c, scr.h, HIDDEN, make_tag(epoch, l, PH_H), S.u.hs))
+            return drain(c, cur);
+        stamp(a, cta, c.ct, 2 + l * 12 + 7);
         {
-            const Chunk *ch;
-            const uint8_t *w = take(c, a, cur, DOWN, ch);
+            const uint8_t *w = take(c, cur, DOWN);
             if (!w) return drain(c, cur);
-            const int nrow = ch->count;
+            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
+            const int nrow = hd.count;
             constexpr int CH = HIDDEN / 16;  // 304 chunks of 16
-            const float *sc = reinterpret_cast<const float *>(w + (size_t)nrow * HIDDEN);
-            const int c1i = c.ct, c2i = c.ct + kNT;
+            const uint8_t *rows = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * HIDDEN);
+            const int ci = c.ct;
+            if (ci < CH) {
+                const float4 *h4 = reinterpret_cast<const float4 *>(S.u.hs + ci * 16);
 #pragma unroll
-            for (int i = 0; i < 16; i++) xr[i] = S.u.hs[c1i * 16 + i];
-#pragma unroll
-            for (int i = 0; i < 16; i++) xr[16 + i] = c2i < CH ? S.u.hs[c2i * 16 + i] : 0.f;
+                for (int i = 0; i < 4; i++) {
+                    const float4 v = h4[i];
+                    xr[4 * i] = v.x;
+                    xr[4 * i + 1] = v.y;
+                    xr[4 * i + 2] = v.z;
+                    xr[4 * i + 3] = v.w;
+                }
+            }
             for (int r = 0; r < nrow; r++) {
-                const uint8_t *wr = w + (size_t)r * HIDDEN;
-                const float *sr = sc + r * (HIDDEN / GROUP);
-                float p = dot16r(*reinterpret_cast<const int4 *>(wr + c1i * 16), xr) * sr[c1i >> 2];
-                if (c2i < CH) p = fmaf(dot16r(*reinterpret_cast<const int4 *>(wr + c2i * 16), xr + 16), sr[c2i >> 2], p);
+                float p = 0.f;
+                if (ci < CH)
+                    p = dot16r(*reinterpret_cast<const int4 *>(rows + (size_t)r * HIDDEN + ci * 16), xr) *
+                        sc[r * (HIDDEN / GROUP) + (ci >> 2)];
                 p = mb::warp_sum(p);
                 if (c.lane == 0) S.red[c.cw][r] = p;
             }
@@ -607,40 +820,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             if (c.ct < nrow) {
                 float sum = 0.f;
 #pragma unroll
-                for (int w8 = 0; w8 < kConsumerWarps; w8++) sum += S.red[w8][c.ct];
-                const int row = ch->first + c.ct;
-                a.b.x[row] = __ldcg(a.b.x + row) + sum;
+                for (int w16 = 0; w16 < kConsumerWarps; w16++) sum += S.red[w16][c.ct];
+                const int row = hd.first + c.ct;
+                dw_store(scr.xin + row, S.xs[row] + sum, make_tag(epoch, l, PH_X));
             }
             give_back(c, cur);
+            remaining--;
         }
-        gsignal(c, &a.sy->counters[l][PH_DOWN]);
+        stamp(a, cta, c.ct, 2 + l * 12 + 8);
     }
 
     if (project) {
         // ---- final norm + tied head, logits kept in shared memory for selection
-        if (!gwait(c, &a.sy->counters[LAYERS - 1][PH_DOWN])) return drain(c, cur);
-        load_vec_cg(S.xs, a.b.x, DIM, c.ct);
-        cbar();
-        rmsnorm(c, S.xs, M->final_norm, S.ns);
-        if (cta == 0)
-            for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
-        load_x896(S.ns, c.lane, xr);
+        if (!gather<1>(c, scr.xin, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
+        stamp(a, cta, c.ct, 300);
         const int lo = a.P->head_lo[cta], n = a.P->head_lo[cta + 1] - lo;
-        while (next_is(a, cur, HEAD, LAYERS)) {
-            const Chunk *ch;
-            const uint8_t *w = take(c, a, cur, HEAD, ch);
+        bool first = true;
+        for (;;) {
+            const int more = next_is(c, cur, remaining, HEAD, LAYERS);
+            if (more < 0) return drain(c, cur);
+            if (!more) break;
+            const uint8_t *w = take(c, cur, HEAD);
             if (!w) return drain(c, cur);
-            const int nrow = ch->count;
-            const float *sc = reinterpret_cast<const float *>(w + (size_t)nrow * DIM);
+            if (first) {
+                rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
+                if (cta == 0)
+                    for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
+                load_x896(S.ns, c.lane, xr);
+                first = false;
+            }
+            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
+            const int nrow = hd.count;
+            const uint8_t *rows = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * DIM);
             for (int r = c.cw; r < nrow; r += kConsumerWarps) {
-                const float d = row896(w + (size_t)r * DIM, sc + r * 14, xr, c.lane);
+                const float d = row896(rows + (size_t)r * DIM, sc + r * 14, xr, c.lane);
                 if (c.lane == 0) {
-                    a.b.logits[ch->first + r] = d;
-                    S.u.hl[ch->first + r - lo] = d;
+                    a.b.logits[hd.first + r] = d;
+                    S.u.hl[hd.first + r - lo] = d;
                 }
             }
             give_back(c, cur);
+            remaining--;
         }
+        cbar();
         if (decode) {
             // penalty (distinct ids of the history window) and control mask on this
             // CTA's vocabulary slice, then the slice's top k as ordered keys
@@ -684,11 +907,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     }
 
     // ---- end of step: the last CTA finishes the token
+    stamp(a, cta, c.ct, 301);
     cbar();
     if (c.ct == 0) {
         __threadfence();
         const unsigned t = atomicAdd(&a.sy->done, 1u);
-        S.flag = t == c.target - 1;
+        S.flag = t == (unsigned)kCTAs - 1;
     }
     cbar();
     if (!S.flag) return;
@@ -730,10 +954,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             a.b.st->token = a.prompt[pos + 1];
         }
     }
+    stamp(a, cta, c.ct, 302);
     if (c.ct == 0) {
         a.b.st->steps++;
+        a.sy->done = 0;
+        const unsigned next = epoch + 1 >= (1u << 24) ? 1u : epoch + 1;
         __threadfence();
-        atomicExch(&a.sy->epoch, epoch + 1);
+        atomicExch(&a.sy->epoch, next);
     }
 }
 
@@ -747,6 +974,18 @@ inline void split(int n, int parts, int i, int &lo, int &hi)
 }  // namespace
 
 size_t smem_bytes() { return sizeof(Smem); }
+
+size_t scratch_words() { return (size_t)DIM + 2 * KV + kPartWords + DIM + DIM + HIDDEN; }
+
+void carve_scratch(unsigned long long *base, Scratch *scr)
+{
+    scr->q = base;
+    scr->kv = scr->q + DIM;
+    scr->part = scr->kv + 2 * KV;
+    scr->xmid = scr->part + kPartWords;
+    scr->xin = scr->xmid + DIM;
+    scr->h = scr->xin + DIM;
+}
 
 int init_device()
 {
@@ -764,23 +1003,24 @@ int init_device()
     return 0;
 }
 
-int build_plan(const FileHeader *hdr, const unsigned char *hfile, Plan *hplan, Chunk **dchunks, uint8_t **dstream,
-               size_t *stream_bytes, cudaStream_t s)
+int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned char *dfile, Plan *hplan,
+               Chunk **dchunks, uint8_t **dstream, size_t *stream_bytes, cudaStream_t s)
 {
     std::vector<Chunk> chunks;
     std::vector<uint8_t> stream;
-    stream.reserve((size_t)540 << 20);
+    stream.reserve((size_t)560 << 20);
     const FileTensor *t = hdr->t;
     auto align16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
-    // append rows (as (tensor, row) pairs) as one chunk: int8 rows, then fp32 scales
+    // one chunk: header, int8 rows, fp32 scales, optional fp32 extras (biases)
     auto emit = [&](uint32_t kind, uint32_t layer, uint32_t first, uint32_t count,
-                    const std::vector<std::pair<const FileTensor *, int>> &rows) {
+                    const std::vector<std::pair<const FileTensor *, int>> &rows, const std::vector<float> &extra,
+                    uint32_t gain_off) {
         Chunk ch{};
         ch.off = stream.size();
-        ch.kind = kind;
-        ch.layer = layer;
-        ch.first = first;
-        ch.count = count;
+        ch.gain_off = gain_off;
+        const ChunkHdr hd{kind, layer, first, count};
+        const uint8_t *hb = reinterpret_cast<const uint8_t *>(&hd);
+        stream.insert(stream.end(), hb, hb + sizeof hd);
         for (auto &r : rows) {
             const uint8_t *src = hfile + r.first->data + (size_t)r.second * r.first->cols;
             stream.insert(stream.end(), src, src + r.first->cols);
@@ -790,9 +1030,12 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, Plan *hplan, C
             const uint8_t *src = hfile + r.first->scales + (size_t)r.second * g * 4;
             stream.insert(stream.end(), src, src + g * 4);
         }
+        const uint8_t *eb = reinterpret_cast<const uint8_t *>(extra.data());
+        stream.insert(stream.end(), eb, eb + extra.size() * 4);
         stream.resize(align16(stream.size()), 0);
         ch.bytes = (uint32_t)(stream.size() - ch.off);
-        if (ch.bytes > (uint32_t)kSlotBytes) return false;
+        const uint32_t limit = gain_off ? (uint32_t)kGainOff : (uint32_t)kSlotBytes;
+        if (ch.bytes > limit || (gain_off && gain_off % 16)) return false;
         chunks.push_back(ch);
         return true;
     };
@@ -802,22 +1045,26 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, Plan *hplan, C
             const FileTensor *lt = t + 1 + l * STRIDE;
             int lo, hi;
             std::vector<std::pair<const FileTensor *, int>> rows;
+            std::vector<float> bias;
             split(kQkvPairs, kCTAs, c, lo, hi);
             for (int p = lo; p < hi; p++) {
-                const FileTensor *m;
+                const FileTensor *m, *b;
                 int tt;
-                if (p < DIM / 2) { m = &lt[WQ]; tt = p; }
-                else if (p < DIM / 2 + KV / 2) { m = &lt[WK]; tt = p - DIM / 2; }
-                else { m = &lt[WV]; tt = p - DIM / 2 - KV / 2; }
+                if (p < DIM / 2) { m = &lt[WQ]; b = &lt[BQ]; tt = p; }
+                else if (p < DIM / 2 + KV / 2) { m = &lt[WK]; b = &lt[BK]; tt = p - DIM / 2; }
+                else { m = &lt[WV]; b = &lt[BV]; tt = p - DIM / 2 - KV / 2; }
                 const int r0 = (tt / 32) * HEAD_DIM + tt % 32;
                 rows.push_back({m, r0});
                 rows.push_back({m, r0 + 32});
+                const float *bv = reinterpret_cast<const float *>(hfile + b->data);
+                bias.push_back(bv[r0]);
+                bias.push_back(bv[r0 + 32]);
             }
-            if (!emit(QKV, l, lo, hi - lo, rows)) return 1;
+            if (!emit(QKV, l, lo, hi - lo, rows, bias, lt[ATTN_NORM].data)) return 1;
             rows.clear();
             split(DIM, kCTAs, c, lo, hi);
             for (int r = lo; r < hi; r++) rows.push_back({&lt[WO], r});
-            if (!emit(OPROJ, l, lo, hi - lo, rows)) return 1;
+            if (!emit(OPROJ, l, lo, hi - lo, rows, {}, 0)) return 1;
             split(HIDDEN, kCTAs, c, lo, hi);
             for (int p0 = lo; p0 < hi; p0 += kGateupPerChunk) {
                 const int p1 = p0 + kGateupPerChunk < hi ? p0 + kGateupPerChunk : hi;
@@ -826,26 +1073,29 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, Plan *hplan, C
                     rows.push_back({&lt[WGATE], p});
                     rows.push_back({&lt[WUP], p});
                 }
-                if (!emit(GATEUP, l, p0, p1 - p0, rows)) return 1;
+                if (!emit(GATEUP, l, p0, p1 - p0, rows, {}, p0 == lo ? lt[FFN_NORM].data : 0)) return 1;
             }
             rows.clear();
             split(DIM, kCTAs, c, lo, hi);
             for (int r = lo; r < hi; r++) rows.push_back({&lt[WDOWN], r});
-            if (!emit(DOWN, l, lo, hi - lo, rows)) return 1;
+            if (!emit(DOWN, l, lo, hi - lo, rows, {}, 0)) return 1;
         }
         int lo, hi;
         split(VOCAB, kCTAs, c, lo, hi);
         hplan->head_lo[c] = lo;
+        hplan->head_begin[c] = (uint32_t)chunks.size();
         if (hi - lo > kHeadSlice) return 1;
         for (int r0 = lo; r0 < hi; r0 += kHeadPerChunk) {
             const int r1 = r0 + kHeadPerChunk < hi ? r0 + kHeadPerChunk : hi;
             std::vector<std::pair<const FileTensor *, int>> rows;
             for (int r = r0; r < r1; r++) rows.push_back({&t[0], r});
-            if (!emit(HEAD, LAYERS, r0, r1 - r0, rows)) return 1;
+            if (!emit(HEAD, LAYERS, r0, r1 - r0, rows, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
         }
     }
     hplan->chunk_begin[kCTAs] = (uint32_t)chunks.size();
     hplan->head_lo[kCTAs] = VOCAB;
+    for (int c = 0; c < kCTAs; c++)
+        if (hplan->chunk_begin[c + 1] - hplan->chunk_begin[c] > (uint32_t)kMaxChunksPerCta) return 1;
     if (cudaMalloc(dstream, stream.size()) != cudaSuccess ||
         cudaMalloc(dchunks, chunks.size() * sizeof(Chunk)) != cudaSuccess ||
         cudaMemcpyAsync(*dstream, stream.data(), stream.size(), cudaMemcpyHostToDevice, s) != cudaSuccess ||
@@ -857,15 +1107,16 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, Plan *hplan, C
     }
     hplan->stream = *dstream;
     hplan->chunks = *dchunks;
+    hplan->blob = dfile;
     *stream_bytes = stream.size();
     return 0;
 }
 
 int enqueue_step(const Model *dm, const Plan *dplan, const Buffers &b, Sync *sync, const Scratch &scr, int mode,
                  const sampling::Params *prm, sampling::SeqState *seq, int *out_ring, int *out_count,
-                 const int *prompt, unsigned *host_error, cudaStream_t s)
+                 const int *prompt, unsigned *host_error, cudaStream_t s, unsigned long long *trace)
 {
-    Args a{dm, dplan, b, sync, scr, mode, prm, seq, out_ring, out_count, prompt, host_error};
+    Args a{dm, dplan, b, sync, scr, mode, prm, seq, out_ring, out_count, prompt, host_error, trace};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCTAs);
     cfg.blockDim = dim3(kThreads);

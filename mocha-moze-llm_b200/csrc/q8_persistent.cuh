@@ -9,62 +9,77 @@
 
 namespace q8p {
 
-constexpr int kCTAs = 148;             // one CTA per SM
-constexpr int kConsumerWarps = 8;
+constexpr int kCTAs = 148;                // one CTA per SM
+constexpr int kConsumerWarps = 16;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 streams weights
-constexpr int kSlots = 5;              // shared-memory ring slots
-constexpr int kSlotBytes = 36864;      // 7 rows of down (5168 B) or 38 rows of 896
-constexpr int kAttnChunk = 32;         // positions per attention unit
+constexpr int kSlots = 4;                 // shared-memory ring slots
+constexpr int kSlotBytes = 36864;
+constexpr int kGainBytes = q8::DIM * 4;   // RMSNorm gain delivered with some chunks
+constexpr int kGainOff = kSlotBytes - kGainBytes;
+constexpr int kMaxSplit = 10;             // attention splits per query head
+constexpr int kAttnTarget = 64;           // positions per split when possible
+constexpr int kAttnLenMax = (q8::CONTEXT + kMaxSplit - 1) / kMaxSplit;  // 103
 
 enum Kind : uint32_t { QKV = 0, OPROJ = 1, GATEUP = 2, DOWN = 3, HEAD = 4 };
-enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GATEUP = 3, PH_DOWN = 4, kPhases = 5 };
 enum Mode { FORWARD = 0, FORWARD_PROJECT = 1, PREFILL = 2, DECODE = 3 };
 
-// One contiguous piece of a CTA's weight stream: `count` rows (or row pairs) starting
-// at `first`, stored as int8 rows followed by their fp32 scales, padded to 16 bytes.
+// Where the producer finds a chunk of the weight stream.  The chunk itself starts
+// with a 16-byte ChunkHdr, so the consumers never read descriptors from global memory.
 struct Chunk {
-    uint64_t off;    // byte offset in the stream buffer
-    uint32_t bytes;  // multiple of 16
-    uint32_t kind;
-    uint32_t layer;
-    uint32_t first;  // first row / pair index within the matrix
-    uint32_t count;  // rows or pairs
-    uint32_t pad;
+    uint64_t off;       // byte offset in the stream buffer
+    uint32_t bytes;     // multiple of 16, header included
+    uint32_t gain_off;  // nonzero: byte offset in the model blob of a DIM-float gain
+};
+
+struct ChunkHdr {
+    uint32_t kind, layer, first, count;  // rows or row pairs [first, first+count)
 };
 
 struct Plan {
     const uint8_t *stream;                 // all CTAs' streams back to back
     const Chunk *chunks;                   // all chunks, CTA-major
+    const uint8_t *blob;                   // the uploaded model file (gains)
     uint32_t chunk_begin[kCTAs + 1];
+    uint32_t head_begin[kCTAs];            // first head chunk of each CTA (head chunks are last)
     uint32_t head_lo[kCTAs + 1];           // contiguous vocabulary rows per CTA
 };
 
-// Global synchronisation words (zeroed once at set-up; targets grow with the epoch).
+constexpr int kMaxChunksPerCta = 160;
+
 struct Sync {
-    unsigned counters[q8::LAYERS][kPhases];
-    unsigned done;
-    unsigned epoch;
-    unsigned error;                        // nonzero: a bounded wait expired
-    unsigned tickets[q8::LAYERS][q8::KV_HEADS];
+    unsigned epoch;  // 1 .. 2^24-1, tags the step's data words
+    unsigned done;   // CTAs finished in this step (reset by the last one)
+    unsigned error;  // nonzero: a bounded wait expired or an input was invalid
 };
 
+// Data words exchanged between CTAs: low 32 bits a float, high 32 bits the tag
+// (epoch << 8 | layer << 3 | phase).  A reader polls a word until its tag matches.
 struct Scratch {
-    float *o;                              // combined attention output [DIM]
-    float *partial;                        // [KV_HEADS][CONTEXT/kAttnChunk][GQA][ATTN_PARTIAL]
-    unsigned long long *cand;              // [kCTAs][64] per-CTA candidate keys
+    unsigned long long *q;        // [DIM] rotated queries
+    unsigned long long *kv;       // [KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
+    unsigned long long *part;     // [HEADS][kMaxSplit][ATTN_PARTIAL] attention partials
+    unsigned long long *xmid;     // [DIM] residual after attention
+    unsigned long long *xin;      // [DIM] residual after the FFN (input of the next layer)
+    unsigned long long *h;        // [HIDDEN] SwiGLU output
+    unsigned long long *cand;     // [kCTAs][64] per-CTA candidate keys (plain)
 };
+
+size_t scratch_words();  // total 64-bit words of the data-word buffers (q..h)
+void carve_scratch(unsigned long long *base, Scratch *scr);  // lay q..h out in `base`
 
 // Host side: build the per-CTA weight streams from the reference-format file in host
 // memory, upload them and the chunk table; returns 0 on success.
-int build_plan(const q8::FileHeader *hdr, const unsigned char *hfile, Plan *hplan, Chunk **dchunks,
-               uint8_t **dstream, size_t *stream_bytes, cudaStream_t s);
+int build_plan(const q8::FileHeader *hdr, const unsigned char *hfile, const unsigned char *dfile, Plan *hplan,
+               Chunk **dchunks, uint8_t **dstream, size_t *stream_bytes, cudaStream_t s);
 
 size_t smem_bytes();
 
 // Enqueue one persistent step (cooperative launch) in `mode`.
 int enqueue_step(const q8::Model *dm, const Plan *dplan, const q8::Buffers &b, Sync *sync, const Scratch &scr,
                  int mode, const sampling::Params *prm, sampling::SeqState *seq, int *out_ring, int *out_count,
-                 const int *prompt, unsigned *host_error, cudaStream_t s);
+                 const int *prompt, unsigned *host_error, cudaStream_t s, unsigned long long *trace = nullptr);
+
+constexpr int kTraceStamps = 320;  // per CTA; see the stamp() points in the kernel
 
 int init_device();
 
