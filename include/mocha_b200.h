@@ -73,6 +73,18 @@ int mocha_q8_launches_per_step(mocha_q8 *h);
  * stamps[148][256] (0 = not reached).  Fails on the per-phase graph path. */
 int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps);
 
+/* Penalty + control mask + top-k candidates (the selection gpu_collect performs)
+ * for callers that cannot allocate device memory at call time -- a host that has
+ * reserved the whole GPU memory budget in its own pool, or code running during a
+ * stream capture.  No counterpart in the reference.  logits[0..rows) and
+ * history[0..count) are host arrays; the k best (value, id) pairs, penalised values
+ * and ties to the lower id first, go to host values[k] / ids[k].  stream may be NULL.
+ * All device buffers live in one fixed ~672 KiB __device__ array, so rows <= 151936;
+ * larger requests fail.  The first call on a device looks the array up (make it
+ * before any stream capture); calls that overlap on the GPU share the array and race. */
+int mocha_topk_static(const float *logits, int rows, const int *history, int count, float penalty, int k,
+                      float *values, int *ids, void *stream);
+
 /* Forward steps and kernel launches issued on this handle so far (the counters the
  * reference prints at exit as CUDA_FORWARD_STEPS / CUDA_KERNEL_CALLS). */
 int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches);

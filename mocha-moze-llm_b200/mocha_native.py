@@ -52,6 +52,8 @@ _SIGS = {
     "mocha_q8_stream_begin": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(MochaSampling)]),
     "mocha_q8_stream_next": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "mocha_q8_stream_end": (C.c_int, [C.c_void_p]),
+    "mocha_topk_static": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_void_p,
+                                    C.c_void_p, C.c_void_p]),
     "mocha_q8_trace_step": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "mocha_q8_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
 }

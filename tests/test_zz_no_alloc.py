@@ -1,0 +1,43 @@
+"""mocha_topk_static: candidate selection with every device buffer in a fixed
+__device__ array, for callers that cannot allocate GPU memory when they call it (a
+host owning the whole memory budget in its own pool, or code inside a stream
+capture).  Checked against gpu_collect, which runs the same selection with buffers
+the library allocated, on two calls in a row (the shared array keeps the previous
+call's contents, which must not leak into the next result)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+VOCAB = 151936
+
+
+def test_static_topk_matches_collect(native, q8_model_bytes, golden_q8):
+    lib = native.load()
+    buf = q8_model_bytes
+    assert lib.gpu_init(buf.ctypes.data, buf.nbytes) == 0
+    try:
+        prompt = golden_q8["cases"]["sampled64"]["prompt"]
+        logits = np.empty(VOCAB, np.float32)
+        for pos, tok in enumerate(prompt[:-1]):
+            assert lib.gpu_forward(logits.ctypes.data, tok, pos, 0, 0) == 0
+        hist = np.asarray(prompt[-64:], np.int32)
+        for call, (k, pen) in enumerate(((40, 1.12), (1, 1.0))):
+            # gpu_collect selects from the engine's last projected logits
+            assert lib.gpu_forward(logits.ctypes.data, prompt[-1], len(prompt) - 1 + call, 1, 1) == 0
+            ref = np.empty(VOCAB, np.float32)
+            assert lib.gpu_collect(ref.ctypes.data, hist.ctypes.data, len(hist), pen, k, VOCAB) == 0
+            ref_ids = np.flatnonzero(ref > -3.0e38)
+            vals = np.empty(k, np.float32)
+            ids = np.empty(k, np.int32)
+            rc = lib.mocha_topk_static(logits.ctypes.data, VOCAB, hist.ctypes.data, len(hist), pen, k,
+                                       vals.ctypes.data, ids.ctypes.data, None)
+            assert rc == 0
+            assert sorted(ids.tolist()) == sorted(ref_ids.tolist())
+            assert np.array_equal(vals, ref[ids])                      # same penalised values
+            assert np.all(np.diff(vals) <= 0)                           # best first
+        # beyond the fixed size: rejected, nothing launched
+        big = np.zeros(VOCAB + 1, np.float32)
+        assert lib.mocha_topk_static(big.ctypes.data, VOCAB + 1, hist.ctypes.data, 0, 1.0, 1, vals.ctypes.data,
+                                     ids.ctypes.data, None) == 1
+    finally:
+        assert lib.gpu_finish() == 0
