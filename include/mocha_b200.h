@@ -89,6 +89,35 @@ int mocha_topk_static(const float *logits, int rows, const int *history, int cou
  * reference prints at exit as CUDA_FORWARD_STEPS / CUDA_KERNEL_CALLS). */
 int mocha_q8_counters(mocha_q8 *h, unsigned long long *steps, unsigned long long *launches);
 
+/* ---- GGUF models (llama / qwen2, Q4_K / Q6_K / Q8_0 weights) --------------------
+ * The forward of the reference's GGUF path (llama.cpp's graph for these
+ * architectures, whose matmuls the reference bridge offloads) with attention,
+ * RoPE, norms, KV cache and sampling on the device as well.  No counterpart handle
+ * exists in the reference; the matmul bridge itself is mocha_gguf_matmul. */
+typedef struct mocha_gguf mocha_gguf;
+
+typedef struct {
+    int arch;           /* 0 = llama, 1 = qwen2 */
+    int layers, dim, ffn, heads, kv_heads, head_dim, vocab, context;
+    float eps, rope_base;
+    int rope_neox;      /* 1: split-half pairs (qwen2); 0: interleaved pairs (llama) */
+    int rope_factors;   /* 1 when rope_freqs.weight (llama3 scaling) is present */
+    int eos;            /* tokenizer.ggml.eos_token_id, or -1 */
+} mocha_gguf_info;
+
+/* Parse a GGUF v2/v3 file in host memory and upload it to `device`. */
+int mocha_gguf_open(int device, const void *file, unsigned long long bytes, mocha_gguf **out);
+int mocha_gguf_close(mocha_gguf *m);
+int mocha_gguf_get_info(mocha_gguf *m, mocha_gguf_info *info);
+/* One step for `token` at `pos`; with project, logits (vocab floats) are returned. */
+int mocha_gguf_forward(mocha_gguf *m, int token, int pos, int project, float *logits);
+/* Device-side token loop as mocha_q8_generate (no control-token mask; EOS from the file). */
+int mocha_gguf_generate(mocha_gguf *m, const int *prompt, int n_prompt, int n_new, const mocha_sampling *s,
+                        int *out_tokens, int *n_out, mocha_timing *timing);
+/* Device-timed greedy decode as mocha_q8_bench_decode. */
+int mocha_gguf_bench_decode(mocha_gguf *m, int token, int pos0, int pos_end, int warmup, int steps, float *ms);
+int mocha_gguf_launches_per_step(mocha_gguf *m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,15 +86,14 @@ MB_DEV void stage_x(const float *x, int cols, float *xs, float *x16)
 
 __global__ void __launch_bounds__(kThreads)
     k_gemv_q4k(const uint8_t *__restrict__ body, int rows, int cols, const float *__restrict__ x, int x_stride,
-               float *__restrict__ y, int y_stride)
+               float *__restrict__ y, int y_stride, int accumulate)
 {
     extern __shared__ __align__(16) float smem[];
     float *xs = smem, *x16 = smem + cols;
     stage_x(x + (size_t)blockIdx.y * x_stride, cols, xs, x16);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kWarps + warp;
-    if (row >= rows) return;
     const int nb = cols / 256;
+    for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
     const uint8_t *rp = body + (size_t)row * nb * 144;
     float acc = 0.f;
     for (int qc = lane; qc < nb * 8; qc += 32) {
@@ -120,20 +119,23 @@ __global__ void __launch_bounds__(kThreads)
         acc += (d * sc_hi) * s_hi - (dmin * m_hi) * x16[e_hi >> 4];
     }
     acc = mb::warp_sum(acc);
-    if (lane == 0) y[(size_t)blockIdx.y * y_stride + row] = acc;
+    if (lane == 0) {
+        float *out = y + (size_t)blockIdx.y * y_stride + row;
+        *out = accumulate ? *out + acc : acc;
+    }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads)
     k_gemv_q6k(const uint8_t *__restrict__ body, const uint16_t *__restrict__ dq, int rows, int cols,
-               const float *__restrict__ x, int x_stride, float *__restrict__ y, int y_stride)
+               const float *__restrict__ x, int x_stride, float *__restrict__ y, int y_stride, int accumulate)
 {
     extern __shared__ __align__(16) float smem[];
     float *xs = smem, *x16 = smem + cols;
     stage_x(x + (size_t)blockIdx.y * x_stride, cols, xs, x16);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kWarps + warp;
-    if (row >= rows) return;
     const int nb = cols / 256;
+    for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
     float acc = 0.f;
     for (int qc = lane; qc < nb * 8; qc += 32) {
         const int blk = qc >> 3, c8 = qc & 7;
@@ -160,12 +162,16 @@ __global__ void __launch_bounds__(kThreads)
         acc += (d * sc_lo) * s_lo + (d * sc_hi) * s_hi;
     }
     acc = mb::warp_sum(acc);
-    if (lane == 0) y[(size_t)blockIdx.y * y_stride + row] = acc;
+    if (lane == 0) {
+        float *out = y + (size_t)blockIdx.y * y_stride + row;
+        *out = accumulate ? *out + acc : acc;
+    }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads)
     k_gemv_q80(const uint8_t *__restrict__ body, const uint16_t *__restrict__ dq, int rows, int cols,
-               const float *__restrict__ x, int x_stride, float *__restrict__ y, int y_stride)
+               const float *__restrict__ x, int x_stride, float *__restrict__ y, int y_stride, int accumulate)
 {
     extern __shared__ __align__(16) float smem[];
     float *xs = smem;
@@ -174,18 +180,21 @@ __global__ void __launch_bounds__(kThreads)
             *reinterpret_cast<const float4 *>(x + (size_t)blockIdx.y * x_stride + i);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kWarps + warp;
-    if (row >= rows) return;
     const int nb = cols / 32;
-    const uint8_t *rp = body + (size_t)row * cols;
-    float acc = 0.f;
-    for (int c = lane; c < cols / 16; c += 32) {
-        const int4 q = mb::ld_stream16(rp + c * 16);
-        const float d = half_bits_to_float(__ldg(dq + (size_t)row * nb + (c >> 1)));
-        acc = fmaf(d, mb::dot16_s8_f32(q, xs + c * 16), acc);
+    for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
+        const uint8_t *rp = body + (size_t)row * cols;
+        float acc = 0.f;
+        for (int c = lane; c < cols / 16; c += 32) {
+            const int4 q = mb::ld_stream16(rp + c * 16);
+            const float d = half_bits_to_float(__ldg(dq + (size_t)row * nb + (c >> 1)));
+            acc = fmaf(d, mb::dot16_s8_f32(q, xs + c * 16), acc);
+        }
+        acc = mb::warp_sum(acc);
+        if (lane == 0) {
+            float *out = y + (size_t)blockIdx.y * y_stride + row;
+            *out = accumulate ? *out + acc : acc;
+        }
     }
-    acc = mb::warp_sum(acc);
-    if (lane == 0) y[(size_t)blockIdx.y * y_stride + row] = acc;
 }
 
 __global__ void k_repack_q6k(const uint8_t *__restrict__ raw, size_t nblocks, uint8_t *__restrict__ body,
@@ -253,6 +262,46 @@ __global__ void k_dequant(DevMat m, float *__restrict__ out)
     }
 }
 
+// row `*row_index` of m, dequantised exactly (same formulas as k_dequant)
+__global__ void k_dequant_row(DevMat m, const int *__restrict__ row_index, float *__restrict__ out)
+{
+    const size_t r = (size_t)*row_index;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < m.cols; c += gridDim.x * blockDim.x) {
+        float v;
+        if (m.type == Q8_0) {
+            const int nb = m.cols / 32;
+            v = __fmul_rn(half_bits_to_float(m.d[r * nb + c / 32]), (float)(int8_t)m.body[r * m.cols + c]);
+        } else if (m.type == Q4_K) {
+            const int nb = m.cols / 256, blk = c / 256, i = c & 255, j = i / 32;
+            const uint8_t *p = m.body + (r * nb + blk) * 144;
+            const float d = half_bits_to_float(p[0] | (p[1] << 8)), dmin = half_bits_to_float(p[2] | (p[3] << 8));
+            const uint8_t *s = p + 4;
+            uint32_t sc, mn;
+            if (j < 4) {
+                sc = s[j] & 63u;
+                mn = s[j + 4] & 63u;
+            } else {
+                sc = (s[j + 4] & 15u) | ((uint32_t)(s[j - 4] >> 6) << 4);
+                mn = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+            }
+            uint32_t q = p[16 + (i / 64) * 32 + (i & 31)];
+            q = (j & 1) ? q >> 4 : q & 15u;
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+        } else {
+            const int nb = m.cols / 256, blk = c / 256, i = c & 255;
+            const size_t bi = r * nb + blk;
+            const uint8_t *p = m.body + bi * 208;
+            const int half = i / 128, g = (i & 127) / 32, l = i & 31;
+            uint32_t lo = p[half * 64 + (g & 1) * 32 + l];
+            lo = g < 2 ? lo & 15u : lo >> 4;
+            const uint32_t hi = (p[128 + half * 32 + l] >> (2 * g)) & 3u;
+            const int q = (int)(lo | (hi << 4)) - 32;
+            v = __fmul_rn(__fmul_rn(half_bits_to_float(m.d[bi]), (float)(int8_t)p[192 + i / 16]), (float)q);
+        }
+        out[c] = v;
+    }
+}
+
 int launch_ok(const char *what)
 {
     const cudaError_t e = cudaGetLastError();
@@ -292,6 +341,12 @@ int enqueue_repack(int type, const uint8_t *raw, int rows, int cols, uint8_t *ds
     return launch_ok("gguf repack");
 }
 
+int enqueue_dequant_row(const DevMat &m, const int *row_index, float *out, cudaStream_t s)
+{
+    k_dequant_row<<<(m.cols + 255) / 256, 256, 0, s>>>(m, row_index, out);
+    return launch_ok("gguf dequant row");
+}
+
 int enqueue_dequant(const DevMat &m, float *out, cudaStream_t s)
 {
     k_dequant<<<mb::kSMs * 8, 256, 0, s>>>(m, out);
@@ -299,7 +354,7 @@ int enqueue_dequant(const DevMat &m, float *out, cudaStream_t s)
 }
 
 int enqueue_gemv(const DevMat &m, const float *x, int vectors, int x_stride_f, float *y, int y_stride_f,
-                 cudaStream_t s)
+                 cudaStream_t s, bool accumulate)
 {
     if (vectors < 1 || vectors > 65535 || m.cols % 256 || m.cols <= 0 || m.rows <= 0) return 1;
     const size_t smem = (size_t)(m.cols + (m.type == Q8_0 ? 0 : m.cols / 16)) * sizeof(float);
@@ -316,13 +371,16 @@ int enqueue_gemv(const DevMat &m, const float *x, int vectors, int x_stride_f, f
             return 1;
         configured[dev] = true;
     }
-    const dim3 grid((m.rows + kWarps - 1) / kWarps, vectors);
+    // enough CTAs to fill the GPU a few times over; each CTA stages x once and walks rows
+    const int row_blocks = (m.rows + kWarps - 1) / kWarps;
+    const dim3 grid(row_blocks < mb::kSMs * 8 ? row_blocks : mb::kSMs * 8, vectors);
+    const int acc = accumulate ? 1 : 0;
     if (m.type == Q4_K)
-        k_gemv_q4k<<<grid, kThreads, smem, s>>>(m.body, m.rows, m.cols, x, x_stride_f, y, y_stride_f);
+        k_gemv_q4k<<<grid, kThreads, smem, s>>>(m.body, m.rows, m.cols, x, x_stride_f, y, y_stride_f, acc);
     else if (m.type == Q6_K)
-        k_gemv_q6k<<<grid, kThreads, smem, s>>>(m.body, m.d, m.rows, m.cols, x, x_stride_f, y, y_stride_f);
+        k_gemv_q6k<<<grid, kThreads, smem, s>>>(m.body, m.d, m.rows, m.cols, x, x_stride_f, y, y_stride_f, acc);
     else if (m.type == Q8_0)
-        k_gemv_q80<<<grid, kThreads, smem, s>>>(m.body, m.d, m.rows, m.cols, x, x_stride_f, y, y_stride_f);
+        k_gemv_q80<<<grid, kThreads, smem, s>>>(m.body, m.d, m.rows, m.cols, x, x_stride_f, y, y_stride_f, acc);
     else
         return 1;
     return launch_ok("gguf gemv");

@@ -43,9 +43,13 @@ DevMat make_devmat(int type, int rows, int cols, uint8_t *dst);
 // out[r*cols + c] = dequantised weight, exact (no fused multiply-add), for checking.
 int enqueue_dequant(const DevMat &m, float *out, cudaStream_t s);
 
-// y[v*y_stride_f + r] = sum_c W[r][c] * x[v*x_stride_f + c] for v < vectors (fp32
-// activations, fp32 accumulation); strides in floats.
+// y[v*y_stride_f + r] (+)= sum_c W[r][c] * x[v*x_stride_f + c] for v < vectors (fp32
+// activations, fp32 accumulation); strides in floats.  With accumulate the dot is added
+// to y (residual connections).
 int enqueue_gemv(const DevMat &m, const float *x, int vectors, int x_stride_f, float *y, int y_stride_f,
-                 cudaStream_t s);
+                 cudaStream_t s, bool accumulate = false);
+
+// out[c] = exact dequantised weight (row *row_index, read on the device), c < cols.
+int enqueue_dequant_row(const DevMat &m, const int *row_index, float *out, cudaStream_t s);
 
 }  // namespace gguf

@@ -144,7 +144,7 @@ __global__ void k_sample(const unsigned long long *__restrict__ keys, const Para
     uint32_t seed = st->seed;
     int token = draw_token(keys, p, seed);
     st->seed = seed;
-    if (token < 0 || token >= p.vocab) token = p.eos;  // never index past the embedding
+    if (token < 0 || token >= p.vocab) token = p.eos >= 0 ? p.eos : 0;  // never index past the embedding
     record_token(token, p, st, out_ring, out_count);
     *token_out = token;
     if (pos_inout) (*pos_inout)++;

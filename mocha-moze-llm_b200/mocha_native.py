@@ -22,6 +22,13 @@ class MochaSampling(C.Structure):
                 ("repeat_penalty", C.c_float), ("seed", C.c_uint)]
 
 
+class MochaGgufInfo(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("arch", "layers", "dim", "ffn", "heads", "kv_heads", "head_dim", "vocab",
+                                       "context")] + \
+               [("eps", C.c_float), ("rope_base", C.c_float), ("rope_neox", C.c_int), ("rope_factors", C.c_int),
+                ("eos", C.c_int)]
+
+
 class MochaTiming(C.Structure):
     _fields_ = [("prefill_s", C.c_double), ("decode_s", C.c_double), ("generated", C.c_int)]
 
@@ -55,6 +62,15 @@ _SIGS = {
     "mocha_topk_static": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_void_p,
                                     C.c_void_p, C.c_void_p]),
     "mocha_q8_trace_step": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "mocha_gguf_open": (C.c_int, [C.c_int, C.c_void_p, C.c_ulonglong, C.POINTER(C.c_void_p)]),
+    "mocha_gguf_close": (C.c_int, [C.c_void_p]),
+    "mocha_gguf_get_info": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "mocha_gguf_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "mocha_gguf_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(MochaSampling),
+                                      C.c_void_p, C.POINTER(C.c_int), C.POINTER(MochaTiming)]),
+    "mocha_gguf_bench_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.POINTER(C.c_float)]),
+    "mocha_gguf_launches_per_step": (C.c_int, [C.c_void_p]),
     "mocha_q8_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
 }
 
@@ -149,6 +165,57 @@ class Q8Handle:
         rc = self.lib.mocha_q8_bench_decode(self.h, token, pos0, pos_end, warmup, steps, C.byref(ms))
         if rc != 0:
             raise RuntimeError("mocha_q8_bench_decode failed")
+        return ms.value
+
+
+class GgufHandle:
+    """A GGUF llama / qwen2 model resident on one device (mocha_gguf handle)."""
+
+    def __init__(self, device: int, file_bytes, lib: C.CDLL | None = None):
+        self.lib = lib or load()
+        self._buf = file_bytes
+        ptr = C.c_void_p()
+        addr, size = _addr(file_bytes)
+        if self.lib.mocha_gguf_open(device, addr, size, C.byref(ptr)) != 0:
+            raise RuntimeError("mocha_gguf_open failed")
+        self.h = ptr
+        self.info = MochaGgufInfo()
+        self.lib.mocha_gguf_get_info(self.h, C.byref(self.info))
+
+    def close(self):
+        if self.h:
+            self.lib.mocha_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, token: int, pos: int, project: bool = True):
+        import numpy as np
+        out = np.empty(self.info.vocab, dtype=np.float32)
+        if self.lib.mocha_gguf_forward(self.h, token, pos, int(project), out.ctypes.data) != 0:
+            raise RuntimeError("mocha_gguf_forward failed")
+        return out
+
+    def generate(self, prompt, n_new, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0, seed=42):
+        import numpy as np
+        p = np.asarray(prompt, dtype=np.int32)
+        out = np.zeros(n_new, dtype=np.int32)
+        n = C.c_int()
+        t = MochaTiming()
+        s = MochaSampling(temperature, top_k, top_p, penalty, seed)
+        if self.lib.mocha_gguf_generate(self.h, p.ctypes.data, len(p), n_new, C.byref(s), out.ctypes.data,
+                                        C.byref(n), C.byref(t)) != 0:
+            raise RuntimeError("mocha_gguf_generate failed")
+        return out[:n.value].tolist(), t
+
+    def bench_decode(self, token, pos0, pos_end, warmup, steps) -> float:
+        ms = C.c_float()
+        if self.lib.mocha_gguf_bench_decode(self.h, token, pos0, pos_end, warmup, steps, C.byref(ms)) != 0:
+            raise RuntimeError("mocha_gguf_bench_decode failed")
         return ms.value
 
 

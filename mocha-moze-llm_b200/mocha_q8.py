@@ -108,8 +108,7 @@ def write_random_model(path: str, seed: int = 1) -> str:
 
 def model_path(seed: int = 1, cache_dir: str | None = None) -> str:
     """Path of the cached random model for ``seed``, writing it on first use."""
-    cache_dir = cache_dir or os.environ.get("MOCHA_MODEL_CACHE") or os.path.join(
-        os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "_work", "models")
+    cache_dir = cache_dir or os.environ.get("MOCHA_MODEL_CACHE") or "/tmp/mocha-b200-models"
     os.makedirs(cache_dir, exist_ok=True)
     path = os.path.join(cache_dir, f"qwen05b-q8-seed{seed}.bin")
     if not os.path.exists(path) or os.path.getsize(path) != FILE_BYTES:

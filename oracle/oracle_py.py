@@ -145,3 +145,104 @@ def gguf_matmul(type_id, raw, cols, rows, x):
     if rc:
         raise ValueError("gguf_o_matmul rejected the arguments")
     return y
+
+
+# ---- GGUF model forward (llama / qwen2) ---------------------------------------------
+
+class _GoTensor(C.Structure):
+    _fields_ = [("type", C.c_int), ("rows", C.c_int), ("cols", C.c_int), ("data", C.c_void_p)]
+
+
+class _GoModel(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("layers", "dim", "heads", "kv_heads", "head_dim", "ffn", "vocab", "context",
+                                       "neox")] + \
+               [("eps", C.c_float), ("rope_base", C.c_float), ("embd", _GoTensor), ("out_norm", _GoTensor),
+                ("rope_freqs", _GoTensor)] + \
+               [(n, C.POINTER(_GoTensor)) for n in ("attn_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo", "ffn_norm",
+                                                    "wg", "wu", "wd")]
+
+
+class GGUFOracle:
+    """llama / qwen2 GGUF forward restated in C (unpinned: llama.cpp is not available)."""
+
+    def __init__(self, path, context=1024):
+        from gguf import GGUFReader
+        L = lib()
+        L.go_create.restype = C.c_void_p
+        L.go_create.argtypes = [C.POINTER(_GoModel)]
+        L.go_destroy.argtypes = [C.c_void_p]
+        L.go_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        self.reader = r = GGUFReader(path)
+        arch = bytes(r.fields["general.architecture"].parts[-1]).decode()
+
+        def num(key):
+            f = r.fields[f"{arch}.{key}"]
+            return f.parts[f.data[0]][0]
+
+        self.tensors = {t.name: t for t in r.tensors}
+        self._keep = []
+
+        def gt(name):
+            if name not in self.tensors:
+                return _GoTensor(0, 0, 0, None)
+            t = self.tensors[name]
+            arr = np.ascontiguousarray(t.data)
+            self._keep.append(arr)
+            cols = int(t.shape[0])
+            rows = int(t.shape[1]) if len(t.shape) > 1 else 1
+            return _GoTensor(int(t.tensor_type), rows, cols, arr.ctypes.data)
+
+        layers = int(num("block_count"))
+        dim = int(num("embedding_length"))
+        heads = int(num("attention.head_count"))
+        m = _GoModel()
+        m.layers, m.dim, m.heads = layers, dim, heads
+        m.kv_heads = int(num("attention.head_count_kv"))
+        m.head_dim = dim // heads
+        m.ffn = int(num("feed_forward_length"))
+        m.vocab = int(self.tensors["token_embd.weight"].shape[1])
+        m.context = context
+        m.neox = 1 if arch == "qwen2" else 0
+        m.eps = float(num("attention.layer_norm_rms_epsilon"))
+        m.rope_base = float(num("rope.freq_base"))
+        m.embd = gt("token_embd.weight")
+        m.out_norm = gt("output_norm.weight")
+        m.rope_freqs = gt("rope_freqs.weight")
+        arrays = {}
+        for key, suffix in (("attn_norm", "attn_norm.weight"), ("wq", "attn_q.weight"), ("wk", "attn_k.weight"),
+                            ("wv", "attn_v.weight"), ("bq", "attn_q.bias"), ("bk", "attn_k.bias"),
+                            ("bv", "attn_v.bias"), ("wo", "attn_output.weight"), ("ffn_norm", "ffn_norm.weight"),
+                            ("wg", "ffn_gate.weight"), ("wu", "ffn_up.weight"), ("wd", "ffn_down.weight")):
+            arr = (_GoTensor * layers)(*[gt(f"blk.{l}.{suffix}") for l in range(layers)])
+            arrays[key] = arr
+            setattr(m, key, C.cast(arr, C.POINTER(_GoTensor)))
+        self._arrays = arrays
+        self.model = m
+        self.vocab = m.vocab
+        self.arch = arch
+        self.s = L.go_create(C.byref(m))
+        if not self.s:
+            raise MemoryError("go_create failed")
+
+    def __del__(self):
+        if getattr(self, "s", None):
+            lib().go_destroy(self.s)
+            self.s = None
+
+    def forward(self, token, pos, project=True):
+        out = np.empty(self.vocab, np.float32) if project else None
+        lib().go_forward(self.s, token, pos, out.ctypes.data if project else None)
+        return out
+
+    def greedy(self, prompt, n):
+        out = []
+        tok = prompt[0]
+        for pos in range(len(prompt) + n - 1):
+            project = pos + 1 >= len(prompt)
+            logits = self.forward(tok, pos, project)
+            if pos + 1 < len(prompt):
+                tok = prompt[pos + 1]
+                continue
+            tok = int(np.argmax(logits))
+            out.append(tok)
+        return out
