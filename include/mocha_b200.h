@@ -118,6 +118,15 @@ int mocha_gguf_generate(mocha_gguf *m, const int *prompt, int n_prompt, int n_ne
 int mocha_gguf_bench_decode(mocha_gguf *m, int token, int pos0, int pos_end, int warmup, int steps, float *ms);
 int mocha_gguf_launches_per_step(mocha_gguf *m);
 
+/* ---- tensor-core GEMM check (no reference counterpart) ----------------------------
+ * y[n][rows] = x[n][cols] . dequant(q, scales)^T for one grouped-Q8 matrix (int8
+ * [rows][cols] row-major, fp32 scale per 64 consecutive weights), computed by the
+ * tcgen05 GEMM of the batched paths.  rows % 128 == 0, cols % 64 == 0, 1 <= n <= 1024;
+ * splits = 0 lets the kernel choose its K split.  Allocates and frees its own device
+ * buffers; for tests. */
+int mocha_tc_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
+                        const float *x, float *y, int splits);
+
 #ifdef __cplusplus
 }
 #endif

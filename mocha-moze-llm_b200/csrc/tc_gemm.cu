@@ -1,0 +1,275 @@
+// tcgen05 GEMM with TMA-fed shared-memory ring and TMEM accumulator (see tc_gemm.cuh).
+#include <stdio.h>
+
+#include "mb_async.cuh"
+#include "tc_gemm.cuh"
+
+namespace mb {
+namespace tc {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // bf16 elements per 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = kBM * kBK * 2;
+
+template <int BN>
+struct Cfg {
+    static constexpr int stages = BN <= 64 ? 4 : (BN <= 128 ? 3 : 2);
+    static constexpr uint32_t b_bytes = BN * kBK * 2;
+    static constexpr uint32_t stage_bytes = 2 * kABytes + 2 * b_bytes;
+    static constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
+    static constexpr size_t smem = 1024 + (size_t)stages * stage_bytes + 256;
+};
+
+MB_DEV void gemm_fail(int *err, volatile int *abort, int code)
+{
+    *abort = 1;
+    atomicCAS(err, 0, code);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_bf16x3(const __grid_constant__ GemmParams p)
+{
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(smem + C::stages * C::stage_bytes);
+    uint64_t *empty = full + C::stages;
+    uint64_t *accum = empty + C::stages;
+    uint32_t *tmem_slot = (uint32_t *)(accum + 1);
+    volatile int *abort = (volatile int *)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+    const int ks0 = blockIdx.z * p.ksteps;
+    const int nk = min(p.ksteps, p.K / kBK - ks0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::stages; s++) {
+            as::mbar_init(&full[s], 1);
+            as::mbar_init(&empty[s], 1);
+        }
+        as::mbar_init(accum, 1);
+        *abort = 0;
+        as::fence_barrier_init();
+    }
+    if (warp == 1) as::tmem_alloc(tmem_slot, C::tmem_cols);
+    as::tc_fence_before();
+    __syncthreads();
+    as::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer
+        as::prefetch_map(&p.a_hi);
+        as::prefetch_map(&p.a_lo);
+        as::prefetch_map(&p.b_hi);
+        as::prefetch_map(&p.b_lo);
+        int issued = 0;
+        for (int k = 0; k < nk; k++) {
+            const int s = k % C::stages;
+            if (k >= C::stages && !as::mbar_wait(&empty[s], ((k / C::stages) & 1) ^ 1, abort)) {
+                gemm_fail(p.err, abort, 11);
+                break;
+            }
+            uint8_t *st = smem + s * C::stage_bytes;
+            as::mbar_expect_tx(&full[s], C::stage_bytes);
+            const int kc = (ks0 + k) * kBK;
+            as::tma_load_2d(st, &p.a_hi, kc, m0, &full[s]);
+            as::tma_load_2d(st + kABytes, &p.a_lo, kc, m0, &full[s]);
+            as::tma_load_2d(st + 2 * kABytes, &p.b_hi, kc, n0, &full[s]);
+            as::tma_load_2d(st + 2 * kABytes + C::b_bytes, &p.b_lo, kc, n0, &full[s]);
+            issued++;
+        }
+        if (*abort) {
+            // let the copies already in flight land before the CTA can exit
+            const int first = issued > C::stages ? issued - C::stages : 0;
+            for (int k = first; k < issued; k++) {
+                const volatile int never = 0;
+                as::mbar_wait(&full[k % C::stages], (k / C::stages) & 1, &never);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        constexpr uint32_t idesc = as::idesc_bf16_f32(kBM, BN);
+        for (int k = 0; k < nk; k++) {
+            const int s = k % C::stages;
+            if (!as::mbar_wait(&full[s], (k / C::stages) & 1, abort)) {
+                gemm_fail(p.err, abort, 12);
+                break;
+            }
+            as::tc_fence_after();
+            const uint32_t a_hi = as::smem_u32(smem + s * C::stage_bytes);
+            const uint32_t a_lo = a_hi + kABytes, b_hi = a_hi + 2 * kABytes, b_lo = b_hi + C::b_bytes;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; kk++) {
+                const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzled row
+                as::mma_bf16(tmem, as::sw128_desc(a_hi + off), as::sw128_desc(b_hi + off), idesc, k > 0 || kk > 0);
+                as::mma_bf16(tmem, as::sw128_desc(a_hi + off), as::sw128_desc(b_lo + off), idesc, true);
+                as::mma_bf16(tmem, as::sw128_desc(a_lo + off), as::sw128_desc(b_hi + off), idesc, true);
+            }
+            as::mma_commit(&empty[s]);
+        }
+        as::mma_commit(accum);
+        if (*abort) {
+            const volatile int never = 0;
+            as::mbar_wait(accum, 0, &never);  // every issued MMA has finished with TMEM
+        }
+    } else if (warp >= 2) {
+        // epilogue: TMEM lanes (warp % 4) * 32 .. +31 are weight rows of this warp
+        const int q = warp & 3;
+        const bool waited = as::mbar_wait(accum, 0, abort);
+        as::tc_fence_after();
+        // tcgen05.ld is warp-collective: take the decision for the whole warp
+        const bool ok = __all_sync(0xffffffffu, waited && !*abort);
+        if (!waited) gemm_fail(p.err, abort, 13);
+        if (ok) {
+            const int m = m0 + q * 32 + lane;
+            float *d = p.d + (long long)blockIdx.z * p.split_stride + m;
+            const int n_end = min(BN, p.N - n0);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                if (c >= n_end) break;
+                uint32_t r[16];
+                as::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+                as::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (c + j < n_end) d[(long long)(n0 + c + j) * p.ldd] = __uint_as_float(r[j]);
+            }
+        }
+        as::tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        as::tc_fence_after();
+        as::tmem_free(tmem, C::tmem_cols);
+    }
+}
+
+__global__ void k_split_weights(const int8_t *__restrict__ q, const float *__restrict__ scales, size_t count,
+                                __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+        const float w = (float)q[i] * scales[i >> 6];
+        split_bf16(w, hi[i], lo[i]);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)ptr;
+    }
+    return fn;
+}
+
+// Row-major bf16 [rows][K] with a box of {64, box_rows} and 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, long long rows, long long K, int box_rows)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) {
+        fprintf(stderr, "mocha: cuTensorMapEncodeTiled unavailable\n");
+        return 1;
+    }
+    if (((uintptr_t)base & 15) || (K * 2) % 16 || K % kBK || box_rows < 1 || box_rows > 256) {
+        fprintf(stderr, "mocha: bad tensor map geometry\n");
+        return 1;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        fprintf(stderr, "mocha: cuTensorMapEncodeTiled failed (%d)\n", (int)r);
+        return 1;
+    }
+    return 0;
+}
+
+template <int BN>
+int setup_attr()
+{
+    static bool done = false;
+    if (!done) {
+        MB_CHECK(cudaFuncSetAttribute(k_gemm_bf16x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Cfg<BN>::smem));
+        done = true;
+    }
+    return 0;
+}
+
+}  // namespace
+
+int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int M, int K,
+              const __nv_bfloat16 *x_hi, const __nv_bfloat16 *x_lo, int n_max, float *d, long long ldd, int splits,
+              int *err)
+{
+    if (M <= 0 || M % kBM || K <= 0 || K % kBK || n_max <= 0 || ldd < M) {
+        fprintf(stderr, "mocha: gemm_plan: unsupported shape M=%d K=%d n=%d\n", M, K, n_max);
+        return 1;
+    }
+    g->bn = n_max <= 64 ? 64 : 128;
+    if (make_map(&g->p.a_hi, w_hi, M, K, kBM) || make_map(&g->p.a_lo, w_lo, M, K, kBM) ||
+        make_map(&g->p.b_hi, x_hi, n_max, K, g->bn) || make_map(&g->p.b_lo, x_lo, n_max, K, g->bn))
+        return 1;
+    const int ksteps = K / kBK;
+    const int tiles = (M / kBM) * ((n_max + g->bn - 1) / g->bn);
+    if (splits <= 0) splits = (2 * kSMs + tiles - 1) / tiles;
+    if (splits > ksteps) splits = ksteps;
+    if (splits < 1) splits = 1;
+    const int per = (ksteps + splits - 1) / splits;
+    g->splits = (ksteps + per - 1) / per;
+    g->p.ksteps = per;
+    g->p.d = d;
+    g->p.ldd = ldd;
+    g->p.split_stride = (long long)n_max * ldd;
+    g->p.M = M;
+    g->p.N = n_max;
+    g->p.K = K;
+    g->p.err = err;
+    g->smem = g->bn == 64 ? Cfg<64>::smem : Cfg<128>::smem;
+    return g->bn == 64 ? setup_attr<64>() : setup_attr<128>();
+}
+
+int gemm_launch(const Gemm &g, int n, cudaStream_t s)
+{
+    if (n <= 0 || n > g.p.N) {
+        fprintf(stderr, "mocha: gemm_launch: n=%d outside 1..%d\n", n, g.p.N);
+        return 1;
+    }
+    GemmParams p = g.p;
+    p.N = n;
+    const dim3 grid(p.M / kBM, (n + g.bn - 1) / g.bn, g.splits);
+    if (g.bn == 64)
+        k_gemm_bf16x3<64><<<grid, kThreads, g.smem, s>>>(p);
+    else
+        k_gemm_bf16x3<128><<<grid, kThreads, g.smem, s>>>(p);
+    MB_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int split_weights(const int8_t *q, const float *scales, size_t count, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
+                  cudaStream_t s)
+{
+    k_split_weights<<<kSMs * 8, 256, 0, s>>>(q, scales, count, hi, lo);
+    MB_CHECK(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace tc
+}  // namespace mb

@@ -72,6 +72,8 @@ _SIGS = {
                                           C.POINTER(C.c_float)]),
     "mocha_gguf_launches_per_step": (C.c_int, [C.c_void_p]),
     "mocha_q8_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
+    "mocha_tc_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_int]),
 }
 
 
