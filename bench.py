@@ -32,6 +32,11 @@ PROMPT_LEN, NEW_TOKENS, PROMPT_SEED, MODEL_SEED = 34, 256, 7, 1
 WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per token
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 REF_SAMPLE_TOKENS = 32
+# prefill workload: one 1024-token prompt, head on the last position
+PREFILL_LEN = 1024
+PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
+# batched serving workload: 512 sequences, 128-token prompts, 384 generated, 64 per GPU at a time
+SERVE_SEQS, SERVE_PROMPT, SERVE_NEW, SERVE_BATCH = 512, 128, 384, 64
 
 
 def dist_env():
@@ -186,6 +191,75 @@ def reference_arm(args):
     return 0
 
 
+def peak_tflops():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def bench_batched(group, data, args):
+    """Prefill of one 1024-token prompt and the batched serving job on this rank's
+    share of the 512 sequences (tcgen05 GEMM path)."""
+    import numpy as np
+
+    import mocha_native
+    rank, world, local = group.rank, group.world, group.local
+    h = mocha_native.Q8BatchHandle(local, data, max_rows=SERVE_BATCH * SERVE_PROMPT, slots=SERVE_BATCH)
+    group.barrier()
+    pre_ms = h.bench_prefill(PREFILL_LEN, 1234 + rank, args.warmup, args.steps)
+    # batched serving: sequences i with i % world == rank
+    mine = [i for i in range(SERVE_SEQS) if i % world == rank]
+    prompts = np.random.default_rng(2024).integers(0, 151936, (SERVE_SEQS, SERVE_PROMPT))[mine]
+    h.generate(prompts[:SERVE_BATCH], 8, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
+    group.barrier()
+    t0 = time.perf_counter()
+    toks, t = h.generate(prompts, SERVE_NEW, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
+    wall = time.perf_counter() - t0
+    launches = h.launches_per_step()
+    h.close()
+    return {"prefill_ms": pre_ms, "decode_s": t.decode_s, "prefill_s": t.prefill_s, "generated": t.generated,
+            "nseq": len(mine), "wall": wall, "launches": launches}
+
+
+def batched_objects(gathered, args, world):
+    tf_peak, tf_kind = peak_tflops()
+    hbm_peak, hbm_kind = peaks()
+    pre_ms = max(g["prefill_ms"] for g in gathered) / args.steps
+    prefill_tps = PREFILL_LEN * world / (pre_ms / 1e3)
+    achieved_tf = PREFILL_FLOP / (pre_ms / 1e3) / 1e12
+    prefill = {"value": prefill_tps, "unit": "tok/s", "ms_per_prompt": pre_ms,
+               "config": {"workload": "one 1024-token prompt of uniform random ids, head on the last position",
+                          "per_gpu": True},
+               "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                            "frac": achieved_tf / tf_peak, "peak_kind": tf_kind,
+                            "algorithmic_flop_per_prompt": PREFILL_FLOP,
+                            "note": "bf16 hi/lo split: the tensor pipe issues 3x the layer-GEMM FLOPs"}}
+    decode_s = max(g["decode_s"] for g in gathered)
+    wall = max(g["wall"] for g in gathered)
+    gen = sum(g["generated"] for g in gathered)
+    first = sum(g["nseq"] for g in gathered)
+    decode_tps = (gen - first) / decode_s
+    # per GPU and decode step: weights once + the KV of 64 sequences at mean position
+    steps_per_gpu = (SERVE_NEW - 1) * ((SERVE_SEQS // world + SERVE_BATCH - 1) // SERVE_BATCH)
+    mean_pos1 = (SERVE_PROMPT + 1 + SERVE_PROMPT + SERVE_NEW - 1) / 2
+    step_bytes = WEIGHT_BYTES + SERVE_BATCH * KV_BYTES_PER_POS * mean_pos1
+    achieved = step_bytes * steps_per_gpu / decode_s / 1e9
+    batched = {"value": decode_tps, "unit": "tok/s", "decode_s": decode_s,
+               "e2e": {"value": gen / wall, "unit": "tok/s", "path": "mocha_q8b_generate (prompt pass included)"},
+               "config": {"workload": "512 sequences x (128-token prompt + 384 generated), T=0.7 top-k 40 "
+                                      "top-p 0.9 penalty 1.12, 64 per GPU per wave",
+                          "parallelism": f"replicas x{world}", "scaling": "strong (512 sequences in total)"},
+               "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                            "frac": achieved / hbm_peak, "peak_kind": hbm_kind,
+                            "algorithmic_bytes_per_step": step_bytes,
+                            "note": "weights counted in the reference format (int8 + fp32 scales); this path "
+                                    "streams bf16 hi/lo copies, 4 B per weight"},
+               "gpu_launches_per_step": gathered[0]["launches"]}
+    return prefill, batched
+
+
 def cpu_baseline(model_path, prompt):
     binary = os.path.join(ORACLE, "_ref", "minimind_cpu")
     cores = os.cpu_count()
@@ -212,6 +286,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the prefill and batched-serving objects")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -245,7 +320,8 @@ def main():
         e2e_wall += time.perf_counter() - t0
     launches = mocha_native.load().mocha_q8_launches_per_step(h.h) * NEW_TOKENS * args.steps
     h.close()
-    gathered = group.gather({"ms": ms, "e2e": e2e_wall, "clocks": clocks})
+    extra = {} if args.no_batched else bench_batched(group, data, args)
+    gathered = group.gather({"ms": ms, "e2e": e2e_wall, "clocks": clocks, **extra})
     if rank != 0:
         group.close()
         return 0
@@ -277,6 +353,8 @@ def main():
         "gpu_launches": launches * world,
         "clocks": gathered[0]["clocks"],
     }
+    if not args.no_batched:
+        out["prefill"], out["batched"] = batched_objects(gathered, args, world)
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(path, mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED))
     print(json.dumps(out))

@@ -118,6 +118,48 @@ int mocha_gguf_generate(mocha_gguf *m, const int *prompt, int n_prompt, int n_ne
 int mocha_gguf_bench_decode(mocha_gguf *m, int token, int pos0, int pos_end, int warmup, int steps, float *ms);
 int mocha_gguf_launches_per_step(mocha_gguf *m);
 
+/* ---- batched engine: prefill and multi-sequence decode on tensor cores ------------
+ * The batched extension of the reference ABI (gpu_forward_batch / gpu_sample_batch /
+ * gpu_prefill with an explicit device index; no reference counterpart).  A handle owns
+ * the model, bf16 hi/lo copies of every weight for the tcgen05 GEMMs, activation
+ * buffers for `max_rows` rows and the fp32 KV cache of `slots` sequences
+ * ([slot][layer][kv head][pos][64]). */
+typedef struct mocha_q8b mocha_q8b;
+
+int mocha_q8b_open(int device, const void *file, unsigned long long bytes, int max_rows, int slots, mocha_q8b **out);
+int mocha_q8b_close(mocha_q8b *h);
+
+/* One forward over n rows: row i runs tokens[i] at position pos[i] of KV slot
+ * slots[i] (keys 0..pos[i] of that slot must already hold earlier positions; rows of
+ * one slot run in increasing position order within the call).  Logits of the
+ * n_project rows listed in project_rows go to logits[n_project][151936] when non-NULL
+ * (n_project <= slots). */
+int mocha_q8b_forward(mocha_q8b *h, int n, const int *tokens, const int *pos, const int *slots, int n_project,
+                      const int *project_rows, float *logits);
+
+/* Prompt prefill of one slot: positions 0..n-1; logits of the last position. */
+int mocha_q8b_prefill(mocha_q8b *h, int slot, const int *tokens, int n, float *logits);
+
+/* The reference token loop for nseq sequences of prompt_len tokens each: n_new tokens
+ * per sequence (fewer if EOS comes first; EOS not reported), sampling as in
+ * mocha_sampling with seed seed_base + sequence index.  out_tokens[nseq][n_new],
+ * out_counts[nseq]. */
+int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, int n_new,
+                       const mocha_sampling *sampling, unsigned seed_base, int *out_tokens, int *out_counts,
+                       mocha_timing *timing);
+
+/* Device-timed prefill of an n-token seeded random prompt in slot 0 (head on the
+ * last position): warmup passes, then *ms = CUDA-event time of `steps` passes. */
+int mocha_q8b_bench_prefill(mocha_q8b *h, int n, unsigned seed, int warmup, int steps, float *ms);
+
+/* Kernels launched by one decode step of the batched loop. */
+int mocha_q8b_launches_per_step(mocha_q8b *h);
+
+/* The batched sampler alone on caller logits[n][151936]: history[n][64] with counts
+ * (penalty window), seeds[n]; writes tokens[n]. */
+int mocha_q8b_sample_check(mocha_q8b *h, int n, const float *logits, const int *history, const int *history_counts,
+                           const mocha_sampling *sampling, const unsigned *seeds, int *tokens);
+
 /* ---- tensor-core GEMM check (no reference counterpart) ----------------------------
  * y[n][rows] = x[n][cols] . dequant(q, scales)^T for one grouped-Q8 matrix (int8
  * [rows][cols] row-major, fp32 scale per 64 consecutive weights), computed by the

@@ -1,0 +1,934 @@
+// Batched grouped-Q8 engine: prompt prefill and multi-sequence decode on tcgen05
+// GEMMs (tc_gemm.cuh), with attention, norms, RoPE, KV cache and sampling on the
+// device.
+//
+// Every step processes a set of activation rows; row t carries (token, position,
+// KV slot), so one pipeline serves a 1024-token prompt (one slot, positions
+// 0..1023), the prompts of many sequences at once (rows of several slots), and one
+// decode step of a batch (one row per slot).  Per layer:
+//
+//   norm+split -> QKV GEMM (q|k|v rows fused, 1152 x 896) -> bias + RoPE + KV write
+//   -> attention over key chunks of 64 -> chunk combine + split -> O GEMM
+//   -> residual + norm + split -> gate|up GEMM (9728 x 896) -> SwiGLU + split
+//   -> down GEMM -> residual + norm (next layer, or the final norm of projected rows)
+//
+// then the tied-embedding head GEMM for the projected rows and, in the token loop,
+// the reference sampler for each projected row (penalty over the last 64 tokens,
+// control mask, top-k / temperature / top-p / xorshift32; src/minimind.cpp:160-179).
+// The math follows the reference CPU forward (src/minimind.cpp:51-82): RMSNorm
+// y = x * (1/sqrt(sum x^2/896 + 1e-6)) * g, bias after the projection, split-half RoPE
+// with the CPU's own powf/cosf/sinf tables, scores * 0.125 (applied to q, exact),
+// softmax over positions 0..pos, SwiGLU g/(1+exp(-g))*u, residual adds.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "mb_common.cuh"
+#include "mocha_b200.h"
+#include "q8_decode.cuh"
+#include "q8_layout.h"
+#include "sampling.cuh"
+#include "sampling_dev.cuh"
+#include "tc_gemm.cuh"
+
+namespace qb {
+
+using namespace q8;
+using bf16 = __nv_bfloat16;
+using mb::tc::Gemm;
+
+constexpr int QKV_ROWS = DIM + 2 * KV;  // q | k | v output rows of the fused projection
+constexpr int GU_ROWS = 2 * HIDDEN;     // gate | up
+constexpr int CHUNK = 64;               // keys per attention CTA
+constexpr int NCHUNK = CONTEXT / CHUNK;
+constexpr int PART = 2 + HEAD_DIM;      // chunk max, chunk sum, 64 weighted-V sums
+constexpr int NT = DIM / 4;             // row kernels: 4 features per thread
+constexpr int QKV_THREADS = (DIM + 2 * KV) / 2;  // one thread per RoPE pair / V pair
+constexpr int SLICE = 4096;             // sampler stage 1: ids per CTA
+constexpr int NSLICE = (VOCAB + SLICE - 1) / SLICE;
+constexpr int SAMPLE_THREADS = 1024;
+
+// KV cache: [slot][layer][kv head][position][64] fp32.
+__host__ __device__ __forceinline__ size_t kv_off(int slot, int layer, int kvh, int pos)
+{
+    return ((((size_t)slot * LAYERS + layer) * KV_HEADS + kvh) * CONTEXT + pos) * HEAD_DIM;
+}
+
+struct Rows {
+    const int *tok, *pos, *slot;
+};
+
+// ---- row kernels ----------------------------------------------------------------------
+
+// y = x * rsqrt-style scale * gain, split into a bf16 pair, written to row `dst`.
+MB_DEV void norm_store(const float (&v)[4], float *red, const float *__restrict__ gain, bf16 *hi, bf16 *lo, int dst)
+{
+    const float ss = mb::block_sum<NT>(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3], red);
+    if (dst < 0) return;
+    const float s = 1.f / sqrtf(ss / DIM + RMS_EPS);
+    const int i0 = threadIdx.x * 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float y = v[j] * s * __ldg(gain + i0 + j);
+        mb::tc::split_bf16(y, hi[(size_t)dst * DIM + i0 + j], lo[(size_t)dst * DIM + i0 + j]);
+    }
+}
+
+// x[t] = dequant(embed[tok[t]]); xn[t] = split(rms(x[t]) * gain)
+__global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const float *__restrict__ gain, float *x,
+                                                   bf16 *xh, bf16 *xl)
+{
+    __shared__ float red[32];
+    const int t = blockIdx.x, i0 = threadIdx.x * 4;
+    const int token = rows.tok[t];
+    const char4 c = *reinterpret_cast<const char4 *>(embed.w + (size_t)token * DIM + i0);
+    const float sc = embed.s[((size_t)token * DIM + i0) / GROUP];
+    const float v[4] = {c.x * sc, c.y * sc, c.z * sc, c.w * sc};
+    *reinterpret_cast<float4 *>(x + (size_t)t * DIM + i0) = make_float4(v[0], v[1], v[2], v[3]);
+    norm_store(v, red, gain, xh, xl, t);
+}
+
+// x[t] += sum_s part[s][t]; then the norm of the new x into row dst_row[t] (or t).
+__global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__restrict__ part, int splits,
+                                                      long long sstride, const float *__restrict__ gain, bf16 *hi,
+                                                      bf16 *lo, const int *__restrict__ dst_row)
+{
+    __shared__ float red[32];
+    const int t = blockIdx.x, i0 = threadIdx.x * 4;
+    float4 acc = *reinterpret_cast<const float4 *>(part + (size_t)t * DIM + i0);
+    for (int s = 1; s < splits; s++) {
+        const float4 p = *reinterpret_cast<const float4 *>(part + s * sstride + (size_t)t * DIM + i0);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+    }
+    float4 *xp = reinterpret_cast<float4 *>(x + (size_t)t * DIM + i0);
+    const float4 xv = *xp;
+    const float v[4] = {xv.x + acc.x, xv.y + acc.y, xv.z + acc.z, xv.w + acc.w};
+    *xp = make_float4(v[0], v[1], v[2], v[3]);
+    norm_store(v, red, gain, hi, lo, dst_row ? dst_row[t] : t);
+}
+
+// q/k/v = sum of partials + bias; split-half RoPE on q and k; q (times 0.125) to the
+// query buffer, k and v to the KV cache at (slot, layer, pos).
+__global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restrict__ part, int splits, long long sstride,
+                                                          const float *__restrict__ bias, Rows rows,
+                                                          const float *__restrict__ rope_cos,
+                                                          const float *__restrict__ rope_sin, float *q, float *kc,
+                                                          float *vc, int layer)
+{
+    const int t = blockIdx.x, j = threadIdx.x;
+    const int pos = rows.pos[t], slot = rows.slot[t];
+    int kind, head, i;
+    if (j < DIM / 2) {
+        kind = 0;
+        head = j / 32;
+        i = j % 32;
+    } else if (j < DIM / 2 + KV / 2) {
+        kind = 1;
+        head = (j - DIM / 2) / 32;
+        i = (j - DIM / 2) % 32;
+    } else {
+        kind = 2;
+        head = (j - DIM / 2 - KV / 2) / 32;
+        i = (j - DIM / 2 - KV / 2) % 32;
+    }
+    const int r0 = (kind == 0 ? 0 : kind == 1 ? DIM : DIM + KV) + head * HEAD_DIM + i;
+    const float *p = part + (size_t)t * QKV_ROWS;
+    float d0 = p[r0], d1 = p[r0 + 32];
+    for (int s = 1; s < splits; s++) {
+        d0 += p[s * sstride + r0];
+        d1 += p[s * sstride + r0 + 32];
+    }
+    d0 += __ldg(bias + r0);
+    d1 += __ldg(bias + r0 + 32);
+    if (kind == 2) {
+        float *v = vc + kv_off(slot, layer, head, pos);
+        v[i] = d0;
+        v[i + 32] = d1;
+        return;
+    }
+    const float cs = __ldg(rope_cos + pos * 32 + i), sn = __ldg(rope_sin + pos * 32 + i);
+    const float a = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
+    const float b = __fadd_rn(__fmul_rn(d1, cs), __fmul_rn(d0, sn));
+    if (kind == 0) {
+        q[(size_t)t * DIM + head * HEAD_DIM + i] = a * 0.125f;
+        q[(size_t)t * DIM + head * HEAD_DIM + i + 32] = b * 0.125f;
+    } else {
+        float *k = kc + kv_off(slot, layer, head, pos);
+        k[i] = a;
+        k[i + 32] = b;
+    }
+}
+
+// One KV head, one chunk of up to 64 keys, the 7 query heads that share it: chunk
+// max, sum of exp(s - max) and the exp-weighted V sums.
+__global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q, Rows rows, const float *__restrict__ kc,
+                                                    const float *__restrict__ vc, int layer, float *__restrict__ part)
+{
+    const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+    const int pos = rows.pos[t], slot = rows.slot[t];
+    const int k0 = c * CHUNK;
+    if (k0 > pos) return;
+    const int nk = min(CHUNK, pos + 1 - k0);
+    __shared__ float sq[GQA][HEAD_DIM];
+    __shared__ float sk[CHUNK][HEAD_DIM + 1];
+    __shared__ float sv[CHUNK][HEAD_DIM];
+    __shared__ float sp[GQA][CHUNK];
+    __shared__ float smax[GQA], ssum[GQA];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int idx = tid; idx < GQA * HEAD_DIM; idx += 128)
+        sq[idx / HEAD_DIM][idx % HEAD_DIM] = q[(size_t)t * DIM + g * GQA * HEAD_DIM + idx];
+    const size_t base = kv_off(slot, layer, g, k0);
+    for (int idx = tid; idx < nk * HEAD_DIM; idx += 128) {
+        sk[idx / HEAD_DIM][idx % HEAD_DIM] = kc[base + idx];
+        sv[idx / HEAD_DIM][idx % HEAD_DIM] = vc[base + idx];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < GQA * CHUNK; idx += 128) {
+        const int h = idx / CHUNK, kk = idx % CHUNK;
+        float z = -INFINITY;
+        if (kk < nk) {
+            z = 0.f;
+#pragma unroll 16
+            for (int d = 0; d < HEAD_DIM; d++) z += sq[h][d] * sk[kk][d];
+        }
+        sp[h][kk] = z;
+    }
+    __syncthreads();
+    for (int h = warp; h < GQA; h += 4) {
+        const float m = mb::warp_max(fmaxf(sp[h][lane], sp[h][lane + 32]));
+        const float e0 = lane < nk ? expf(sp[h][lane] - m) : 0.f;
+        const float e1 = lane + 32 < nk ? expf(sp[h][lane + 32] - m) : 0.f;
+        sp[h][lane] = e0;
+        sp[h][lane + 32] = e1;
+        const float s = mb::warp_sum(e0 + e1);
+        if (lane == 0) {
+            smax[h] = m;
+            ssum[h] = s;
+        }
+    }
+    __syncthreads();
+    float *out = part + ((size_t)t * HEADS + g * GQA) * NCHUNK * PART;
+    for (int idx = tid; idx < GQA * HEAD_DIM; idx += 128) {
+        const int h = idx / HEAD_DIM, d = idx % HEAD_DIM;
+        float acc = 0.f;
+        for (int kk = 0; kk < nk; kk++) acc += sp[h][kk] * sv[kk][d];
+        out[((size_t)h * NCHUNK + c) * PART + 2 + d] = acc;
+    }
+    if (tid < GQA) {
+        out[((size_t)tid * NCHUNK + c) * PART] = smax[tid];
+        out[((size_t)tid * NCHUNK + c) * PART + 1] = ssum[tid];
+    }
+}
+
+// Combine the chunks of one (row, head) into the attention output, split for the O GEMM.
+__global__ void __launch_bounds__(HEAD_DIM) k_attn_combine(const float *__restrict__ part, Rows rows, bf16 *ah, bf16 *al)
+{
+    const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+    const int nc = rows.pos[t] / CHUNK + 1;
+    const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
+    float m = -INFINITY;
+    for (int c = 0; c < nc; c++) m = fmaxf(m, p[c * PART]);
+    float l = 0.f, acc = 0.f;
+    for (int c = 0; c < nc; c++) {
+        const float w = expf(p[c * PART] - m);
+        l += p[c * PART + 1] * w;
+        acc += p[c * PART + 2 + d] * w;
+    }
+    const size_t o = (size_t)t * DIM + h * HEAD_DIM + d;
+    mb::tc::split_bf16(acc / l, ah[o], al[o]);
+}
+
+// h = silu(gate) * up from the gate|up partials, split for the down GEMM.
+__global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride, bf16 *hh,
+                                                bf16 *hl)
+{
+    const int t = blockIdx.x;
+    const float *p = part + (size_t)t * GU_ROWS;
+    for (int i = threadIdx.x; i < HIDDEN; i += 256) {
+        float g = p[i], u = p[HIDDEN + i];
+        for (int s = 1; s < splits; s++) {
+            g += p[s * sstride + i];
+            u += p[s * sstride + HIDDEN + i];
+        }
+        const float h = (g / (1.f + expf(-g))) * u;
+        mb::tc::split_bf16(h, hh[(size_t)t * HIDDEN + i], hl[(size_t)t * HIDDEN + i]);
+    }
+}
+
+// ---- batched sampler -----------------------------------------------------------------
+
+MB_DEV void bitonic_desc(unsigned long long *keys, int n)
+{
+    for (int size = 2; size <= n; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int t = threadIdx.x; t < n / 2; t += blockDim.x) {
+                const int i = 2 * t - (t & (stride - 1)), j = i + stride;
+                const unsigned long long a = keys[i], b = keys[j];
+                if (((i & size) == 0) ? (a < b) : (a > b)) {
+                    keys[i] = b;
+                    keys[j] = a;
+                }
+            }
+            __syncthreads();
+        }
+}
+
+// Stage 1: for projected row r and a slice of SLICE ids, penalty (once per distinct
+// id of the slot's history), control mask, and the slice's top k keys.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__restrict__ logits, const int *proj_src,
+                                                              Rows rows, int nslots, const sampling::SeqState *st,
+                                                              const sampling::Params *prm,
+                                                              unsigned long long *__restrict__ out)
+{
+    __shared__ unsigned long long keys[SLICE];
+    __shared__ float vals[SLICE];
+    const int r = blockIdx.y, lo = blockIdx.x * SLICE;
+    const int n = min(VOCAB - lo, SLICE);
+    const sampling::Params p = *prm;
+    const int k = min(max(p.top_k, 1), sampling::kMaxK);
+    const int slot = rows.slot[proj_src[r]];
+    if (slot < 0 || slot >= nslots) return;
+    const sampling::SeqState *s = st + slot;
+    const float *lg = logits + (size_t)r * VOCAB + lo;
+    for (int i = threadIdx.x; i < SLICE; i += SAMPLE_THREADS) vals[i] = i < n ? lg[i] : 0.f;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int count = min(max(s->history_count, 0), sampling::kHistory);
+        for (int j = threadIdx.x; j < count; j += 32) {
+            const int id = s->history[j];
+            bool dup = false;
+            for (int u = 0; u < j; u++) dup |= s->history[u] == id;
+            if (!dup && id >= lo && id < lo + n) {
+                const float v = vals[id - lo];
+                vals[id - lo] = v < 0 ? v * p.penalty : v / p.penalty;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < SLICE; i += SAMPLE_THREADS) {
+        unsigned long long key = 0ull;
+        if (i < n) {
+            const int id = lo + i;
+            const float v = (id >= p.control_first && id != p.eos) ? -1e30f : vals[i];
+            key = mb::rank_key(v, id);
+        }
+        keys[i] = key;
+    }
+    __syncthreads();
+    bitonic_desc(keys, SLICE);
+    for (int j = threadIdx.x; j < k; j += SAMPLE_THREADS)
+        out[((size_t)r * NSLICE + blockIdx.x) * sampling::kMaxK + j] = keys[j];
+}
+
+// Stage 2: merge the slices, draw the token, record it for the slot and set up the
+// slot's next decode row (next_* arrays, indexed by projected row).
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned long long *__restrict__ in,
+                                                              const int *proj_src, Rows rows, int nslots,
+                                                              sampling::SeqState *st, const sampling::Params *prm,
+                                                              int *next_tok, int *next_pos, int *next_slot,
+                                                              int *out_tokens, int *out_count, int out_stride)
+{
+    constexpr int kMerge = 4096;  // >= NSLICE * kMaxK = 2432
+    __shared__ unsigned long long keys[kMerge];
+    const int r = blockIdx.x;
+    const sampling::Params p = *prm;
+    const int k = min(max(p.top_k, 1), sampling::kMaxK);
+    const int src = proj_src[r];
+    const int slot = rows.slot[src], pos = rows.pos[src];
+    if (slot < 0 || slot >= nslots) return;
+    for (int i = threadIdx.x; i < kMerge; i += SAMPLE_THREADS) {
+        const int sl = i / k, j = i % k;
+        keys[i] = (sl < NSLICE) ? in[((size_t)r * NSLICE + sl) * sampling::kMaxK + j] : 0ull;
+    }
+    __syncthreads();
+    bitonic_desc(keys, kMerge);
+    if (threadIdx.x == 0) {
+        sampling::SeqState *s = st + slot;
+        uint32_t seed = s->seed;
+        int token = sampling::draw_token(keys, p, seed);
+        if (token < 0 || token >= VOCAB) token = p.eos;
+        if (!s->finished) {
+            s->seed = seed;
+            const int n = s->n_out;
+            if (n < out_stride) out_tokens[(size_t)slot * out_stride + n] = token;
+            s->n_out = n + 1;
+            out_count[slot] = n + 1;
+            sampling::record_token(token, p, s, nullptr, nullptr);
+        }
+        next_tok[r] = s->finished ? p.eos : token;
+        next_pos[r] = min(pos + 1, CONTEXT - 1);
+        next_slot[r] = slot;
+    }
+}
+
+// ---- engine -------------------------------------------------------------------------
+
+struct Weights {
+    bf16 *hi = nullptr, *lo = nullptr;
+};
+
+struct PlanSet {
+    Gemm qkv[LAYERS], o[LAYERS], gu[LAYERS], down[LAYERS];
+};
+
+}  // namespace qb
+
+struct mocha_q8b {
+    int device = 0, max_rows = 0, slots = 0;
+    cudaStream_t stream = nullptr;
+    unsigned char *d_file = nullptr;
+    q8::Model m{};
+    qb::Weights w_qkv[q8::LAYERS], w_o[q8::LAYERS], w_gu[q8::LAYERS], w_down[q8::LAYERS], w_head;
+    float *bqkv = nullptr;  // [LAYERS][1152]
+    float *x = nullptr, *q = nullptr, *part = nullptr, *apart = nullptr, *logits = nullptr;
+    __nv_bfloat16 *xh = nullptr, *xl = nullptr, *ah = nullptr, *al = nullptr, *hh = nullptr, *hl = nullptr;
+    __nv_bfloat16 *headh = nullptr, *headl = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    int *tok = nullptr, *pos = nullptr, *slot = nullptr;            // prompt rows [max_rows]
+    int *ntok = nullptr, *npos = nullptr, *nslot = nullptr;         // decode rows [slots]
+    int *proj_src = nullptr, *proj_dst = nullptr, *ident = nullptr;  // [slots], [max_rows], [slots]
+    int *err = nullptr;
+    unsigned long long *keys = nullptr;
+    sampling::SeqState *st = nullptr;
+    sampling::Params *params = nullptr;
+    int *out_tokens = nullptr, *out_count = nullptr;
+    int out_stride = 0;
+    qb::PlanSet pre, dec;
+    mb::tc::Gemm head;
+    cudaGraphExec_t g_step = nullptr;
+    int g_step_n = 0;
+    cudaEvent_t ev[4] = {};
+    size_t part_floats = 0;
+};
+
+namespace qb {
+namespace {
+
+#define QB_TRY(x) MB_CHECK(x)
+
+int check_err(mocha_q8b *h)
+{
+    int e = 0;
+    QB_TRY(cudaMemcpy(&e, h->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        fprintf(stderr, "mocha_q8b: device-side wait gave up (code %d)\n", e);
+        return 1;
+    }
+    return 0;
+}
+
+template <class T>
+int dalloc(T **p, size_t count)
+{
+    QB_TRY(cudaMalloc((void **)p, sizeof(T) * count + 256));
+    return 0;
+}
+
+int alloc_pair(Weights &w, size_t count)
+{
+    if (dalloc(&w.hi, count) || dalloc(&w.lo, count)) return 1;
+    return 0;
+}
+
+// Split rows [0, rows) of a grouped-Q8 matrix into rows [row0, row0+rows) of a pair.
+int split_into(mocha_q8b *h, const Mat &m, size_t rows, size_t cols, Weights &w, size_t row0)
+{
+    return mb::tc::split_weights(m.w, m.s, rows * cols, w.hi + row0 * cols, w.lo + row0 * cols, h->stream);
+}
+
+int plan_set(mocha_q8b *h, PlanSet &ps, int n_max)
+{
+    for (int l = 0; l < LAYERS; l++) {
+        if (mb::tc::gemm_plan(&ps.qkv[l], h->w_qkv[l].hi, h->w_qkv[l].lo, QKV_ROWS, DIM, h->xh, h->xl, n_max, h->part,
+                              QKV_ROWS, 0, h->err) ||
+            mb::tc::gemm_plan(&ps.o[l], h->w_o[l].hi, h->w_o[l].lo, DIM, DIM, h->ah, h->al, n_max, h->part, DIM, 0,
+                              h->err) ||
+            mb::tc::gemm_plan(&ps.gu[l], h->w_gu[l].hi, h->w_gu[l].lo, GU_ROWS, DIM, h->xh, h->xl, n_max, h->part,
+                              GU_ROWS, 0, h->err) ||
+            mb::tc::gemm_plan(&ps.down[l], h->w_down[l].hi, h->w_down[l].lo, DIM, HIDDEN, h->hh, h->hl, n_max,
+                              h->part, DIM, 0, h->err))
+            return 1;
+    }
+    return 0;
+}
+
+size_t plan_floats(const PlanSet &ps)
+{
+    size_t m = 0;
+    for (int l = 0; l < LAYERS; l++) {
+        const Gemm *g[4] = {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]};
+        for (const Gemm *x : g) m = std::max(m, (size_t)x->splits * (size_t)x->p.split_stride);
+    }
+    return m;
+}
+
+// The whole transformer for rows [0, n) plus the head for `np` projected rows
+// (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of headh/headl).
+int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np)
+{
+    const PlanSet &ps = decode_set ? h->dec : h->pre;
+    cudaStream_t s = h->stream;
+    k_embed_norm<<<n, NT, 0, s>>>(h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->xh, h->xl);
+    for (int l = 0; l < LAYERS; l++) {
+        const Layer &L = h->m.layer[l];
+        if (mb::tc::gemm_launch(ps.qkv[l], n, s)) return 1;
+        k_qkv_post<<<n, QKV_THREADS, 0, s>>>(h->part, ps.qkv[l].splits, ps.qkv[l].p.split_stride,
+                                              h->bqkv + (size_t)l * QKV_ROWS, rows, h->rope_cos, h->rope_sin, h->q,
+                                              h->kc, h->vc, l);
+        k_attn_chunk<<<dim3(NCHUNK, KV_HEADS, n), 128, 0, s>>>(h->q, rows, h->kc, h->vc, l, h->apart);
+        k_attn_combine<<<dim3(HEADS, n), HEAD_DIM, 0, s>>>(h->apart, rows, h->ah, h->al);
+        if (mb::tc::gemm_launch(ps.o[l], n, s)) return 1;
+        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, ps.o[l].splits, ps.o[l].p.split_stride, L.ffn_norm, h->xh,
+                                          h->xl, nullptr);
+        if (mb::tc::gemm_launch(ps.gu[l], n, s)) return 1;
+        k_swiglu<<<n, 256, 0, s>>>(h->part, ps.gu[l].splits, ps.gu[l].p.split_stride, h->hh, h->hl);
+        if (mb::tc::gemm_launch(ps.down[l], n, s)) return 1;
+        const bool last = l + 1 == LAYERS;
+        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, ps.down[l].splits, ps.down[l].p.split_stride,
+                                          last ? h->m.final_norm : h->m.layer[l + 1].attn_norm,
+                                          last ? h->headh : h->xh, last ? h->headl : h->xl,
+                                          last ? proj_dst : nullptr);
+    }
+    if (np > 0 && mb::tc::gemm_launch(h->head, np, s)) return 1;
+    QB_TRY(cudaGetLastError());
+    return 0;
+}
+
+// Sampling for projected rows 0..np-1; proj_src[r] is the activation row of
+// projected row r (the identity map in decode steps).
+int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src)
+{
+    k_bs_stage1<<<dim3(NSLICE, np), SAMPLE_THREADS, 0, h->stream>>>(h->logits, proj_src, rows, h->slots, h->st,
+                                                                   h->params, h->keys);
+    k_bs_stage2<<<np, SAMPLE_THREADS, 0, h->stream>>>(h->keys, proj_src, rows, h->slots, h->st, h->params, h->ntok,
+                                                      h->npos, h->nslot, h->out_tokens, h->out_count, h->out_stride);
+    QB_TRY(cudaGetLastError());
+    return 0;
+}
+
+int upload_rows(mocha_q8b *h, int n, const int *tokens, const int *pos, const int *slots)
+{
+    QB_TRY(cudaMemcpyAsync(h->tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->pos, pos, sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->slot, slots, sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    return 0;
+}
+
+bool rows_valid(mocha_q8b *h, int n, const int *tokens, const int *pos, const int *slots)
+{
+    if (n <= 0 || n > h->max_rows || !tokens || !pos || !slots) return false;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= VOCAB || pos[i] < 0 || pos[i] >= CONTEXT || slots[i] < 0 ||
+            slots[i] >= h->slots)
+            return false;
+    return true;
+}
+
+// Set the projected rows: proj_src[r] = row, proj_dst[row] = r (others -1).
+int set_projection(mocha_q8b *h, int n, int np, const int *src)
+{
+    std::vector<int> dst(n, -1);
+    for (int r = 0; r < np; r++) dst[src[r]] = r;
+    QB_TRY(cudaMemcpyAsync(h->proj_src, src, sizeof(int) * np, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->proj_dst, dst.data(), sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaStreamSynchronize(h->stream));  // dst is a stack vector
+    return 0;
+}
+
+int capture_step(mocha_q8b *h, int n)
+{
+    if (h->g_step && h->g_step_n == n) return 0;
+    if (h->g_step) {
+        cudaGraphExecDestroy(h->g_step);
+        h->g_step = nullptr;
+    }
+    cudaGraph_t g;
+    QB_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    const Rows r{h->ntok, h->npos, h->nslot};
+    int rc = enqueue_forward(h, r, n, true, h->ident, n);
+    if (!rc) rc = enqueue_sample(h, r, n, h->ident);
+    const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
+    if (rc || e != cudaSuccess) {
+        fprintf(stderr, "mocha_q8b: step capture failed\n");
+        return 1;
+    }
+    QB_TRY(cudaGraphInstantiate(&h->g_step, g, 0));
+    cudaGraphDestroy(g);
+    h->g_step_n = n;
+    return 0;
+}
+
+}  // namespace
+}  // namespace qb
+
+using namespace qb;
+
+extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long bytes, int max_rows, int slots,
+                              mocha_q8b **out)
+{
+    if (!out || !q8::valid_file(file, (size_t)bytes, false) || max_rows < 1 || max_rows > 16384 || slots < 1 ||
+        slots > 256) {
+        fprintf(stderr, "mocha_q8b_open: bad arguments or not a Qwen2.5-0.5B grouped-Q8 file\n");
+        return 1;
+    }
+    *out = nullptr;
+    int ndev = 0;
+    QB_TRY(cudaGetDeviceCount(&ndev));
+    cudaDeviceProp prop;
+    if (device < 0 || device >= ndev || cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+        fprintf(stderr, "mocha_q8b_open: device %d is not a compute capability 10.x GPU\n", device);
+        return 1;
+    }
+    QB_TRY(cudaSetDevice(device));
+    mocha_q8b *h = new mocha_q8b();
+    h->device = device;
+    h->max_rows = max_rows;
+    h->slots = slots;
+    auto fail = [&]() {
+        mocha_q8b_close(h);
+        return 1;
+    };
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return fail();
+    if (dalloc(&h->d_file, bytes)) return fail();
+    if (cudaMemcpy(h->d_file, file, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return fail();
+    const q8::FileHeader *hd = (const q8::FileHeader *)file;
+    auto mat = [&](const q8::FileTensor &t) {
+        return q8::Mat{(const int8_t *)(h->d_file + t.data), (const float *)(h->d_file + t.scales)};
+    };
+    h->m.embed = mat(hd->t[0]);
+    h->m.final_norm = (const float *)(h->d_file + hd->t[q8::TENSORS - 1].data);
+    std::vector<float> bias((size_t)LAYERS * QKV_ROWS);
+    for (int l = 0; l < LAYERS; l++) {
+        const q8::FileTensor *t = hd->t + 1 + l * q8::STRIDE;
+        q8::Layer &L = h->m.layer[l];
+        L.attn_norm = (const float *)(h->d_file + t[q8::ATTN_NORM].data);
+        L.ffn_norm = (const float *)(h->d_file + t[q8::FFN_NORM].data);
+        L.q = mat(t[q8::WQ]);
+        L.k = mat(t[q8::WK]);
+        L.v = mat(t[q8::WV]);
+        L.o = mat(t[q8::WO]);
+        L.gate = mat(t[q8::WGATE]);
+        L.up = mat(t[q8::WUP]);
+        L.down = mat(t[q8::WDOWN]);
+        const unsigned char *fb = (const unsigned char *)file;
+        memcpy(&bias[(size_t)l * QKV_ROWS], fb + t[q8::BQ].data, sizeof(float) * DIM);
+        memcpy(&bias[(size_t)l * QKV_ROWS + DIM], fb + t[q8::BK].data, sizeof(float) * KV);
+        memcpy(&bias[(size_t)l * QKV_ROWS + DIM + KV], fb + t[q8::BV].data, sizeof(float) * KV);
+    }
+    if (dalloc(&h->bqkv, bias.size())) return fail();
+    if (cudaMemcpy(h->bqkv, bias.data(), sizeof(float) * bias.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail();
+
+    // bf16 pairs of the weights, q|k|v and gate|up fused along the output rows
+    for (int l = 0; l < LAYERS; l++) {
+        const q8::Layer &L = h->m.layer[l];
+        if (alloc_pair(h->w_qkv[l], (size_t)QKV_ROWS * DIM) || alloc_pair(h->w_o[l], (size_t)DIM * DIM) ||
+            alloc_pair(h->w_gu[l], (size_t)GU_ROWS * DIM) || alloc_pair(h->w_down[l], (size_t)DIM * HIDDEN))
+            return fail();
+        if (split_into(h, L.q, DIM, DIM, h->w_qkv[l], 0) || split_into(h, L.k, KV, DIM, h->w_qkv[l], DIM) ||
+            split_into(h, L.v, KV, DIM, h->w_qkv[l], DIM + KV) || split_into(h, L.o, DIM, DIM, h->w_o[l], 0) ||
+            split_into(h, L.gate, HIDDEN, DIM, h->w_gu[l], 0) || split_into(h, L.up, HIDDEN, DIM, h->w_gu[l], HIDDEN) ||
+            split_into(h, L.down, DIM, HIDDEN, h->w_down[l], 0))
+            return fail();
+    }
+    if (alloc_pair(h->w_head, (size_t)VOCAB * DIM) || split_into(h, h->m.embed, VOCAB, DIM, h->w_head, 0))
+        return fail();
+
+    // activations
+    const size_t R = (size_t)max_rows;
+    if (dalloc(&h->x, R * DIM) || dalloc(&h->q, R * DIM) || dalloc(&h->xh, R * DIM) || dalloc(&h->xl, R * DIM) ||
+        dalloc(&h->ah, R * DIM) || dalloc(&h->al, R * DIM) || dalloc(&h->hh, R * HIDDEN) ||
+        dalloc(&h->hl, R * HIDDEN) || dalloc(&h->apart, R * HEADS * NCHUNK * PART) ||
+        dalloc(&h->headh, (size_t)slots * DIM) || dalloc(&h->headl, (size_t)slots * DIM) ||
+        dalloc(&h->logits, (size_t)slots * VOCAB) || dalloc(&h->tok, R) || dalloc(&h->pos, R) ||
+        dalloc(&h->slot, R) || dalloc(&h->ntok, slots) || dalloc(&h->npos, slots) || dalloc(&h->nslot, slots) ||
+        dalloc(&h->proj_src, slots) || dalloc(&h->proj_dst, R) || dalloc(&h->ident, slots) || dalloc(&h->err, 1) ||
+        dalloc(&h->keys, (size_t)slots * NSLICE * sampling::kMaxK) || dalloc(&h->st, slots) ||
+        dalloc(&h->params, 1) || dalloc(&h->out_count, slots))
+        return fail();
+    const size_t kv = kv_off(slots, 0, 0, 0);
+    if (dalloc(&h->kc, kv) || dalloc(&h->vc, kv)) return fail();
+    if (cudaMemset(h->kc, 0, sizeof(float) * kv) || cudaMemset(h->vc, 0, sizeof(float) * kv) ||
+        cudaMemset(h->err, 0, sizeof(int)) || cudaMemset(h->out_count, 0, sizeof(int) * slots) ||
+        cudaMemset(h->st, 0, sizeof(sampling::SeqState) * slots))
+        return fail();
+    {
+        std::vector<int> id(slots);
+        for (int i = 0; i < slots; i++) id[i] = i;
+        if (cudaMemcpy(h->ident, id.data(), sizeof(int) * slots, cudaMemcpyHostToDevice) != cudaSuccess) return fail();
+    }
+    std::vector<float> rc((size_t)CONTEXT * 32), rs((size_t)CONTEXT * 32);
+    q8::fill_rope_tables(rc.data(), rs.data(), CONTEXT, 32, 1000000.f);
+    if (dalloc(&h->rope_cos, rc.size()) || dalloc(&h->rope_sin, rs.size())) return fail();
+    if (cudaMemcpy(h->rope_cos, rc.data(), sizeof(float) * rc.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(h->rope_sin, rs.data(), sizeof(float) * rs.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail();
+
+    // GEMM call sites; the partial buffer is sized from the plans' split counts
+    if (plan_set(h, h->pre, max_rows) || plan_set(h, h->dec, slots)) return fail();
+    if (mb::tc::gemm_plan(&h->head, h->w_head.hi, h->w_head.lo, VOCAB, DIM, h->headh, h->headl, slots, h->logits,
+                          VOCAB, 1, h->err))
+        return fail();
+    h->part_floats = std::max(plan_floats(h->pre), plan_floats(h->dec));
+    if (dalloc(&h->part, h->part_floats)) return fail();
+    for (int l = 0; l < LAYERS; l++)
+        for (PlanSet *ps : {&h->pre, &h->dec}) {
+            ps->qkv[l].p.d = h->part;
+            ps->o[l].p.d = h->part;
+            ps->gu[l].p.d = h->part;
+            ps->down[l].p.d = h->part;
+        }
+    for (int i = 0; i < 4; i++)
+        if (cudaEventCreate(&h->ev[i]) != cudaSuccess) return fail();
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) return fail();
+    *out = h;
+    return 0;
+}
+
+extern "C" int mocha_q8b_close(mocha_q8b *h)
+{
+    if (!h) return 1;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->g_step) cudaGraphExecDestroy(h->g_step);
+    void *ptrs[] = {h->d_file, h->bqkv, h->x, h->q, h->part, h->apart, h->logits, h->xh, h->xl, h->ah, h->al, h->hh,
+                    h->hl, h->headh, h->headl, h->kc, h->vc, h->rope_cos, h->rope_sin, h->tok, h->pos, h->slot,
+                    h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->err, h->keys, h->st,
+                    h->params, h->out_tokens, h->out_count, h->w_head.hi, h->w_head.lo};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    for (int l = 0; l < LAYERS; l++)
+        for (Weights *w : {&h->w_qkv[l], &h->w_o[l], &h->w_gu[l], &h->w_down[l]}) {
+            if (w->hi) cudaFree(w->hi);
+            if (w->lo) cudaFree(w->lo);
+        }
+    for (cudaEvent_t e : h->ev)
+        if (e) cudaEventDestroy(e);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+    return 0;
+}
+
+extern "C" int mocha_q8b_forward(mocha_q8b *h, int n, const int *tokens, const int *pos, const int *slots,
+                                 int n_project, const int *project_rows, float *logits)
+{
+    if (!h || !rows_valid(h, n, tokens, pos, slots) || n_project < 0 || n_project > h->slots ||
+        (n_project && !project_rows)) {
+        fprintf(stderr, "mocha_q8b_forward: bad arguments\n");
+        return 1;
+    }
+    for (int r = 0; r < n_project; r++)
+        if (project_rows[r] < 0 || project_rows[r] >= n) {
+            fprintf(stderr, "mocha_q8b_forward: projected row out of range\n");
+            return 1;
+        }
+    QB_TRY(cudaSetDevice(h->device));
+    if (upload_rows(h, n, tokens, pos, slots) || set_projection(h, n, n_project, project_rows)) return 1;
+    const Rows r{h->tok, h->pos, h->slot};
+    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project)) return 1;
+    if (logits && n_project)
+        QB_TRY(cudaMemcpyAsync(logits, h->logits, sizeof(float) * VOCAB * n_project, cudaMemcpyDeviceToHost,
+                               h->stream));
+    QB_TRY(cudaStreamSynchronize(h->stream));
+    return check_err(h);
+}
+
+extern "C" int mocha_q8b_prefill(mocha_q8b *h, int slot, const int *tokens, int n, float *logits)
+{
+    if (!h || slot < 0 || slot >= h->slots || !tokens || n < 1 || n > CONTEXT || n > h->max_rows) {
+        fprintf(stderr, "mocha_q8b_prefill: bad arguments\n");
+        return 1;
+    }
+    std::vector<int> pos(n), sl(n, slot);
+    for (int i = 0; i < n; i++) pos[i] = i;
+    const int last = n - 1;
+    return mocha_q8b_forward(h, n, tokens, pos.data(), sl.data(), 1, &last, logits);
+}
+
+// The reference token loop for many sequences: sequences are served `slots` at a
+// time; each wave prefills its prompts in one pass (rows of all its slots), samples
+// the first token from the last prompt position, then runs n_new - 1 decode steps as
+// one CUDA graph per step with tokens and positions kept on the device.
+extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, int n_new,
+                                  const mocha_sampling *sp, unsigned seed_base, int *out_tokens, int *out_counts,
+                                  mocha_timing *timing)
+{
+    if (!h || nseq < 1 || !prompts || prompt_len < 1 || n_new < 1 || prompt_len + n_new > CONTEXT || !sp ||
+        !out_tokens || !out_counts || sp->top_k < 1 || sp->top_k > sampling::kMaxK || !(sp->top_p > 0.f) ||
+        sp->top_p > 1.f || sp->temperature < 0.f || sp->repeat_penalty < 1.f) {
+        fprintf(stderr, "mocha_q8b_generate: bad arguments\n");
+        return 1;
+    }
+    QB_TRY(cudaSetDevice(h->device));
+    const int wave = std::min(h->slots, std::max(1, h->max_rows / prompt_len));
+    if (wave < 1) return 1;
+    if (h->out_stride < n_new) {
+        if (h->out_tokens) cudaFree(h->out_tokens);
+        h->out_tokens = nullptr;
+        if (dalloc(&h->out_tokens, (size_t)h->slots * n_new)) return 1;
+        h->out_stride = n_new;
+    }
+    for (int i = 0; i < nseq; i++)
+        for (int j = 0; j < prompt_len; j++)
+            if (prompts[(size_t)i * prompt_len + j] < 0 || prompts[(size_t)i * prompt_len + j] >= VOCAB) {
+                fprintf(stderr, "mocha_q8b_generate: token id out of range\n");
+                return 1;
+            }
+    sampling::Params prm{sp->repeat_penalty, sp->temperature, sp->top_k, sp->top_p, EOS, CONTROL_FIRST, VOCAB};
+    QB_TRY(cudaMemcpyAsync(h->params, &prm, sizeof(prm), cudaMemcpyHostToDevice, h->stream));
+    double prefill_s = 0, decode_s = 0;
+    int generated = 0;
+    std::vector<int> tok, pos, sl, src, counts(h->slots);
+    std::vector<sampling::SeqState> st(h->slots);
+    for (int s0 = 0; s0 < nseq; s0 += wave) {
+        const int b = std::min(wave, nseq - s0);
+        // sampler state: the last 64 prompt tokens, seed base + sequence index
+        for (int i = 0; i < b; i++) {
+            sampling::SeqState &x = st[i];
+            memset(&x, 0, sizeof x);
+            const int *p = prompts + (size_t)(s0 + i) * prompt_len;
+            const int from = std::max(0, prompt_len - sampling::kHistory);
+            for (int j = from; j < prompt_len; j++) x.history[x.history_count++] = p[j];
+            x.history_head = x.history_count % sampling::kHistory;
+            x.seed = seed_base + (unsigned)(s0 + i);
+            x.last_token = p[prompt_len - 1];
+        }
+        QB_TRY(cudaMemcpyAsync(h->st, st.data(), sizeof(sampling::SeqState) * b, cudaMemcpyHostToDevice, h->stream));
+        QB_TRY(cudaMemsetAsync(h->out_count, 0, sizeof(int) * h->slots, h->stream));
+        tok.resize((size_t)b * prompt_len);
+        pos.resize(tok.size());
+        sl.resize(tok.size());
+        src.resize(b);
+        for (int i = 0; i < b; i++) {
+            for (int j = 0; j < prompt_len; j++) {
+                tok[(size_t)i * prompt_len + j] = prompts[(size_t)(s0 + i) * prompt_len + j];
+                pos[(size_t)i * prompt_len + j] = j;
+                sl[(size_t)i * prompt_len + j] = i;
+            }
+            src[i] = i * prompt_len + prompt_len - 1;
+        }
+        const int n = b * prompt_len;
+        if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, b, src.data())) return 1;
+        QB_TRY(cudaEventRecord(h->ev[0], h->stream));
+        const Rows pr{h->tok, h->pos, h->slot};
+        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b) || enqueue_sample(h, pr, b, h->proj_src)) return 1;
+        QB_TRY(cudaEventRecord(h->ev[1], h->stream));
+        if (n_new > 1 && capture_step(h, b)) return 1;
+        for (int step = 1; step < n_new; step++) QB_TRY(cudaGraphLaunch(h->g_step, h->stream));
+        QB_TRY(cudaEventRecord(h->ev[2], h->stream));
+        QB_TRY(cudaEventSynchronize(h->ev[2]));
+        if (check_err(h)) return 1;
+        float a = 0, c = 0;
+        QB_TRY(cudaEventElapsedTime(&a, h->ev[0], h->ev[1]));
+        QB_TRY(cudaEventElapsedTime(&c, h->ev[1], h->ev[2]));
+        prefill_s += a * 1e-3;
+        decode_s += c * 1e-3;
+        QB_TRY(cudaMemcpy(counts.data(), h->out_count, sizeof(int) * b, cudaMemcpyDeviceToHost));
+        for (int i = 0; i < b; i++) {
+            // tokens before EOS; EOS itself is not reported
+            int cnt = std::min(counts[i], n_new);
+            std::vector<int> row(n_new);
+            QB_TRY(cudaMemcpy(row.data(), h->out_tokens + (size_t)i * h->out_stride, sizeof(int) * n_new,
+                              cudaMemcpyDeviceToHost));
+            int kept = 0;
+            while (kept < cnt && row[kept] != EOS) kept++;
+            memcpy(out_tokens + (size_t)(s0 + i) * n_new, row.data(), sizeof(int) * kept);
+            out_counts[s0 + i] = kept;
+            generated += kept;
+        }
+    }
+    if (timing) {
+        timing->prefill_s = prefill_s;
+        timing->decode_s = decode_s;
+        timing->generated = generated;
+    }
+    return 0;
+}
+
+extern "C" int mocha_q8b_launches_per_step(mocha_q8b *h)
+{
+    if (!h) return -1;
+    return 1 + LAYERS * 10 + 1 + 2;  // embed+norm, 10 per layer, head GEMM, two sampler kernels
+}
+
+// Sampler check: the batched sampler on caller-supplied logits (n rows of VOCAB) with
+// per-row history (64 ids each, counts) and seeds; writes the drawn tokens.
+extern "C" int mocha_q8b_sample_check(mocha_q8b *h, int n, const float *logits, const int *history,
+                                      const int *history_counts, const mocha_sampling *sp, const unsigned *seeds,
+                                      int *tokens)
+{
+    if (!h || n < 1 || n > h->slots || !logits || !history || !history_counts || !sp || !seeds || !tokens ||
+        sp->top_k < 1 || sp->top_k > sampling::kMaxK) {
+        fprintf(stderr, "mocha_q8b_sample_check: bad arguments\n");
+        return 1;
+    }
+    QB_TRY(cudaSetDevice(h->device));
+    sampling::Params prm{sp->repeat_penalty, sp->temperature, sp->top_k, sp->top_p, EOS, CONTROL_FIRST, VOCAB};
+    std::vector<sampling::SeqState> st(n);
+    std::vector<int> rows(n), pos(n, 0);
+    for (int i = 0; i < n; i++) {
+        memset(&st[i], 0, sizeof st[i]);
+        const int c = std::min(std::max(history_counts[i], 0), sampling::kHistory);
+        for (int j = 0; j < c; j++) st[i].history[j] = history[(size_t)i * sampling::kHistory + j];
+        st[i].history_count = c;
+        st[i].history_head = c % sampling::kHistory;
+        st[i].seed = seeds[i];
+        rows[i] = i;
+    }
+    if (h->out_stride < 1) {
+        if (dalloc(&h->out_tokens, (size_t)h->slots)) return 1;
+        h->out_stride = 1;
+    }
+    QB_TRY(cudaMemcpyAsync(h->params, &prm, sizeof(prm), cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->st, st.data(), sizeof(sampling::SeqState) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->logits, logits, sizeof(float) * VOCAB * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->slot, rows.data(), sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->pos, pos.data(), sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    QB_TRY(cudaMemcpyAsync(h->proj_src, rows.data(), sizeof(int) * n, cudaMemcpyHostToDevice, h->stream));
+    const Rows r{h->tok, h->pos, h->slot};
+    if (enqueue_sample(h, r, n, h->proj_src)) return 1;
+    QB_TRY(cudaMemcpyAsync(tokens, h->ntok, sizeof(int) * n, cudaMemcpyDeviceToHost, h->stream));
+    QB_TRY(cudaStreamSynchronize(h->stream));
+    return 0;
+}
+
+// Device-timed prefill: `steps` passes (after `warmup`) of an n-token prompt of
+// seeded random ids in slot 0 with the head on the last position; *ms = CUDA-event
+// time of the timed passes.
+extern "C" int mocha_q8b_bench_prefill(mocha_q8b *h, int n, unsigned seed, int warmup, int steps, float *ms)
+{
+    if (!h || n < 1 || n > CONTEXT || n > h->max_rows || warmup < 0 || steps < 1 || !ms) {
+        fprintf(stderr, "mocha_q8b_bench_prefill: bad arguments\n");
+        return 1;
+    }
+    QB_TRY(cudaSetDevice(h->device));
+    std::vector<int> tok(n), pos(n), sl(n, 0);
+    uint32_t s = seed ? seed : 1u;
+    for (int i = 0; i < n; i++) {
+        s ^= s << 13;
+        s ^= s >> 17;
+        s ^= s << 5;
+        tok[i] = (int)(s % (uint32_t)VOCAB);
+        pos[i] = i;
+    }
+    const int last = n - 1;
+    if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, 1, &last)) return 1;
+    const Rows r{h->tok, h->pos, h->slot};
+    for (int i = 0; i < warmup; i++)
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1)) return 1;
+    QB_TRY(cudaEventRecord(h->ev[0], h->stream));
+    for (int i = 0; i < steps; i++)
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1)) return 1;
+    QB_TRY(cudaEventRecord(h->ev[1], h->stream));
+    QB_TRY(cudaEventSynchronize(h->ev[1]));
+    QB_TRY(cudaEventElapsedTime(ms, h->ev[0], h->ev[1]));
+    return check_err(h);
+}

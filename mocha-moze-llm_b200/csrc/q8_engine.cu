@@ -46,6 +46,10 @@ __global__ void k_count_step(q8::DecodeState *st)
     if (threadIdx.x == 0 && blockIdx.x == 0) st->steps++;
 }
 
+}  // namespace
+
+namespace q8 {
+
 // Header and tensor-table checks of src/minimind.cpp:89-93, plus the 16-byte
 // alignment the vector loads need.
 bool valid_file(const void *file, size_t bytes, bool head_only)
@@ -67,7 +71,7 @@ bool valid_file(const void *file, size_t bytes, bool head_only)
     return true;
 }
 
-}  // namespace
+}  // namespace q8
 
 struct mocha_q8 {
     int device = 0;
@@ -407,7 +411,7 @@ int env_device()
 
 extern "C" int gpu_init(const void *file, unsigned bytes)
 {
-    if (g_engine || !valid_file(file, bytes, false)) {
+    if (g_engine || !q8::valid_file(file, bytes, false)) {
         fprintf(stderr, "MOCHA_B200: gpu_init: invalid grouped-Q8 file or already initialised\n");
         return 1;
     }
@@ -548,7 +552,7 @@ extern "C" int mocha_b200_device_count(void)
 
 extern "C" int mocha_q8_open(int device, const void *file, unsigned long long bytes, mocha_q8 **out)
 {
-    if (!out || !valid_file(file, (size_t)bytes, false)) {
+    if (!out || !q8::valid_file(file, (size_t)bytes, false)) {
         fprintf(stderr, "MOCHA_B200: mocha_q8_open: invalid grouped-Q8 file\n");
         return 1;
     }

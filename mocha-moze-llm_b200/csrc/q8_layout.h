@@ -2,6 +2,7 @@
 // Shapes and tensor order are the reference's (src/minimind.h:6-9 with MOCHA_QWEN,
 // tools/convert-qwen.py:46-55); everything else is this library's own layout.
 #pragma once
+#include <stddef.h>
 #include <stdint.h>
 
 namespace q8 {
@@ -42,6 +43,10 @@ struct Model {
     const float *final_norm;
     Layer layer[LAYERS];
 };
+
+// Header and tensor-table checks of the reference loader plus 16-byte alignment of
+// every tensor (head_only: only the embedding needs to be present).
+bool valid_file(const void *file, size_t bytes, bool head_only);
 
 // Split-K attention: positions are processed in chunks of ATTN_CHUNK per CTA.
 constexpr int ATTN_CHUNK = 32;

@@ -72,6 +72,17 @@ _SIGS = {
                                           C.POINTER(C.c_float)]),
     "mocha_gguf_launches_per_step": (C.c_int, [C.c_void_p]),
     "mocha_q8_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
+    "mocha_q8b_open": (C.c_int, [C.c_int, C.c_void_p, C.c_ulonglong, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "mocha_q8b_close": (C.c_int, [C.c_void_p]),
+    "mocha_q8b_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                    C.c_void_p]),
+    "mocha_q8b_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
+    "mocha_q8b_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(MochaSampling),
+                                     C.c_uint, C.c_void_p, C.c_void_p, C.POINTER(MochaTiming)]),
+    "mocha_q8b_launches_per_step": (C.c_int, [C.c_void_p]),
+    "mocha_q8b_bench_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_uint, C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "mocha_q8b_sample_check": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.POINTER(MochaSampling), C.c_void_p, C.c_void_p]),
     "mocha_tc_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
 }
@@ -226,3 +237,93 @@ def _addr(buf):
     import numpy as np
     arr = np.frombuffer(buf, dtype=np.uint8) if not isinstance(buf, np.ndarray) else buf
     return arr.ctypes.data, arr.nbytes
+
+
+class Q8BatchHandle:
+    """The batched grouped-Q8 engine on one device (mocha_q8b handle): tcgen05 GEMMs
+    over rows of (token, position, KV slot)."""
+
+    VOCAB = 151936
+
+    def __init__(self, device: int, file_bytes, max_rows: int = 1024, slots: int = 64, lib: C.CDLL | None = None):
+        import numpy as np
+        self.lib = lib or load()
+        self._file = np.ascontiguousarray(file_bytes, dtype=np.uint8)
+        h = C.c_void_p()
+        if self.lib.mocha_q8b_open(device, self._file.ctypes.data, self._file.nbytes, max_rows, slots, C.byref(h)):
+            raise RuntimeError("mocha_q8b_open failed")
+        self.h = h
+        self.slots = slots
+        self.max_rows = max_rows
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.mocha_q8b_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, tokens, pos, slots, project_rows=()):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(pos, dtype=np.int32)
+        s = np.ascontiguousarray(slots, dtype=np.int32)
+        pr = np.ascontiguousarray(project_rows, dtype=np.int32)
+        out = np.empty((len(pr), self.VOCAB), np.float32)
+        rc = self.lib.mocha_q8b_forward(self.h, len(t), t.ctypes.data, p.ctypes.data, s.ctypes.data, len(pr),
+                                        pr.ctypes.data if len(pr) else None, out.ctypes.data if len(pr) else None)
+        if rc:
+            raise RuntimeError("mocha_q8b_forward failed")
+        return out
+
+    def prefill(self, slot, tokens):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.VOCAB, np.float32)
+        if self.lib.mocha_q8b_prefill(self.h, slot, t.ctypes.data, len(t), out.ctypes.data):
+            raise RuntimeError("mocha_q8b_prefill failed")
+        return out
+
+    def generate(self, prompts, n_new, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0, seed_base=42):
+        import numpy as np
+        pr = np.ascontiguousarray(prompts, dtype=np.int32)
+        nseq, plen = pr.shape
+        out = np.zeros((nseq, n_new), np.int32)
+        counts = np.zeros(nseq, np.int32)
+        s = MochaSampling(temperature, top_k, top_p, penalty, 0)
+        t = MochaTiming()
+        if self.lib.mocha_q8b_generate(self.h, nseq, pr.ctypes.data, plen, n_new, C.byref(s), seed_base,
+                                       out.ctypes.data, counts.ctypes.data, C.byref(t)):
+            raise RuntimeError("mocha_q8b_generate failed")
+        return [out[i, :counts[i]].tolist() for i in range(nseq)], t
+
+    def bench_prefill(self, n, seed, warmup, steps) -> float:
+        ms = C.c_float()
+        if self.lib.mocha_q8b_bench_prefill(self.h, n, seed, warmup, steps, C.byref(ms)):
+            raise RuntimeError("mocha_q8b_bench_prefill failed")
+        return ms.value
+
+    def launches_per_step(self) -> int:
+        return self.lib.mocha_q8b_launches_per_step(self.h)
+
+    def sample(self, logits, histories, temperature, top_k, top_p, penalty, seeds):
+        import numpy as np
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        n = lg.shape[0]
+        hist = np.zeros((n, 64), np.int32)
+        counts = np.zeros(n, np.int32)
+        for i, h in enumerate(histories):
+            h = list(h)[-64:]
+            hist[i, :len(h)] = h
+            counts[i] = len(h)
+        sd = np.ascontiguousarray(seeds, dtype=np.uint32)
+        tok = np.zeros(n, np.int32)
+        s = MochaSampling(temperature, top_k, top_p, penalty, 0)
+        if self.lib.mocha_q8b_sample_check(self.h, n, lg.ctypes.data, hist.ctypes.data, counts.ctypes.data,
+                                           C.byref(s), sd.ctypes.data, tok.ctypes.data):
+            raise RuntimeError("mocha_q8b_sample_check failed")
+        return tok.tolist()

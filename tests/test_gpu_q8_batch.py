@@ -1,0 +1,103 @@
+"""Batched grouped-Q8 engine (tcgen05 GEMMs) against the C oracle of the reference
+CPU forward: prefill logits, multi-slot rows, greedy and sampled token loops, and the
+batched sampler bit-exact on identical logits."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+VOCAB = 151936
+
+
+def close(got, ref):
+    err = np.abs(got - ref)
+    assert np.all(np.isfinite(got))
+    assert np.all(err <= 0.003 * (1 + np.abs(ref))), float(err.max())
+    assert err.max() <= 2e-3 * float(ref.max() - ref.min())
+    return float(err.max())
+
+
+@pytest.fixture(scope="module")
+def batch(native, q8_model_bytes):
+    h = native.Q8BatchHandle(0, q8_model_bytes, max_rows=1024, slots=8)
+    yield h
+    h.close()
+
+
+@pytest.fixture(scope="module")
+def oracle(oracle_lib, q8_model_bytes):
+    return oracle_lib.Q8Oracle(q8_model_bytes)
+
+
+def oracle_prompt_logits(oracle, prompt):
+    oracle.reset()
+    out = None
+    for pos, tok in enumerate(prompt):
+        out = oracle.forward(tok, pos, pos == len(prompt) - 1)
+    return out
+
+
+def test_prefill_logits(batch, oracle):
+    prompt = np.random.default_rng(11).integers(0, VOCAB, 40).tolist()
+    got = batch.prefill(0, prompt)
+    ref = oracle_prompt_logits(oracle, prompt)
+    err = close(got, ref)
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+    print("prefill 40 max abs logit error", err)
+
+
+def test_rows_of_several_slots(batch, oracle):
+    rng = np.random.default_rng(12)
+    p1 = rng.integers(0, VOCAB, 9).tolist()
+    p2 = rng.integers(0, VOCAB, 5).tolist()
+    toks = p1 + p2
+    pos = list(range(len(p1))) + list(range(len(p2)))
+    slots = [3] * len(p1) + [5] * len(p2)
+    got = batch.forward(toks, pos, slots, [len(p1) - 1, len(toks) - 1])
+    for row, prompt in ((0, p1), (1, p2)):
+        close(got[row], oracle_prompt_logits(oracle, prompt))
+
+
+def test_chunked_prefill_equals_one_pass(batch):
+    prompt = np.random.default_rng(13).integers(0, VOCAB, 1024).tolist()
+    one = batch.prefill(1, prompt)
+    a = batch.forward(prompt[:512], list(range(512)), [2] * 512, [])
+    assert a.shape[0] == 0
+    two = batch.forward(prompt[512:], list(range(512, 1024)), [2] * 512, [511])[0]
+    assert np.all(np.isfinite(one))
+    assert np.max(np.abs(one - two)) <= 1e-5 * (1 + np.max(np.abs(one)))
+
+
+def test_greedy_batch_matches_oracle(batch, oracle):
+    prompts = np.random.default_rng(14).integers(0, VOCAB, (3, 16))
+    toks, timing = batch.generate(prompts, 8)
+    for i in range(3):
+        ref, _ = oracle.generate(prompts[i].tolist(), 8)
+        assert toks[i] == ref, i
+    assert timing.generated == sum(len(t) for t in toks)
+
+
+def test_sampled_batch_matches_oracle(batch, oracle):
+    prompts = np.random.default_rng(15).integers(0, VOCAB, (2, 12))
+    toks, _ = batch.generate(prompts, 6, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=100)
+    for i in range(2):
+        ref, _ = oracle.generate(prompts[i].tolist(), 6, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12,
+                                 seed=100 + i)
+        assert toks[i] == ref, i
+
+
+@pytest.mark.parametrize("temperature,top_k,top_p,penalty", [
+    (0.0, 1, 1.0, 1.0), (0.0, 1, 1.0, 1.3), (0.7, 40, 0.9, 1.12), (1.0, 64, 1.0, 1.0), (0.5, 5, 0.5, 1.5)])
+def test_sampler_bit_exact(batch, oracle_lib, temperature, top_k, top_p, penalty):
+    rng = np.random.default_rng(16)
+    n = 6
+    logits = (rng.standard_normal((n, VOCAB)) * 2).astype(np.float32)
+    logits[1, 1000:1010] = logits[1].max() + 1  # ties: lower id first
+    hists = [rng.integers(0, VOCAB, rng.integers(0, 80)).tolist() for _ in range(n)]
+    hists[2] = [int(np.argmax(logits[2]))] * 3 + hists[2][:10]  # repeated id penalised once
+    hists[3] = []
+    seeds = rng.integers(1, 2**32 - 1, n, dtype=np.uint64).astype(np.uint32)
+    got = batch.sample(logits, hists, temperature, top_k, top_p, penalty, seeds)
+    for i in range(n):
+        ref, _, _ = oracle_lib.sample(logits[i], hists[i][-64:], temperature, top_k, top_p, penalty, int(seeds[i]))
+        assert got[i] == ref, (i, got[i], ref)
