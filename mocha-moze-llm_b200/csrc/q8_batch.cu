@@ -247,19 +247,143 @@ __global__ void __launch_bounds__(HEAD_DIM) k_attn_combine(const float *__restri
 }
 
 // h = silu(gate) * up from the gate|up partials, split for the down GEMM.
+// grid (ceil(HIDDEN / 256), rows)
 __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride, bf16 *hh,
                                                 bf16 *hl)
 {
-    const int t = blockIdx.x;
+    const int t = blockIdx.y, i = blockIdx.x * 256 + threadIdx.x;
+    if (i >= HIDDEN) return;
     const float *p = part + (size_t)t * GU_ROWS;
-    for (int i = threadIdx.x; i < HIDDEN; i += 256) {
-        float g = p[i], u = p[HIDDEN + i];
-        for (int s = 1; s < splits; s++) {
-            g += p[s * sstride + i];
-            u += p[s * sstride + HIDDEN + i];
+    float g = p[i], u = p[HIDDEN + i];
+    for (int s = 1; s < splits; s++) {
+        g += p[s * sstride + i];
+        u += p[s * sstride + HIDDEN + i];
+    }
+    const float h = (g / (1.f + expf(-g))) * u;
+    mb::tc::split_bf16(h, hh[(size_t)t * HIDDEN + i], hl[(size_t)t * HIDDEN + i]);
+}
+
+// Prompt attention for a block of 64 consecutive rows of one slot (positions
+// p0..p0+63, p0 a multiple of 64) and one query head: key chunks of 64 staged in
+// shared memory, online softmax, fp32 throughout.  Thread (ty, tx) owns query rows
+// ty + 16i and, for scores, keys tx + 16j (strided so the float4 reads of K rows hit
+// distinct banks); for the output, dims 4tx..4tx+3.
+constexpr int QB = 64;
+constexpr int QB_LD = HEAD_DIM + 4;  // padded row (floats) of the Q, K and P tiles
+constexpr size_t QB_SMEM = sizeof(float) * (3 * QB * QB_LD + CHUNK * HEAD_DIM);
+
+__global__ void __launch_bounds__(256) k_attn_block(const float *__restrict__ q, Rows rows,
+                                                    const float *__restrict__ kc, const float *__restrict__ vc,
+                                                    int layer, bf16 *ah, bf16 *al)
+{
+    extern __shared__ float4 smem4[];
+    float *sQ = reinterpret_cast<float *>(smem4);
+    float *sK = sQ + QB * QB_LD;
+    float *sP = sK + CHUNK * QB_LD;
+    float *sV = sP + QB * QB_LD;
+    const int h = blockIdx.y, g = h / GQA, t0 = blockIdx.x * QB;
+    const int slot = rows.slot[t0], p0 = rows.pos[t0];
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    for (int idx = tid; idx < QB * HEAD_DIM / 4; idx += 256) {
+        const int r = idx / (HEAD_DIM / 4), c4 = idx % (HEAD_DIM / 4);
+        reinterpret_cast<float4 *>(sQ + r * QB_LD)[c4] =
+            *reinterpret_cast<const float4 *>(q + (size_t)(t0 + r) * DIM + h * HEAD_DIM + c4 * 4);
+    }
+    float m[4], l[4], acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+    }
+    const int nchunks = p0 / CHUNK + 1;
+    for (int c = 0; c < nchunks; c++) {
+        const size_t base = kv_off(slot, layer, g, c * CHUNK);
+        __syncthreads();  // previous chunk's K, V and P are no longer read
+        for (int idx = tid; idx < CHUNK * HEAD_DIM / 4; idx += 256) {
+            const int r = idx / (HEAD_DIM / 4), c4 = idx % (HEAD_DIM / 4);
+            reinterpret_cast<float4 *>(sK + r * QB_LD)[c4] = *reinterpret_cast<const float4 *>(kc + base + idx * 4);
+            reinterpret_cast<float4 *>(sV)[idx] = *reinterpret_cast<const float4 *>(vc + base + idx * 4);
         }
-        const float h = (g / (1.f + expf(-g))) * u;
-        mb::tc::split_bf16(h, hh[(size_t)t * HIDDEN + i], hl[(size_t)t * HIDDEN + i]);
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < HEAD_DIM / 4; d4++) {
+            float4 qa[4], kb[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qa[i] = reinterpret_cast<const float4 *>(sQ + (ty + 16 * i) * QB_LD)[d4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) kb[j] = reinterpret_cast<const float4 *>(sK + (tx + 16 * j) * QB_LD)[d4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    sc[i][j] = fmaf(qa[i].x, kb[j].x, sc[i][j]);
+                    sc[i][j] = fmaf(qa[i].y, kb[j].y, sc[i][j]);
+                    sc[i][j] = fmaf(qa[i].z, kb[j].z, sc[i][j]);
+                    sc[i][j] = fmaf(qa[i].w, kb[j].w, sc[i][j]);
+                }
+        }
+        const bool diagonal = c == nchunks - 1;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int qpos = ty + 16 * i;  // relative to p0; the diagonal chunk starts at p0
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (diagonal && tx + 16 * j > qpos) sc[i][j] = -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mnew = fmaxf(m[i], mx);
+            const float scale = expf(m[i] - mnew);
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float e = expf(sc[i][j] - mnew);
+                sP[(ty + 16 * i) * QB_LD + tx + 16 * j] = e;
+                sum += e;
+            }
+#pragma unroll
+            for (int o = 8; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            l[i] = l[i] * scale + sum;
+            m[i] = mnew;
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] *= scale;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int k4 = 0; k4 < CHUNK / 4; k4++) {
+            float4 pa[4], vb[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pa[i] = reinterpret_cast<const float4 *>(sP + (ty + 16 * i) * QB_LD)[k4];
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) vb[kk] = reinterpret_cast<const float4 *>(sV + (k4 * 4 + kk) * HEAD_DIM)[tx];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float pv[4] = {pa[i].x, pa[i].y, pa[i].z, pa[i].w};
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    acc[i][0] = fmaf(pv[kk], vb[kk].x, acc[i][0]);
+                    acc[i][1] = fmaf(pv[kk], vb[kk].y, acc[i][1]);
+                    acc[i][2] = fmaf(pv[kk], vb[kk].z, acc[i][2]);
+                    acc[i][3] = fmaf(pv[kk], vb[kk].w, acc[i][3]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const size_t o = (size_t)(t0 + ty + 16 * i) * DIM + h * HEAD_DIM + tx * 4;
+        const float inv = 1.f / l[i];
+#pragma unroll
+        for (int j = 0; j < 4; j++) mb::tc::split_bf16(acc[i][j] * inv, ah[o + j], al[o + j]);
     }
 }
 
@@ -281,6 +405,116 @@ MB_DEV void bitonic_desc(unsigned long long *keys, int n)
         }
 }
 
+// Exact top k (k <= 64) of n unique 64-bit keys in shared memory, best first, into
+// out[0..k): radix select of the k-th largest key over 8-bit digits from the top
+// (passes stop once the boundary digit holds exactly the keys still needed), then
+// compaction of the keys >= that threshold and a one-warp bitonic sort of the k
+// survivors.  All threads of the block call it.
+struct TopkScratch {
+    unsigned hist[256];
+    unsigned long long prefix, mask;
+    int need, count;
+};
+
+MB_DEV void block_topk(const unsigned long long *keys, int n, int k, unsigned long long *out, TopkScratch &sc)
+{
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) {
+        sc.prefix = 0ull;
+        sc.mask = 0ull;
+        sc.need = k;
+        sc.count = 0;
+    }
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += nt) sc.hist[b] = 0u;
+        __syncthreads();
+        const unsigned long long prefix = sc.prefix, mask = sc.mask;
+        for (int i = tid; i < n; i += nt)
+            if ((keys[i] & mask) == prefix) atomicAdd(&sc.hist[(unsigned)(keys[i] >> shift) & 255u], 1u);
+        __syncthreads();
+        if (tid < 32) {
+            // digit d where the keys above d number < need <= keys at or above d
+            const int lane = tid;
+            unsigned above = 0u;  // keys in digits greater than this lane's 8-digit group
+            unsigned grp = 0u;
+#pragma unroll
+            for (int j = 0; j < 8; j++) grp += sc.hist[255 - (lane * 8 + j)];
+            unsigned incl = grp;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            above = incl - grp;
+            const unsigned need = (unsigned)sc.need;
+            const bool mine = above < need && need <= incl;
+            const unsigned who = __ballot_sync(0xffffffffu, mine);
+            if (mine) {
+                unsigned acc = above;
+                int d = 255 - lane * 8;
+                for (int j = 0; j < 8; j++, d--) {
+                    const unsigned c = sc.hist[d];
+                    if (acc + c >= need) break;
+                    acc += c;
+                }
+                sc.need = (int)(need - acc);
+                sc.prefix = prefix | ((unsigned long long)d << shift);
+                sc.mask = mask | (255ull << shift);
+                sc.count = (int)sc.hist[d];
+            }
+            (void)who;
+        }
+        __syncthreads();
+        if (sc.count == sc.need) break;  // every key with this prefix is in
+    }
+    // keys strictly above the prefix group, plus the prefix group when it is all in
+    const unsigned long long prefix = sc.prefix, mask = sc.mask;
+    const bool all_group = sc.count == sc.need;
+    __syncthreads();
+    if (tid == 0) sc.count = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
+        const unsigned long long key = keys[i];
+        const unsigned long long kp = key & mask;
+        if (kp > prefix || (kp == prefix && all_group)) {
+            const int slot = atomicAdd(&sc.count, 1);
+            if (slot < 64) out[slot] = key;
+        }
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int m = min(sc.count, 64);
+        unsigned long long a = tid < m ? out[tid] : 0ull, b = tid + 32 < m ? out[tid + 32] : 0ull;
+        // bitonic sort of 64 keys held two per lane (a = element lane, b = element lane + 32), descending
+        for (int size = 2; size <= 64; size <<= 1) {
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                if (stride == 32) {
+                    const bool desc = true;
+                    if (desc ? (a < b) : (a > b)) {
+                        const unsigned long long t = a;
+                        a = b;
+                        b = t;
+                    }
+                } else {
+                    // elements i = lane and i = lane + 32 paired with i ^ stride (same half)
+                    const unsigned long long pa = __shfl_xor_sync(0xffffffffu, a, stride);
+                    const unsigned long long pb = __shfl_xor_sync(0xffffffffu, b, stride);
+                    const int ia = tid, ib = tid + 32;
+                    const bool da = (ia & size) == 0, db = (ib & size) == 0;
+                    const bool lowa = (ia & stride) == 0, lowb = (ib & stride) == 0;
+                    // low element keeps the larger value in a descending run
+                    a = (lowa == da) ? (a > pa ? a : pa) : (a < pa ? a : pa);
+                    b = (lowb == db) ? (b > pb ? b : pb) : (b < pb ? b : pb);
+                }
+            }
+        }
+        __syncwarp();
+        if (tid < k) out[tid] = a;
+        if (tid + 32 < k) out[tid + 32] = b;
+    }
+    __syncthreads();
+}
+
 // Stage 1: for projected row r and a slice of SLICE ids, penalty (once per distinct
 // id of the slot's history), control mask, and the slice's top k keys.
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__restrict__ logits, const int *proj_src,
@@ -289,7 +523,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
                                                               unsigned long long *__restrict__ out)
 {
     __shared__ unsigned long long keys[SLICE];
-    __shared__ float vals[SLICE];
+    __shared__ int hist[sampling::kHistory];
     const int r = blockIdx.y, lo = blockIdx.x * SLICE;
     const int n = min(VOCAB - lo, SLICE);
     const sampling::Params p = *prm;
@@ -298,34 +532,35 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
     if (slot < 0 || slot >= nslots) return;
     const sampling::SeqState *s = st + slot;
     const float *lg = logits + (size_t)r * VOCAB + lo;
-    for (int i = threadIdx.x; i < SLICE; i += SAMPLE_THREADS) vals[i] = i < n ? lg[i] : 0.f;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        const int count = min(max(s->history_count, 0), sampling::kHistory);
-        for (int j = threadIdx.x; j < count; j += 32) {
-            const int id = s->history[j];
-            bool dup = false;
-            for (int u = 0; u < j; u++) dup |= s->history[u] == id;
-            if (!dup && id >= lo && id < lo + n) {
-                const float v = vals[id - lo];
-                vals[id - lo] = v < 0 ? v * p.penalty : v / p.penalty;
-            }
-        }
-    }
-    __syncthreads();
+    const int count = min(max(s->history_count, 0), sampling::kHistory);
+    if (threadIdx.x < count) hist[threadIdx.x] = s->history[threadIdx.x];
+    // keys of the masked logits; penalised ids are rewritten below
     for (int i = threadIdx.x; i < SLICE; i += SAMPLE_THREADS) {
         unsigned long long key = 0ull;
         if (i < n) {
             const int id = lo + i;
-            const float v = (id >= p.control_first && id != p.eos) ? -1e30f : vals[i];
-            key = mb::rank_key(v, id);
+            key = mb::rank_key((id >= p.control_first && id != p.eos) ? -1e30f : lg[i], id);
         }
         keys[i] = key;
     }
     __syncthreads();
-    bitonic_desc(keys, SLICE);
+    if (threadIdx.x < 32) {
+        for (int j = threadIdx.x; j < count; j += 32) {
+            const int id = hist[j];
+            bool dup = false;
+            for (int u = 0; u < j; u++) dup |= hist[u] == id;
+            if (!dup && id >= lo && id < lo + n && !(id >= p.control_first && id != p.eos)) {
+                const float v = lg[id - lo];
+                keys[id - lo] = mb::rank_key(v < 0 ? v * p.penalty : v / p.penalty, id);
+            }
+        }
+    }
+    __syncthreads();
+    __shared__ unsigned long long best[sampling::kMaxK];
+    __shared__ TopkScratch sc;
+    block_topk(keys, SLICE, k, best, sc);
     for (int j = threadIdx.x; j < k; j += SAMPLE_THREADS)
-        out[((size_t)r * NSLICE + blockIdx.x) * sampling::kMaxK + j] = keys[j];
+        out[((size_t)r * NSLICE + blockIdx.x) * sampling::kMaxK + j] = best[j];
 }
 
 // Stage 2: merge the slices, draw the token, record it for the slot and set up the
@@ -349,8 +584,11 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned lon
         keys[i] = (sl < NSLICE) ? in[((size_t)r * NSLICE + sl) * sampling::kMaxK + j] : 0ull;
     }
     __syncthreads();
-    bitonic_desc(keys, kMerge);
+    __shared__ unsigned long long best[sampling::kMaxK];
+    __shared__ TopkScratch sc;
+    block_topk(keys, kMerge, k, best, sc);
     if (threadIdx.x == 0) {
+        const unsigned long long *keys = best;
         sampling::SeqState *s = st + slot;
         uint32_t seed = s->seed;
         int token = sampling::draw_token(keys, p, seed);
@@ -465,34 +703,64 @@ size_t plan_floats(const PlanSet &ps)
     size_t m = 0;
     for (int l = 0; l < LAYERS; l++) {
         const Gemm *g[4] = {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]};
-        for (const Gemm *x : g) m = std::max(m, (size_t)x->splits * (size_t)x->p.split_stride);
+        for (const Gemm *x : g) m = std::max(m, mb::tc::gemm_partial_floats(*x));
     }
     return m;
 }
 
+// Attention for rows [0, n): the query-block kernel when every 64-row block is one
+// slot at consecutive positions starting at a multiple of 64 (prompt passes whose
+// per-slot length is a multiple of 64), else the per-row chunk kernels.
+int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, bool block)
+{
+    static bool attr_done[64] = {};
+    if (block) {
+        if (!attr_done[h->device & 63]) {
+            QB_TRY(cudaFuncSetAttribute(k_attn_block, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QB_SMEM));
+            attr_done[h->device & 63] = true;
+        }
+        k_attn_block<<<dim3(n / QB, HEADS), 256, QB_SMEM, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->ah, h->al);
+        return 0;
+    }
+    k_attn_chunk<<<dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->apart);
+    k_attn_combine<<<dim3(HEADS, n), HEAD_DIM, 0, h->stream>>>(h->apart, rows, h->ah, h->al);
+    return 0;
+}
+
+// True when rows (host arrays) qualify for the query-block attention kernel.
+bool block_rows(int n, const int *pos, const int *slots)
+{
+    if (n % QB) return false;
+    for (int b = 0; b < n; b += QB) {
+        if (pos[b] % QB) return false;
+        for (int i = 1; i < QB; i++)
+            if (slots[b + i] != slots[b] || pos[b + i] != pos[b] + i) return false;
+    }
+    return true;
+}
+
 // The whole transformer for rows [0, n) plus the head for `np` projected rows
 // (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of headh/headl).
-int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np)
+int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np,
+                    bool block_attention)
 {
     const PlanSet &ps = decode_set ? h->dec : h->pre;
     cudaStream_t s = h->stream;
     k_embed_norm<<<n, NT, 0, s>>>(h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->xh, h->xl);
+    mb::tc::Split sp;
     for (int l = 0; l < LAYERS; l++) {
         const Layer &L = h->m.layer[l];
-        if (mb::tc::gemm_launch(ps.qkv[l], n, s)) return 1;
-        k_qkv_post<<<n, QKV_THREADS, 0, s>>>(h->part, ps.qkv[l].splits, ps.qkv[l].p.split_stride,
-                                              h->bqkv + (size_t)l * QKV_ROWS, rows, h->rope_cos, h->rope_sin, h->q,
-                                              h->kc, h->vc, l);
-        k_attn_chunk<<<dim3(NCHUNK, KV_HEADS, n), 128, 0, s>>>(h->q, rows, h->kc, h->vc, l, h->apart);
-        k_attn_combine<<<dim3(HEADS, n), HEAD_DIM, 0, s>>>(h->apart, rows, h->ah, h->al);
-        if (mb::tc::gemm_launch(ps.o[l], n, s)) return 1;
-        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, ps.o[l].splits, ps.o[l].p.split_stride, L.ffn_norm, h->xh,
-                                          h->xl, nullptr);
-        if (mb::tc::gemm_launch(ps.gu[l], n, s)) return 1;
-        k_swiglu<<<n, 256, 0, s>>>(h->part, ps.gu[l].splits, ps.gu[l].p.split_stride, h->hh, h->hl);
-        if (mb::tc::gemm_launch(ps.down[l], n, s)) return 1;
+        if (mb::tc::gemm_launch(ps.qkv[l], n, s, &sp)) return 1;
+        k_qkv_post<<<n, QKV_THREADS, 0, s>>>(h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
+                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l);
+        if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
+        if (mb::tc::gemm_launch(ps.o[l], n, s, &sp)) return 1;
+        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->xh, h->xl, nullptr);
+        if (mb::tc::gemm_launch(ps.gu[l], n, s, &sp)) return 1;
+        k_swiglu<<<dim3((HIDDEN + 255) / 256, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->hh, h->hl);
+        if (mb::tc::gemm_launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
-        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, ps.down[l].splits, ps.down[l].p.split_stride,
+        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride,
                                           last ? h->m.final_norm : h->m.layer[l + 1].attn_norm,
                                           last ? h->headh : h->xh, last ? h->headl : h->xl,
                                           last ? proj_dst : nullptr);
@@ -553,7 +821,7 @@ int capture_step(mocha_q8b *h, int n)
     cudaGraph_t g;
     QB_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     const Rows r{h->ntok, h->npos, h->nslot};
-    int rc = enqueue_forward(h, r, n, true, h->ident, n);
+    int rc = enqueue_forward(h, r, n, true, h->ident, n, false);
     if (!rc) rc = enqueue_sample(h, r, n, h->ident);
     const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
     if (rc || e != cudaSuccess) {
@@ -733,7 +1001,7 @@ extern "C" int mocha_q8b_forward(mocha_q8b *h, int n, const int *tokens, const i
     QB_TRY(cudaSetDevice(h->device));
     if (upload_rows(h, n, tokens, pos, slots) || set_projection(h, n, n_project, project_rows)) return 1;
     const Rows r{h->tok, h->pos, h->slot};
-    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project)) return 1;
+    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project, block_rows(n, pos, slots))) return 1;
     if (logits && n_project)
         QB_TRY(cudaMemcpyAsync(logits, h->logits, sizeof(float) * VOCAB * n_project, cudaMemcpyDeviceToHost,
                                h->stream));
@@ -819,7 +1087,9 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
         if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, b, src.data())) return 1;
         QB_TRY(cudaEventRecord(h->ev[0], h->stream));
         const Rows pr{h->tok, h->pos, h->slot};
-        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b) || enqueue_sample(h, pr, b, h->proj_src)) return 1;
+        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b, prompt_len % QB == 0) ||
+            enqueue_sample(h, pr, b, h->proj_src))
+            return 1;
         QB_TRY(cudaEventRecord(h->ev[1], h->stream));
         if (n_new > 1 && capture_step(h, b)) return 1;
         for (int step = 1; step < n_new; step++) QB_TRY(cudaGraphLaunch(h->g_step, h->stream));
@@ -922,11 +1192,12 @@ extern "C" int mocha_q8b_bench_prefill(mocha_q8b *h, int n, unsigned seed, int w
     const int last = n - 1;
     if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, 1, &last)) return 1;
     const Rows r{h->tok, h->pos, h->slot};
+    const bool block = n % QB == 0;
     for (int i = 0; i < warmup; i++)
-        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1)) return 1;
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block)) return 1;
     QB_TRY(cudaEventRecord(h->ev[0], h->stream));
     for (int i = 0; i < steps; i++)
-        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1)) return 1;
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block)) return 1;
     QB_TRY(cudaEventRecord(h->ev[1], h->stream));
     QB_TRY(cudaEventSynchronize(h->ev[1]));
     QB_TRY(cudaEventElapsedTime(ms, h->ev[0], h->ev[1]));

@@ -63,7 +63,8 @@ extern "C" int mocha_tc_gemm_check(int device, int rows, int n, int cols, const 
     MB_CHECK(cudaGetLastError());
     // plan with the partial buffer sized after the split count is known
     if (mb::tc::gemm_plan(&g, whi, wlo, rows, cols, xhi, xlo, n, nullptr, rows, splits, err)) return 1;
-    float *dp = b.alloc<float>((size_t)g.splits * n * rows);
+    const mb::tc::Split sp = mb::tc::gemm_split(g, n);
+    float *dp = b.alloc<float>((size_t)sp.splits * n * rows);
     if (!dp) return 1;
     g.p.d = dp;
     if (mb::tc::gemm_launch(g, n, 0)) return 1;
@@ -74,11 +75,11 @@ extern "C" int mocha_tc_gemm_check(int device, int rows, int n, int cols, const 
         fprintf(stderr, "mocha_tc_gemm_check: kernel reported error %d\n", herr);
         return 1;
     }
-    std::vector<float> part((size_t)g.splits * n * rows);
+    std::vector<float> part((size_t)sp.splits * n * rows);
     MB_CHECK(cudaMemcpy(part.data(), dp, part.size() * 4, cudaMemcpyDeviceToHost));
     for (size_t i = 0; i < (size_t)n * rows; i++) {
         float acc = 0.f;
-        for (int s = 0; s < g.splits; s++) acc += part[(size_t)s * n * rows + i];
+        for (int s = 0; s < sp.splits; s++) acc += part[(size_t)s * n * rows + i];
         y[i] = acc;
     }
     return 0;

@@ -227,17 +227,11 @@ int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int
     if (make_map(&g->p.a_hi, w_hi, M, K, kBM) || make_map(&g->p.a_lo, w_lo, M, K, kBM) ||
         make_map(&g->p.b_hi, x_hi, n_max, K, g->bn) || make_map(&g->p.b_lo, x_lo, n_max, K, g->bn))
         return 1;
-    const int ksteps = K / kBK;
-    const int tiles = (M / kBM) * ((n_max + g->bn - 1) / g->bn);
-    if (splits <= 0) splits = (2 * kSMs + tiles - 1) / tiles;
-    if (splits > ksteps) splits = ksteps;
-    if (splits < 1) splits = 1;
-    const int per = (ksteps + splits - 1) / splits;
-    g->splits = (ksteps + per - 1) / per;
-    g->p.ksteps = per;
+    g->fixed_splits = splits > 0 ? splits : 0;
     g->p.d = d;
     g->p.ldd = ldd;
     g->p.split_stride = (long long)n_max * ldd;
+    g->p.ksteps = K / kBK;
     g->p.M = M;
     g->p.N = n_max;
     g->p.K = K;
@@ -246,15 +240,41 @@ int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int
     return g->bn == 64 ? setup_attr<64>() : setup_attr<128>();
 }
 
-int gemm_launch(const Gemm &g, int n, cudaStream_t s)
+Split gemm_split(const Gemm &g, int n)
+{
+    const int ksteps = g.p.K / kBK;
+    const int tiles = (g.p.M / kBM) * ((n + g.bn - 1) / g.bn);
+    int splits = g.fixed_splits > 0 ? g.fixed_splits : (2 * kSMs + tiles - 1) / tiles;
+    splits = splits < 1 ? 1 : (splits > ksteps ? ksteps : splits);
+    const int per = (ksteps + splits - 1) / splits;
+    return Split{(ksteps + per - 1) / per, (long long)n * g.p.ldd};
+}
+
+size_t gemm_partial_floats(const Gemm &g)
+{
+    size_t m = 0;
+    for (int n = 1; n <= g.p.N; n++) {
+        const Split s = gemm_split(g, n);
+        const size_t f = (size_t)s.splits * (size_t)s.split_stride;
+        m = f > m ? f : m;
+    }
+    return m;
+}
+
+int gemm_launch(const Gemm &g, int n, cudaStream_t s, Split *used)
 {
     if (n <= 0 || n > g.p.N) {
         fprintf(stderr, "mocha: gemm_launch: n=%d outside 1..%d\n", n, g.p.N);
         return 1;
     }
+    const Split sp = gemm_split(g, n);
+    const int ksteps = g.p.K / kBK;
     GemmParams p = g.p;
     p.N = n;
-    const dim3 grid(p.M / kBM, (n + g.bn - 1) / g.bn, g.splits);
+    p.ksteps = (ksteps + sp.splits - 1) / sp.splits;
+    p.split_stride = sp.split_stride;
+    if (used) *used = sp;
+    const dim3 grid(p.M / kBM, (n + g.bn - 1) / g.bn, sp.splits);
     if (g.bn == 64)
         k_gemm_bf16x3<64><<<grid, kThreads, g.smem, s>>>(p);
     else

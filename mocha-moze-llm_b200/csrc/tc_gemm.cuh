@@ -35,15 +35,30 @@ struct GemmParams {
 };
 
 // One GEMM call site: tensor maps for a fixed weight and a fixed activation buffer.
+// The K split is chosen per launch from the row count; split s of a launch with n
+// rows writes d + s * n * ldd.
 struct Gemm {
     GemmParams p;
-    int bn = 0, splits = 1;
+    int bn = 0;
+    int fixed_splits = 0;  // > 0: always this many splits
     size_t smem = 0;
 };
 
+struct Split {
+    int splits;              // partial tiles to sum, in order
+    long long split_stride;  // floats between them (n * ldd)
+};
+
+// Split count and stride a launch with n rows uses.
+Split gemm_split(const Gemm &g, int n);
+
+// Largest splits * n * ldd over n in [1, n_max]: the partial-buffer size in floats.
+size_t gemm_partial_floats(const Gemm &g);
+
 // Builds a call site: weights `w_hi/w_lo` [M][K], activations `x_hi/x_lo` [n_max][K]
 // (rows beyond the `n` given at launch are never read into results), output `d`.
-// `splits` = 0 picks a split count that fills the GPU.  Returns 0 on success.
+// `splits` = 0 picks, per launch, a split count that fills the GPU.  Returns 0 on
+// success.
 int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int M, int K,
               const __nv_bfloat16 *x_hi, const __nv_bfloat16 *x_lo, int n_max, float *d, long long ldd, int splits,
               int *err);
@@ -51,7 +66,7 @@ int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int
 // Launches for the first `n` activation rows (n <= n_max).  `n` changes only the
 // grid, never the tensor maps, so a plan can be reused inside a CUDA graph capture
 // for a fixed n.
-int gemm_launch(const Gemm &g, int n, cudaStream_t s);
+int gemm_launch(const Gemm &g, int n, cudaStream_t s, Split *used = nullptr);
 
 // Weights: bf16 pair of q*s for a grouped-Q8 matrix (int8 [M][K], fp32 scale per 64).
 int split_weights(const int8_t *q, const float *scales, size_t count, __nv_bfloat16 *hi, __nv_bfloat16 *lo,

@@ -65,7 +65,9 @@ def test_chunked_prefill_equals_one_pass(batch):
     assert a.shape[0] == 0
     two = batch.forward(prompt[512:], list(range(512, 1024)), [2] * 512, [511])[0]
     assert np.all(np.isfinite(one))
-    assert np.max(np.abs(one - two)) <= 1e-5 * (1 + np.max(np.abs(one)))
+    # the GEMM K split depends on the row count, so only the summation order differs
+    assert np.max(np.abs(one - two)) <= 2e-4 * (1 + np.max(np.abs(one)))
+    assert int(np.argmax(one)) == int(np.argmax(two))
 
 
 def test_greedy_batch_matches_oracle(batch, oracle):
