@@ -246,21 +246,29 @@ __global__ void __launch_bounds__(HEAD_DIM) k_attn_combine(const float *__restri
     mb::tc::split_bf16(acc / l, ah[o], al[o]);
 }
 
-// h = silu(gate) * up from the gate|up partials, split for the down GEMM.
-// grid (ceil(HIDDEN / 256), rows)
+// h = silu(gate) * up from the gate|up partials, split for the down GEMM; two
+// features per thread.  grid (ceil(HIDDEN / 512), rows)
 __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride, bf16 *hh,
                                                 bf16 *hl)
 {
-    const int t = blockIdx.y, i = blockIdx.x * 256 + threadIdx.x;
+    const int t = blockIdx.y, i = (blockIdx.x * 256 + threadIdx.x) * 2;
     if (i >= HIDDEN) return;
     const float *p = part + (size_t)t * GU_ROWS;
-    float g = p[i], u = p[HIDDEN + i];
+    float2 g = *reinterpret_cast<const float2 *>(p + i), u = *reinterpret_cast<const float2 *>(p + HIDDEN + i);
     for (int s = 1; s < splits; s++) {
-        g += p[s * sstride + i];
-        u += p[s * sstride + HIDDEN + i];
+        const float2 gs = *reinterpret_cast<const float2 *>(p + s * sstride + i);
+        const float2 us = *reinterpret_cast<const float2 *>(p + s * sstride + HIDDEN + i);
+        g.x += gs.x;
+        g.y += gs.y;
+        u.x += us.x;
+        u.y += us.y;
     }
-    const float h = (g / (1.f + expf(-g))) * u;
-    mb::tc::split_bf16(h, hh[(size_t)t * HIDDEN + i], hl[(size_t)t * HIDDEN + i]);
+    const float h0 = (g.x / (1.f + expf(-g.x))) * u.x, h1 = (g.y / (1.f + expf(-g.y))) * u.y;
+    __nv_bfloat162 hi, lo;
+    mb::tc::split_bf16(h0, hi.x, lo.x);
+    mb::tc::split_bf16(h1, hi.y, lo.y);
+    *reinterpret_cast<__nv_bfloat162 *>(hh + (size_t)t * HIDDEN + i) = hi;
+    *reinterpret_cast<__nv_bfloat162 *>(hl + (size_t)t * HIDDEN + i) = lo;
 }
 
 // Prompt attention for a block of 64 consecutive rows of one slot (positions
@@ -757,7 +765,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
         if (mb::tc::gemm_launch(ps.o[l], n, s, &sp)) return 1;
         k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->xh, h->xl, nullptr);
         if (mb::tc::gemm_launch(ps.gu[l], n, s, &sp)) return 1;
-        k_swiglu<<<dim3((HIDDEN + 255) / 256, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->hh, h->hl);
+        k_swiglu<<<dim3((HIDDEN + 511) / 512, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->hh, h->hl);
         if (mb::tc::gemm_launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
         k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride,

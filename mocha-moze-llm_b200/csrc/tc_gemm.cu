@@ -19,7 +19,7 @@ struct Cfg {
     static constexpr int stages = BN <= 64 ? 4 : (BN <= 128 ? 3 : 2);
     static constexpr uint32_t b_bytes = BN * kBK * 2;
     static constexpr uint32_t stage_bytes = 2 * kABytes + 2 * b_bytes;
-    static constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
+    static constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;  // per accumulator buffer
     static constexpr size_t smem = 1024 + (size_t)stages * stage_bytes + 256;
 };
 
@@ -29,64 +29,75 @@ MB_DEV void gemm_fail(int *err, volatile int *abort, int code)
     atomicCAS(err, 0, code);
 }
 
+// Persistent form: gridDim.x CTAs walk the tiles (m fastest, then n, then split) in
+// a static stride.  The TMA ring runs continuously across tiles; the accumulator is
+// double-buffered in TMEM so the epilogue of one tile overlaps the MMAs of the next.
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1) k_gemm_bf16x3(const __grid_constant__ GemmParams p)
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_bf16x3(const __grid_constant__ GemmParams p, int m_tiles,
+                                                             int n_tiles, int tiles)
 {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *full = (uint64_t *)(smem + C::stages * C::stage_bytes);
     uint64_t *empty = full + C::stages;
-    uint64_t *accum = empty + C::stages;
-    uint32_t *tmem_slot = (uint32_t *)(accum + 1);
+    uint64_t *acc_full = empty + C::stages;  // [2]
+    uint64_t *acc_empty = acc_full + 2;      // [2]
+    uint64_t *drain = acc_empty + 2;         // MMA completion on the abort path
+    uint32_t *tmem_slot = (uint32_t *)(drain + 1);
     volatile int *abort = (volatile int *)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-    const int ks0 = blockIdx.z * p.ksteps;
-    const int nk = min(p.ksteps, p.K / kBK - ks0);
+    const int ksteps_total = p.K / kBK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::stages; s++) {
             as::mbar_init(&full[s], 1);
             as::mbar_init(&empty[s], 1);
         }
-        as::mbar_init(accum, 1);
+        for (int b = 0; b < 2; b++) {
+            as::mbar_init(&acc_full[b], 1);
+            as::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        }
+        as::mbar_init(drain, 1);
         *abort = 0;
         as::fence_barrier_init();
     }
-    if (warp == 1) as::tmem_alloc(tmem_slot, C::tmem_cols);
+    if (warp == 1) as::tmem_alloc(tmem_slot, 2 * C::tmem_cols);
     as::tc_fence_before();
     __syncthreads();
     as::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // TMA producer
+        // TMA producer: every k step of every tile of this CTA through the ring
         as::prefetch_map(&p.a_hi);
         as::prefetch_map(&p.a_lo);
         as::prefetch_map(&p.b_hi);
         as::prefetch_map(&p.b_lo);
-        int issued = 0;
-        for (int k = 0; k < nk; k++) {
-            const int s = k % C::stages;
-            if (k >= C::stages && !as::mbar_wait(&empty[s], ((k / C::stages) & 1) ^ 1, abort)) {
-                gemm_fail(p.err, abort, 11);
-                break;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+            const int mt = tile % m_tiles, nt = (tile / m_tiles) % n_tiles, z = tile / (m_tiles * n_tiles);
+            const int ks0 = z * p.ksteps, nk = min(p.ksteps, ksteps_total - ks0);
+            for (int k = 0; k < nk; k++, it++) {
+                const int s = it % C::stages;
+                if (it >= C::stages && !as::mbar_wait(&empty[s], ((it / C::stages) & 1) ^ 1, abort)) {
+                    gemm_fail(p.err, abort, 11);
+                    break;
+                }
+                uint8_t *st = smem + s * C::stage_bytes;
+                as::mbar_expect_tx(&full[s], C::stage_bytes);
+                const int kc = (ks0 + k) * kBK;
+                as::tma_load_2d(st, &p.a_hi, kc, mt * kBM, &full[s]);
+                as::tma_load_2d(st + kABytes, &p.a_lo, kc, mt * kBM, &full[s]);
+                as::tma_load_2d(st + 2 * kABytes, &p.b_hi, kc, nt * BN, &full[s]);
+                as::tma_load_2d(st + 2 * kABytes + C::b_bytes, &p.b_lo, kc, nt * BN, &full[s]);
             }
-            uint8_t *st = smem + s * C::stage_bytes;
-            as::mbar_expect_tx(&full[s], C::stage_bytes);
-            const int kc = (ks0 + k) * kBK;
-            as::tma_load_2d(st, &p.a_hi, kc, m0, &full[s]);
-            as::tma_load_2d(st + kABytes, &p.a_lo, kc, m0, &full[s]);
-            as::tma_load_2d(st + 2 * kABytes, &p.b_hi, kc, n0, &full[s]);
-            as::tma_load_2d(st + 2 * kABytes + C::b_bytes, &p.b_lo, kc, n0, &full[s]);
-            issued++;
         }
         if (*abort) {
             // let the copies already in flight land before the CTA can exit
-            const int first = issued > C::stages ? issued - C::stages : 0;
-            for (int k = first; k < issued; k++) {
+            const int first = it > C::stages ? it - C::stages : 0;
+            for (int k = first; k < it; k++) {
                 const volatile int never = 0;
                 as::mbar_wait(&full[k % C::stages], (k / C::stages) & 1, &never);
             }
@@ -94,58 +105,81 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_bf16x3(const __grid_consta
     } else if (warp == 1 && lane == 0) {
         // MMA issuer
         constexpr uint32_t idesc = as::idesc_bf16_f32(kBM, BN);
-        for (int k = 0; k < nk; k++) {
-            const int s = k % C::stages;
-            if (!as::mbar_wait(&full[s], (k / C::stages) & 1, abort)) {
-                gemm_fail(p.err, abort, 12);
+        int it = 0, local = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
+            const int z = tile / (m_tiles * n_tiles);
+            const int nk = min(p.ksteps, ksteps_total - z * p.ksteps);
+            const int buf = local & 1;
+            if (local >= 2 && !as::mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, abort)) {
+                gemm_fail(p.err, abort, 14);
                 break;
             }
             as::tc_fence_after();
-            const uint32_t a_hi = as::smem_u32(smem + s * C::stage_bytes);
-            const uint32_t a_lo = a_hi + kABytes, b_hi = a_hi + 2 * kABytes, b_lo = b_hi + C::b_bytes;
+            const uint32_t acc = tmem + (uint32_t)(buf * C::tmem_cols);
+            for (int k = 0; k < nk; k++, it++) {
+                const int s = it % C::stages;
+                if (!as::mbar_wait(&full[s], (it / C::stages) & 1, abort)) {
+                    gemm_fail(p.err, abort, 12);
+                    break;
+                }
+                as::tc_fence_after();
+                const uint32_t a_hi = as::smem_u32(smem + s * C::stage_bytes);
+                const uint32_t a_lo = a_hi + kABytes, b_hi = a_hi + 2 * kABytes, b_lo = b_hi + C::b_bytes;
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; kk++) {
-                const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzled row
-                as::mma_bf16(tmem, as::sw128_desc(a_hi + off), as::sw128_desc(b_hi + off), idesc, k > 0 || kk > 0);
-                as::mma_bf16(tmem, as::sw128_desc(a_hi + off), as::sw128_desc(b_lo + off), idesc, true);
-                as::mma_bf16(tmem, as::sw128_desc(a_lo + off), as::sw128_desc(b_hi + off), idesc, true);
+                for (int kk = 0; kk < kBK / 16; kk++) {
+                    const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzled row
+                    as::mma_bf16(acc, as::sw128_desc(a_hi + off), as::sw128_desc(b_hi + off), idesc, k > 0 || kk > 0);
+                    as::mma_bf16(acc, as::sw128_desc(a_hi + off), as::sw128_desc(b_lo + off), idesc, true);
+                    as::mma_bf16(acc, as::sw128_desc(a_lo + off), as::sw128_desc(b_hi + off), idesc, true);
+                }
+                as::mma_commit(&empty[s]);
             }
-            as::mma_commit(&empty[s]);
+            as::mma_commit(&acc_full[buf]);
         }
-        as::mma_commit(accum);
         if (*abort) {
+            // every issued MMA has finished with shared memory and TMEM
+            as::mma_commit(drain);
             const volatile int never = 0;
-            as::mbar_wait(accum, 0, &never);  // every issued MMA has finished with TMEM
+            as::mbar_wait(drain, 0, &never);
         }
     } else if (warp >= 2) {
         // epilogue: TMEM lanes (warp % 4) * 32 .. +31 are weight rows of this warp
         const int q = warp & 3;
-        const bool waited = as::mbar_wait(accum, 0, abort);
-        as::tc_fence_after();
-        // tcgen05.ld is warp-collective: take the decision for the whole warp
-        const bool ok = __all_sync(0xffffffffu, waited && !*abort);
-        if (!waited) gemm_fail(p.err, abort, 13);
-        if (ok) {
-            const int m = m0 + q * 32 + lane;
-            float *d = p.d + (long long)blockIdx.z * p.split_stride + m;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, local++) {
+            const int mt = tile % m_tiles, nt = (tile / m_tiles) % n_tiles, z = tile / (m_tiles * n_tiles);
+            const int buf = local & 1;
+            const bool waited = as::mbar_wait(&acc_full[buf], (local >> 1) & 1, abort);
+            as::tc_fence_after();
+            const bool ok = __all_sync(0xffffffffu, waited && !*abort);
+            if (!ok) {
+                if (!waited) gemm_fail(p.err, abort, 13);
+                break;
+            }
+            const int n0 = nt * BN;
+            const int m = mt * kBM + q * 32 + lane;
+            float *d = p.d + (long long)z * p.split_stride + m;
             const int n_end = min(BN, p.N - n0);
+            const uint32_t acc = tmem + (uint32_t)(buf * C::tmem_cols) + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 16) {
                 if (c >= n_end) break;
                 uint32_t r[16];
-                as::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+                as::tmem_ld16(acc + (uint32_t)c, r);
                 as::tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 16; j++)
                     if (c + j < n_end) d[(long long)(n0 + c + j) * p.ldd] = __uint_as_float(r[j]);
             }
+            as::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) as::mbar_arrive(&acc_empty[buf]);
         }
-        as::tc_fence_before();
     }
     __syncthreads();
     if (warp == 1) {
         as::tc_fence_after();
-        as::tmem_free(tmem, C::tmem_cols);
+        as::tmem_free(tmem, 2 * C::tmem_cols);
     }
 }
 
@@ -244,7 +278,8 @@ Split gemm_split(const Gemm &g, int n)
 {
     const int ksteps = g.p.K / kBK;
     const int tiles = (g.p.M / kBM) * ((n + g.bn - 1) / g.bn);
-    int splits = g.fixed_splits > 0 ? g.fixed_splits : (2 * kSMs + tiles - 1) / tiles;
+    // persistent CTAs: one wave of tiles is enough, more splits only add partial traffic
+    int splits = g.fixed_splits > 0 ? g.fixed_splits : (kSMs + tiles - 1) / tiles;
     splits = splits < 1 ? 1 : (splits > ksteps ? ksteps : splits);
     const int per = (ksteps + splits - 1) / splits;
     return Split{(ksteps + per - 1) / per, (long long)n * g.p.ldd};
@@ -274,11 +309,13 @@ int gemm_launch(const Gemm &g, int n, cudaStream_t s, Split *used)
     p.ksteps = (ksteps + sp.splits - 1) / sp.splits;
     p.split_stride = sp.split_stride;
     if (used) *used = sp;
-    const dim3 grid(p.M / kBM, (n + g.bn - 1) / g.bn, sp.splits);
+    const int m_tiles = p.M / kBM, n_tiles = (n + g.bn - 1) / g.bn;
+    const int tiles = m_tiles * n_tiles * sp.splits;
+    const int grid = tiles < kSMs ? tiles : kSMs;
     if (g.bn == 64)
-        k_gemm_bf16x3<64><<<grid, kThreads, g.smem, s>>>(p);
+        k_gemm_bf16x3<64><<<grid, kThreads, g.smem, s>>>(p, m_tiles, n_tiles, tiles);
     else
-        k_gemm_bf16x3<128><<<grid, kThreads, g.smem, s>>>(p);
+        k_gemm_bf16x3<128><<<grid, kThreads, g.smem, s>>>(p, m_tiles, n_tiles, tiles);
     MB_CHECK(cudaGetLastError());
     return 0;
 }
