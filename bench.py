@@ -32,6 +32,7 @@ PROMPT_LEN, NEW_TOKENS, PROMPT_SEED, MODEL_SEED = 34, 256, 7, 1
 WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per token
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 REF_SAMPLE_TOKENS = 32
+TRAFFIC_PER_TOKEN = 530_606_336  # DRAM read + write per k_step launch (526.93 + 3.67 MB), ncu, position 34
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
@@ -199,7 +200,7 @@ def peak_tflops():
     return 1590.0, "fallback"
 
 
-def bench_batched(group, data, args):
+def bench_batched(group, data, args, parts):
     """Prefill of one 1024-token prompt and the batched serving job on this rank's
     share of the 512 sequences (tcgen05 GEMM path)."""
     import numpy as np
@@ -208,14 +209,18 @@ def bench_batched(group, data, args):
     rank, world, local = group.rank, group.world, group.local
     h = mocha_native.Q8BatchHandle(local, data, max_rows=SERVE_BATCH * SERVE_PROMPT, slots=SERVE_BATCH)
     group.barrier()
-    pre_ms = h.bench_prefill(PREFILL_LEN, 1234 + rank, args.warmup, args.steps)
+    pre_ms = h.bench_prefill(PREFILL_LEN, 1234 + rank, args.warmup, args.steps) if "prefill" in parts else 0.0
+    if "batched" not in parts:
+        h.close()
+        return {"prefill_ms": pre_ms, "decode_s": 0.0, "prefill_s": 0.0, "generated": 0, "nseq": 0, "wall": 0.0,
+                "launches": 0}
     # batched serving: sequences i with i % world == rank
-    mine = [i for i in range(SERVE_SEQS) if i % world == rank]
-    prompts = np.random.default_rng(2024).integers(0, 151936, (SERVE_SEQS, SERVE_PROMPT))[mine]
+    mine = [i for i in range(args.serve_seqs) if i % world == rank]
+    prompts = np.random.default_rng(2024).integers(0, 151936, (args.serve_seqs, SERVE_PROMPT))[mine]
     h.generate(prompts[:SERVE_BATCH], 8, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
     group.barrier()
     t0 = time.perf_counter()
-    toks, t = h.generate(prompts, SERVE_NEW, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
+    toks, t = h.generate(prompts, args.serve_new, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
     wall = time.perf_counter() - t0
     launches = h.launches_per_step()
     h.close()
@@ -223,41 +228,40 @@ def bench_batched(group, data, args):
             "nseq": len(mine), "wall": wall, "launches": launches}
 
 
-def batched_objects(gathered, args, world):
+def prefill_object(gathered, args, world):
     tf_peak, tf_kind = peak_tflops()
-    hbm_peak, hbm_kind = peaks()
     pre_ms = max(g["prefill_ms"] for g in gathered) / args.steps
-    prefill_tps = PREFILL_LEN * world / (pre_ms / 1e3)
     achieved_tf = PREFILL_FLOP / (pre_ms / 1e3) / 1e12
-    prefill = {"value": prefill_tps, "unit": "tok/s", "ms_per_prompt": pre_ms,
-               "config": {"workload": "one 1024-token prompt of uniform random ids, head on the last position",
-                          "per_gpu": True},
-               "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s",
-                            "frac": achieved_tf / tf_peak, "peak_kind": tf_kind,
-                            "algorithmic_flop_per_prompt": PREFILL_FLOP,
-                            "note": "bf16 hi/lo split: the tensor pipe issues 3x the layer-GEMM FLOPs"}}
+    return {"value": PREFILL_LEN * world / (pre_ms / 1e3), "unit": "tok/s", "ms_per_prompt": pre_ms,
+            "config": {"workload": "one 1024-token prompt of uniform random ids per GPU, head on the last position"},
+            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": achieved_tf / tf_peak, "peak_kind": tf_kind,
+                         "algorithmic_flop_per_prompt": PREFILL_FLOP,
+                         "note": "bf16 hi/lo split: the tensor pipe issues 3x the layer-GEMM FLOPs"}}
+
+
+def batched_object(gathered, args, world):
+    hbm_peak, hbm_kind = peaks()
     decode_s = max(g["decode_s"] for g in gathered)
     wall = max(g["wall"] for g in gathered)
     gen = sum(g["generated"] for g in gathered)
     first = sum(g["nseq"] for g in gathered)
-    decode_tps = (gen - first) / decode_s
     # per GPU and decode step: weights once + the KV of 64 sequences at mean position
-    steps_per_gpu = (SERVE_NEW - 1) * ((SERVE_SEQS // world + SERVE_BATCH - 1) // SERVE_BATCH)
-    mean_pos1 = (SERVE_PROMPT + 1 + SERVE_PROMPT + SERVE_NEW - 1) / 2
+    steps_per_gpu = (args.serve_new - 1) * ((args.serve_seqs // world + SERVE_BATCH - 1) // SERVE_BATCH)
+    mean_pos1 = (SERVE_PROMPT + 1 + SERVE_PROMPT + args.serve_new - 1) / 2
     step_bytes = WEIGHT_BYTES + SERVE_BATCH * KV_BYTES_PER_POS * mean_pos1
     achieved = step_bytes * steps_per_gpu / decode_s / 1e9
-    batched = {"value": decode_tps, "unit": "tok/s", "decode_s": decode_s,
-               "e2e": {"value": gen / wall, "unit": "tok/s", "path": "mocha_q8b_generate (prompt pass included)"},
-               "config": {"workload": "512 sequences x (128-token prompt + 384 generated), T=0.7 top-k 40 "
-                                      "top-p 0.9 penalty 1.12, 64 per GPU per wave",
-                          "parallelism": f"replicas x{world}", "scaling": "strong (512 sequences in total)"},
-               "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                            "frac": achieved / hbm_peak, "peak_kind": hbm_kind,
-                            "algorithmic_bytes_per_step": step_bytes,
-                            "note": "weights counted in the reference format (int8 + fp32 scales); this path "
-                                    "streams bf16 hi/lo copies, 4 B per weight"},
-               "gpu_launches_per_step": gathered[0]["launches"]}
-    return prefill, batched
+    return {"value": (gen - first) / decode_s, "unit": "tok/s", "decode_s": decode_s,
+            "e2e": {"value": gen / wall, "unit": "tok/s", "path": "mocha_q8b_generate (prompt pass included)"},
+            "config": {"workload": f"{args.serve_seqs} sequences x (128-token prompt + {args.serve_new} generated), "
+                                   "T=0.7 top-k 40 top-p 0.9 penalty 1.12, 64 per GPU per wave",
+                       "parallelism": f"replicas x{world}", "scaling": f"strong ({args.serve_seqs} sequences in total)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": hbm_kind,
+                         "algorithmic_bytes_per_step": step_bytes,
+                         "note": "weights counted in the reference format (int8 + fp32 scales); this path "
+                                 "streams bf16 hi/lo copies, 4 B per weight"},
+            "gpu_launches_per_step": gathered[0]["launches"]}
 
 
 def cpu_baseline(model_path, prompt):
@@ -287,6 +291,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the prefill and batched-serving objects")
+    ap.add_argument("--serve-seqs", type=int, default=SERVE_SEQS, help="batched job size (smaller for profiling)")
+    ap.add_argument("--serve-new", type=int, default=SERVE_NEW, help="tokens per sequence of the batched job")
+    ap.add_argument("--parts", default="decode,prefill,batched",
+                    help="comma list of workloads to run (profiling runs select one); the default runs all three")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -300,62 +308,72 @@ def main():
     group = Group()
     rank, world, local = group.rank, group.world, group.local
     path, data = model_bytes(group)
+    parts = set(args.parts.split(","))
     prompt = mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED + rank)
-    h = mocha_native.Q8Handle(local, data)
-    # fill the KV cache for the prompt and take its first token
-    first, _ = h.generate(prompt, 1)
-    tok = first[0] if first else prompt[-1]
     pos0, pos_end = PROMPT_LEN - 1, PROMPT_LEN - 1 + NEW_TOKENS
-    group.barrier()
-    with Clocks(local) as clk:
-        ms = h.bench_decode(tok, pos0, pos_end, args.warmup * NEW_TOKENS, args.steps * NEW_TOKENS)
-    clocks = clk.summary()
-    group.barrier()
-    # end to end through the public C ABI with host buffers
-    e2e_wall = 0.0
-    h.generate(prompt, NEW_TOKENS)
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        toks, t = h.generate(prompt, NEW_TOKENS)
-        e2e_wall += time.perf_counter() - t0
-    launches = mocha_native.load().mocha_q8_launches_per_step(h.h) * NEW_TOKENS * args.steps
-    h.close()
-    extra = {} if args.no_batched else bench_batched(group, data, args)
+    ms, e2e_wall, clocks, launches = 0.0, 0.0, None, 0
+    if "decode" in parts:
+        h = mocha_native.Q8Handle(local, data)
+        # fill the KV cache for the prompt and take its first token
+        first, _ = h.generate(prompt, 1)
+        tok = first[0] if first else prompt[-1]
+        group.barrier()
+        with Clocks(local) as clk:
+            ms = h.bench_decode(tok, pos0, pos_end, args.warmup * NEW_TOKENS, args.steps * NEW_TOKENS)
+        clocks = clk.summary()
+        group.barrier()
+        # end to end through the public C ABI with host buffers
+        h.generate(prompt, NEW_TOKENS)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            toks, t = h.generate(prompt, NEW_TOKENS)
+            e2e_wall += time.perf_counter() - t0
+        launches = mocha_native.load().mocha_q8_launches_per_step(h.h) * NEW_TOKENS * args.steps
+        h.close()
+    run_batched = not args.no_batched and bool(parts & {"prefill", "batched"})
+    extra = bench_batched(group, data, args, parts) if run_batched else {}
     gathered = group.gather({"ms": ms, "e2e": e2e_wall, "clocks": clocks, **extra})
     if rank != 0:
         group.close()
         return 0
-    ms_max = max(g["ms"] for g in gathered)
-    e2e_max = max(g["e2e"] for g in gathered)
-    total_tokens = NEW_TOKENS * args.steps * world
-    value = total_tokens / (ms_max / 1e3)
-    e2e = NEW_TOKENS * args.steps * world / e2e_max
-    per_token_s = ms_max / 1e3 / (NEW_TOKENS * args.steps)
-    mean_pos1 = (pos0 + 1 + pos_end) / 2
-    algo = WEIGHT_BYTES + KV_BYTES_PER_POS * mean_pos1
-    peak, peak_kind = peaks()
-    achieved = algo / per_token_s / 1e9
-    out = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": value / PUBLISHED_TOKS, "dtype": "f32",
-        "data": "synthetic: random-init weights N(0,0.02) (seed 1), group-64 int8; 34 random prompt ids per rank",
-        "config": {"workload": "Qwen2.5-0.5B grouped-Q8 b=1 greedy decode: 34-token prompt, 256 generated "
-                               "(positions 33..288), one step = one 256-token decode",
-                   "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS, "parallelism": f"replicas x{world}",
-                   "l2": "weights (525 MB) exceed the 126 MB L2; no flush needed"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "whole decode step (one CUDA graph per token)",
-                     "algorithmic_bytes_per_launch": algo, "peak_kind": peak_kind},
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT_LEN * 4 + 32,
-                "d2h_bytes_per_step": NEW_TOKENS * 4,
-                "path": "mocha_q8_generate (C ABI, host prompt in / host tokens out), prompt pass included"},
-        "gpu_launches": launches * world,
-        "clocks": gathered[0]["clocks"],
-    }
-    if not args.no_batched:
-        out["prefill"], out["batched"] = batched_objects(gathered, args, world)
-    if not args.no_cpu_baseline:
+    out = {"metric": METRIC, "value": None, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "parts": sorted(parts)}
+    if "decode" in parts:
+        ms_max = max(g["ms"] for g in gathered)
+        e2e_max = max(g["e2e"] for g in gathered)
+        total_tokens = NEW_TOKENS * args.steps * world
+        value = total_tokens / (ms_max / 1e3)
+        e2e = NEW_TOKENS * args.steps * world / e2e_max
+        per_token_s = ms_max / 1e3 / (NEW_TOKENS * args.steps)
+        mean_pos1 = (pos0 + 1 + pos_end) / 2
+        algo = WEIGHT_BYTES + KV_BYTES_PER_POS * mean_pos1
+        peak, peak_kind = peaks()
+        achieved = algo / per_token_s / 1e9
+        out.update({
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_TOKS, "dtype": "f32",
+            "data": "synthetic: random-init weights N(0,0.02) (seed 1), group-64 int8; 34 random prompt ids per rank",
+            "config": {"workload": "Qwen2.5-0.5B grouped-Q8 b=1 greedy decode: 34-token prompt, 256 generated "
+                                   "(positions 33..288), one step = one 256-token decode",
+                       "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "weights (525 MB) exceed the 126 MB L2; no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": TRAFFIC_PER_TOKEN,
+                         "kernel": "k_step: one persistent cooperative launch per token",
+                         "algorithmic_bytes_per_launch": algo, "peak_kind": peak_kind},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT_LEN * 4 + 32,
+                    "d2h_bytes_per_step": NEW_TOKENS * 4,
+                    "path": "mocha_q8_generate (C ABI, host prompt in / host tokens out), prompt pass included"},
+            "gpu_launches": launches * world,
+            "clocks": gathered[0]["clocks"],
+        })
+    if run_batched and "prefill" in parts:
+        out["prefill"] = prefill_object(gathered, args, world)
+    if run_batched and "batched" in parts:
+        out["batched"] = batched_object(gathered, args, world)
+    if not args.no_cpu_baseline and "decode" in parts:
         out["cpu_baseline"] = cpu_baseline(path, mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED))
     print(json.dumps(out))
     group.close()
