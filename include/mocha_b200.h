@@ -169,6 +169,12 @@ int mocha_q8b_sample_check(mocha_q8b *h, int n, const float *logits, const int *
 int mocha_tc_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
                         const float *x, float *y, int splits);
 
+/* The same product through the int8 tcgen05 GEMM of the batched engine: x split into
+ * three int8 limbs per 64-group, exact int32 group sums, fp32 promotion.
+ * rows % 128 == 0, cols % 128 == 0, 1 <= n <= 1024.  No reference counterpart. */
+int mocha_tq_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
+                        const float *x, float *y, int splits);
+
 #ifdef __cplusplus
 }
 #endif

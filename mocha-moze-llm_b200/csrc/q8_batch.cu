@@ -35,12 +35,13 @@
 #include "sampling.cuh"
 #include "sampling_dev.cuh"
 #include "tc_gemm.cuh"
+#include "tc_q8gemm.cuh"
 
 namespace qb {
 
 using namespace q8;
 using bf16 = __nv_bfloat16;
-using mb::tc::Gemm;
+using mb::tq::Gemm;
 
 constexpr int QKV_ROWS = DIM + 2 * KV;  // q | k | v output rows of the fused projection
 constexpr int GU_ROWS = 2 * HIDDEN;     // gate | up
@@ -65,23 +66,30 @@ struct Rows {
 
 // ---- row kernels ----------------------------------------------------------------------
 
-// y = x * rsqrt-style scale * gain, split into a bf16 pair, written to row `dst`.
-MB_DEV void norm_store(const float (&v)[4], float *red, const float *__restrict__ gain, bf16 *hi, bf16 *lo, int dst)
+// Limbs of a DIM-wide GEMM input: int8 [rows * 3][DIM] and group scales [rows][DIM/64].
+struct Limbs {
+    int8_t *q;
+    float *s;
+};
+
+// y = x * (1/sqrt(sum x^2 / DIM + eps)) * gain, stored as int8 limbs of row `dst`
+// (16 lanes hold one 64-group).
+MB_DEV void norm_store(const float (&v)[4], float *red, const float *__restrict__ gain, Limbs out, int dst)
 {
     const float ss = mb::block_sum<NT>(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3], red);
     if (dst < 0) return;
     const float s = 1.f / sqrtf(ss / DIM + RMS_EPS);
     const int i0 = threadIdx.x * 4;
+    float y[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const float y = v[j] * s * __ldg(gain + i0 + j);
-        mb::tc::split_bf16(y, hi[(size_t)dst * DIM + i0 + j], lo[(size_t)dst * DIM + i0 + j]);
-    }
+    for (int j = 0; j < 4; j++) y[j] = v[j] * s * __ldg(gain + i0 + j);
+    mb::tq::store_limbs<4, 16>(y, out.q + (size_t)dst * 3 * DIM, DIM, i0, out.s + (size_t)dst * (DIM / GROUP) + i0 / GROUP,
+                               threadIdx.x & 15);
 }
 
 // x[t] = dequant(embed[tok[t]]); xn[t] = split(rms(x[t]) * gain)
 __global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const float *__restrict__ gain, float *x,
-                                                   bf16 *xh, bf16 *xl)
+                                                   Limbs out)
 {
     __shared__ float red[32];
     const int t = blockIdx.x, i0 = threadIdx.x * 4;
@@ -90,13 +98,13 @@ __global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const f
     const float sc = embed.s[((size_t)token * DIM + i0) / GROUP];
     const float v[4] = {c.x * sc, c.y * sc, c.z * sc, c.w * sc};
     *reinterpret_cast<float4 *>(x + (size_t)t * DIM + i0) = make_float4(v[0], v[1], v[2], v[3]);
-    norm_store(v, red, gain, xh, xl, t);
+    norm_store(v, red, gain, out, t);
 }
 
 // x[t] += sum_s part[s][t]; then the norm of the new x into row dst_row[t] (or t).
 __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__restrict__ part, int splits,
-                                                      long long sstride, const float *__restrict__ gain, bf16 *hi,
-                                                      bf16 *lo, const int *__restrict__ dst_row)
+                                                      long long sstride, const float *__restrict__ gain, Limbs out,
+                                                      const int *__restrict__ dst_row)
 {
     __shared__ float red[32];
     const int t = blockIdx.x, i0 = threadIdx.x * 4;
@@ -112,7 +120,7 @@ __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__r
     const float4 xv = *xp;
     const float v[4] = {xv.x + acc.x, xv.y + acc.y, xv.z + acc.z, xv.w + acc.w};
     *xp = make_float4(v[0], v[1], v[2], v[3]);
-    norm_store(v, red, gain, hi, lo, dst_row ? dst_row[t] : t);
+    norm_store(v, red, gain, out, dst_row ? dst_row[t] : t);
 }
 
 // q/k/v = sum of partials + bias; split-half RoPE on q and k; q (times 0.125) to the
@@ -228,28 +236,31 @@ __global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q,
     }
 }
 
-// Combine the chunks of one (row, head) into the attention output, split for the O GEMM.
-__global__ void __launch_bounds__(HEAD_DIM) k_attn_combine(const float *__restrict__ part, Rows rows, bf16 *ah, bf16 *al)
+// Combine the chunks of one (row, head) into the attention output, as limbs for the O
+// GEMM (one warp, two dims per lane: the head is one 64-group).
+__global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out)
 {
-    const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+    const int h = blockIdx.x, t = blockIdx.y, d = 2 * threadIdx.x;
     const int nc = rows.pos[t] / CHUNK + 1;
     const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
     float m = -INFINITY;
     for (int c = 0; c < nc; c++) m = fmaxf(m, p[c * PART]);
-    float l = 0.f, acc = 0.f;
+    float l = 0.f, a0 = 0.f, a1 = 0.f;
     for (int c = 0; c < nc; c++) {
         const float w = expf(p[c * PART] - m);
         l += p[c * PART + 1] * w;
-        acc += p[c * PART + 2 + d] * w;
+        a0 += p[c * PART + 2 + d] * w;
+        a1 += p[c * PART + 3 + d] * w;
     }
-    const size_t o = (size_t)t * DIM + h * HEAD_DIM + d;
-    mb::tc::split_bf16(acc / l, ah[o], al[o]);
+    const float v[2] = {a0 / l, a1 / l};
+    mb::tq::store_limbs<2, 32>(v, out.q + (size_t)t * 3 * DIM, DIM, h * HEAD_DIM + d,
+                               out.s + (size_t)t * (DIM / GROUP) + h, threadIdx.x);
 }
 
-// h = silu(gate) * up from the gate|up partials, split for the down GEMM; two
+// h = silu(gate) * up from the gate|up partials, as limbs for the down GEMM; two
 // features per thread.  grid (ceil(HIDDEN / 512), rows)
-__global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride, bf16 *hh,
-                                                bf16 *hl)
+__global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride,
+                                                int8_t *hq, float *hs)
 {
     const int t = blockIdx.y, i = (blockIdx.x * 256 + threadIdx.x) * 2;
     if (i >= HIDDEN) return;
@@ -263,12 +274,10 @@ __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, 
         u.x += us.x;
         u.y += us.y;
     }
-    const float h0 = (g.x / (1.f + expf(-g.x))) * u.x, h1 = (g.y / (1.f + expf(-g.y))) * u.y;
-    __nv_bfloat162 hi, lo;
-    mb::tc::split_bf16(h0, hi.x, lo.x);
-    mb::tc::split_bf16(h1, hi.y, lo.y);
-    *reinterpret_cast<__nv_bfloat162 *>(hh + (size_t)t * HIDDEN + i) = hi;
-    *reinterpret_cast<__nv_bfloat162 *>(hl + (size_t)t * HIDDEN + i) = lo;
+    const float hv[2] = {(g.x / (1.f + expf(-g.x))) * u.x, (g.y / (1.f + expf(-g.y))) * u.y};
+    // a warp holds 64 consecutive features: one group of the down projection's input
+    mb::tq::store_limbs<2, 32>(hv, hq + (size_t)t * 3 * HIDDEN, HIDDEN, i,
+                               hs + (size_t)t * (HIDDEN / GROUP) + i / GROUP, threadIdx.x & 31);
 }
 
 // Prompt attention for a block of 64 consecutive rows of one slot (positions
@@ -282,7 +291,7 @@ constexpr size_t QB_SMEM = sizeof(float) * (3 * QB * QB_LD + CHUNK * HEAD_DIM);
 
 __global__ void __launch_bounds__(256) k_attn_block(const float *__restrict__ q, Rows rows,
                                                     const float *__restrict__ kc, const float *__restrict__ vc,
-                                                    int layer, bf16 *ah, bf16 *al)
+                                                    int layer, Limbs out)
 {
     extern __shared__ float4 smem4[];
     float *sQ = reinterpret_cast<float *>(smem4);
@@ -388,10 +397,12 @@ __global__ void __launch_bounds__(256) k_attn_block(const float *__restrict__ q,
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const size_t o = (size_t)(t0 + ty + 16 * i) * DIM + h * HEAD_DIM + tx * 4;
+        const int row = t0 + ty + 16 * i;
         const float inv = 1.f / l[i];
-#pragma unroll
-        for (int j = 0; j < 4; j++) mb::tc::split_bf16(acc[i][j] * inv, ah[o + j], al[o + j]);
+        const float v[4] = {acc[i][0] * inv, acc[i][1] * inv, acc[i][2] * inv, acc[i][3] * inv};
+        // the 16 lanes of one ty hold the head's 64 dims: one group
+        mb::tq::store_limbs<4, 16>(v, out.q + (size_t)row * 3 * DIM, DIM, h * HEAD_DIM + tx * 4,
+                                   out.s + (size_t)row * (DIM / GROUP) + h, tx);
     }
 }
 
@@ -617,8 +628,12 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned lon
 
 // ---- engine -------------------------------------------------------------------------
 
+// A grouped-Q8 matrix for the int8 GEMM: int8 [rows][cols] and fp32 scales [rows][cols/64].
 struct Weights {
-    bf16 *hi = nullptr, *lo = nullptr;
+    const int8_t *q = nullptr;
+    const float *s = nullptr;
+    int8_t *own_q = nullptr;  // device copies owned by the handle (fused matrices)
+    float *own_s = nullptr;
 };
 
 struct PlanSet {
@@ -635,8 +650,9 @@ struct mocha_q8b {
     qb::Weights w_qkv[q8::LAYERS], w_o[q8::LAYERS], w_gu[q8::LAYERS], w_down[q8::LAYERS], w_head;
     float *bqkv = nullptr;  // [LAYERS][1152]
     float *x = nullptr, *q = nullptr, *part = nullptr, *apart = nullptr, *logits = nullptr;
-    __nv_bfloat16 *xh = nullptr, *xl = nullptr, *ah = nullptr, *al = nullptr, *hh = nullptr, *hl = nullptr;
-    __nv_bfloat16 *headh = nullptr, *headl = nullptr;
+    qb::Limbs lx{}, la{}, lhead{};  // GEMM inputs: normed x, attention output, head rows
+    int8_t *lhq = nullptr;          // SwiGLU output limbs [rows * 3][HIDDEN]
+    float *lhs = nullptr;           // and their scales [rows][HIDDEN / 64]
     float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     int *tok = nullptr, *pos = nullptr, *slot = nullptr;            // prompt rows [max_rows]
     int *ntok = nullptr, *npos = nullptr, *nslot = nullptr;         // decode rows [slots]
@@ -648,7 +664,7 @@ struct mocha_q8b {
     int *out_tokens = nullptr, *out_count = nullptr;
     int out_stride = 0;
     qb::PlanSet pre, dec;
-    mb::tc::Gemm head;
+    mb::tq::Gemm head;
     cudaGraphExec_t g_step = nullptr;
     int g_step_n = 0;
     cudaEvent_t ev[4] = {};
@@ -678,29 +694,37 @@ int dalloc(T **p, size_t count)
     return 0;
 }
 
-int alloc_pair(Weights &w, size_t count)
+// Fuse matrices along their rows into a device copy owned by `w` (int8 rows and fp32
+// scales back to back, in the order given).
+int fuse(mocha_q8b *h, Weights &w, std::initializer_list<std::pair<Mat, int>> parts, int cols)
 {
-    if (dalloc(&w.hi, count) || dalloc(&w.lo, count)) return 1;
+    size_t rows = 0;
+    for (auto &pr : parts) rows += (size_t)pr.second;
+    if (dalloc(&w.own_q, rows * cols) || dalloc(&w.own_s, rows * (cols / GROUP))) return 1;
+    size_t r0 = 0;
+    for (auto &pr : parts) {
+        QB_TRY(cudaMemcpyAsync(w.own_q + r0 * cols, pr.first.w, (size_t)pr.second * cols, cudaMemcpyDeviceToDevice,
+                               h->stream));
+        QB_TRY(cudaMemcpyAsync(w.own_s + r0 * (cols / GROUP), pr.first.s, sizeof(float) * pr.second * (cols / GROUP),
+                               cudaMemcpyDeviceToDevice, h->stream));
+        r0 += (size_t)pr.second;
+    }
+    w.q = w.own_q;
+    w.s = w.own_s;
     return 0;
-}
-
-// Split rows [0, rows) of a grouped-Q8 matrix into rows [row0, row0+rows) of a pair.
-int split_into(mocha_q8b *h, const Mat &m, size_t rows, size_t cols, Weights &w, size_t row0)
-{
-    return mb::tc::split_weights(m.w, m.s, rows * cols, w.hi + row0 * cols, w.lo + row0 * cols, h->stream);
 }
 
 int plan_set(mocha_q8b *h, PlanSet &ps, int n_max)
 {
     for (int l = 0; l < LAYERS; l++) {
-        if (mb::tc::gemm_plan(&ps.qkv[l], h->w_qkv[l].hi, h->w_qkv[l].lo, QKV_ROWS, DIM, h->xh, h->xl, n_max, h->part,
-                              QKV_ROWS, 0, h->err) ||
-            mb::tc::gemm_plan(&ps.o[l], h->w_o[l].hi, h->w_o[l].lo, DIM, DIM, h->ah, h->al, n_max, h->part, DIM, 0,
-                              h->err) ||
-            mb::tc::gemm_plan(&ps.gu[l], h->w_gu[l].hi, h->w_gu[l].lo, GU_ROWS, DIM, h->xh, h->xl, n_max, h->part,
-                              GU_ROWS, 0, h->err) ||
-            mb::tc::gemm_plan(&ps.down[l], h->w_down[l].hi, h->w_down[l].lo, DIM, HIDDEN, h->hh, h->hl, n_max,
-                              h->part, DIM, 0, h->err))
+        if (mb::tq::plan(&ps.qkv[l], h->w_qkv[l].q, h->w_qkv[l].s, QKV_ROWS, DIM, h->lx.q, h->lx.s, n_max, h->part,
+                         QKV_ROWS, 0, h->err) ||
+            mb::tq::plan(&ps.o[l], h->w_o[l].q, h->w_o[l].s, DIM, DIM, h->la.q, h->la.s, n_max, h->part, DIM, 0,
+                         h->err) ||
+            mb::tq::plan(&ps.gu[l], h->w_gu[l].q, h->w_gu[l].s, GU_ROWS, DIM, h->lx.q, h->lx.s, n_max, h->part,
+                         GU_ROWS, 0, h->err) ||
+            mb::tq::plan(&ps.down[l], h->w_down[l].q, h->w_down[l].s, DIM, HIDDEN, h->lhq, h->lhs, n_max, h->part,
+                         DIM, 0, h->err))
             return 1;
     }
     return 0;
@@ -711,7 +735,7 @@ size_t plan_floats(const PlanSet &ps)
     size_t m = 0;
     for (int l = 0; l < LAYERS; l++) {
         const Gemm *g[4] = {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]};
-        for (const Gemm *x : g) m = std::max(m, mb::tc::gemm_partial_floats(*x));
+        for (const Gemm *x : g) m = std::max(m, mb::tq::partial_floats(*x));
     }
     return m;
 }
@@ -727,11 +751,11 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, bool block)
             QB_TRY(cudaFuncSetAttribute(k_attn_block, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QB_SMEM));
             attr_done[h->device & 63] = true;
         }
-        k_attn_block<<<dim3(n / QB, HEADS), 256, QB_SMEM, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->ah, h->al);
+        k_attn_block<<<dim3(n / QB, HEADS), 256, QB_SMEM, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->la);
         return 0;
     }
     k_attn_chunk<<<dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->apart);
-    k_attn_combine<<<dim3(HEADS, n), HEAD_DIM, 0, h->stream>>>(h->apart, rows, h->ah, h->al);
+    k_attn_combine<<<dim3(HEADS, n), 32, 0, h->stream>>>(h->apart, rows, h->la);
     return 0;
 }
 
@@ -748,32 +772,31 @@ bool block_rows(int n, const int *pos, const int *slots)
 }
 
 // The whole transformer for rows [0, n) plus the head for `np` projected rows
-// (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of headh/headl).
+// (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of the head limbs).
 int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np,
                     bool block_attention)
 {
     const PlanSet &ps = decode_set ? h->dec : h->pre;
     cudaStream_t s = h->stream;
-    k_embed_norm<<<n, NT, 0, s>>>(h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->xh, h->xl);
+    k_embed_norm<<<n, NT, 0, s>>>(h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->lx);
     mb::tc::Split sp;
     for (int l = 0; l < LAYERS; l++) {
         const Layer &L = h->m.layer[l];
-        if (mb::tc::gemm_launch(ps.qkv[l], n, s, &sp)) return 1;
+        if (mb::tq::launch(ps.qkv[l], n, s, &sp)) return 1;
         k_qkv_post<<<n, QKV_THREADS, 0, s>>>(h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
                                               h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l);
         if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
-        if (mb::tc::gemm_launch(ps.o[l], n, s, &sp)) return 1;
-        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->xh, h->xl, nullptr);
-        if (mb::tc::gemm_launch(ps.gu[l], n, s, &sp)) return 1;
-        k_swiglu<<<dim3((HIDDEN + 511) / 512, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->hh, h->hl);
-        if (mb::tc::gemm_launch(ps.down[l], n, s, &sp)) return 1;
+        if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
+        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr);
+        if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;
+        k_swiglu<<<dim3((HIDDEN + 511) / 512, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->lhq, h->lhs);
+        if (mb::tq::launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
         k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride,
                                           last ? h->m.final_norm : h->m.layer[l + 1].attn_norm,
-                                          last ? h->headh : h->xh, last ? h->headl : h->xl,
-                                          last ? proj_dst : nullptr);
+                                          last ? h->lhead : h->lx, last ? proj_dst : nullptr);
     }
-    if (np > 0 && mb::tc::gemm_launch(h->head, np, s)) return 1;
+    if (np > 0 && mb::tq::launch(h->head, np, s)) return 1;
     QB_TRY(cudaGetLastError());
     return 0;
 }
@@ -903,27 +926,27 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
     if (cudaMemcpy(h->bqkv, bias.data(), sizeof(float) * bias.size(), cudaMemcpyHostToDevice) != cudaSuccess)
         return fail();
 
-    // bf16 pairs of the weights, q|k|v and gate|up fused along the output rows
+    // int8 weights as stored; q|k|v and gate|up fused along the output rows into copies
     for (int l = 0; l < LAYERS; l++) {
         const q8::Layer &L = h->m.layer[l];
-        if (alloc_pair(h->w_qkv[l], (size_t)QKV_ROWS * DIM) || alloc_pair(h->w_o[l], (size_t)DIM * DIM) ||
-            alloc_pair(h->w_gu[l], (size_t)GU_ROWS * DIM) || alloc_pair(h->w_down[l], (size_t)DIM * HIDDEN))
+        if (fuse(h, h->w_qkv[l], {{L.q, DIM}, {L.k, KV}, {L.v, KV}}, DIM) ||
+            fuse(h, h->w_gu[l], {{L.gate, HIDDEN}, {L.up, HIDDEN}}, DIM))
             return fail();
-        if (split_into(h, L.q, DIM, DIM, h->w_qkv[l], 0) || split_into(h, L.k, KV, DIM, h->w_qkv[l], DIM) ||
-            split_into(h, L.v, KV, DIM, h->w_qkv[l], DIM + KV) || split_into(h, L.o, DIM, DIM, h->w_o[l], 0) ||
-            split_into(h, L.gate, HIDDEN, DIM, h->w_gu[l], 0) || split_into(h, L.up, HIDDEN, DIM, h->w_gu[l], HIDDEN) ||
-            split_into(h, L.down, DIM, HIDDEN, h->w_down[l], 0))
-            return fail();
+        h->w_o[l].q = L.o.w;
+        h->w_o[l].s = L.o.s;
+        h->w_down[l].q = L.down.w;
+        h->w_down[l].s = L.down.s;
     }
-    if (alloc_pair(h->w_head, (size_t)VOCAB * DIM) || split_into(h, h->m.embed, VOCAB, DIM, h->w_head, 0))
-        return fail();
+    h->w_head.q = h->m.embed.w;
+    h->w_head.s = h->m.embed.s;
 
     // activations
     const size_t R = (size_t)max_rows;
-    if (dalloc(&h->x, R * DIM) || dalloc(&h->q, R * DIM) || dalloc(&h->xh, R * DIM) || dalloc(&h->xl, R * DIM) ||
-        dalloc(&h->ah, R * DIM) || dalloc(&h->al, R * DIM) || dalloc(&h->hh, R * HIDDEN) ||
-        dalloc(&h->hl, R * HIDDEN) || dalloc(&h->apart, R * HEADS * NCHUNK * PART) ||
-        dalloc(&h->headh, (size_t)slots * DIM) || dalloc(&h->headl, (size_t)slots * DIM) ||
+    if (dalloc(&h->x, R * DIM) || dalloc(&h->q, R * DIM) || dalloc(&h->lx.q, 3 * R * DIM) ||
+        dalloc(&h->lx.s, R * (DIM / GROUP)) || dalloc(&h->la.q, 3 * R * DIM) || dalloc(&h->la.s, R * (DIM / GROUP)) ||
+        dalloc(&h->lhq, 3 * R * HIDDEN) || dalloc(&h->lhs, R * (HIDDEN / GROUP)) ||
+        dalloc(&h->apart, R * HEADS * NCHUNK * PART) || dalloc(&h->lhead.q, 3 * (size_t)slots * DIM) ||
+        dalloc(&h->lhead.s, (size_t)slots * (DIM / GROUP)) ||
         dalloc(&h->logits, (size_t)slots * VOCAB) || dalloc(&h->tok, R) || dalloc(&h->pos, R) ||
         dalloc(&h->slot, R) || dalloc(&h->ntok, slots) || dalloc(&h->npos, slots) || dalloc(&h->nslot, slots) ||
         dalloc(&h->proj_src, slots) || dalloc(&h->proj_dst, R) || dalloc(&h->ident, slots) || dalloc(&h->err, 1) ||
@@ -950,8 +973,8 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
 
     // GEMM call sites; the partial buffer is sized from the plans' split counts
     if (plan_set(h, h->pre, max_rows) || plan_set(h, h->dec, slots)) return fail();
-    if (mb::tc::gemm_plan(&h->head, h->w_head.hi, h->w_head.lo, VOCAB, DIM, h->headh, h->headl, slots, h->logits,
-                          VOCAB, 1, h->err))
+    if (mb::tq::plan(&h->head, h->w_head.q, h->w_head.s, VOCAB, DIM, h->lhead.q, h->lhead.s, slots, h->logits, VOCAB,
+                     1, h->err))
         return fail();
     h->part_floats = std::max(plan_floats(h->pre), plan_floats(h->dec));
     if (dalloc(&h->part, h->part_floats)) return fail();
@@ -975,16 +998,16 @@ extern "C" int mocha_q8b_close(mocha_q8b *h)
     cudaSetDevice(h->device);
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->g_step) cudaGraphExecDestroy(h->g_step);
-    void *ptrs[] = {h->d_file, h->bqkv, h->x, h->q, h->part, h->apart, h->logits, h->xh, h->xl, h->ah, h->al, h->hh,
-                    h->hl, h->headh, h->headl, h->kc, h->vc, h->rope_cos, h->rope_sin, h->tok, h->pos, h->slot,
-                    h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->err, h->keys, h->st,
-                    h->params, h->out_tokens, h->out_count, h->w_head.hi, h->w_head.lo};
+    void *ptrs[] = {h->d_file, h->bqkv, h->x, h->q, h->part, h->apart, h->logits, h->lx.q, h->lx.s, h->la.q,
+                    h->la.s, h->lhq, h->lhs, h->lhead.q, h->lhead.s, h->kc, h->vc, h->rope_cos, h->rope_sin, h->tok,
+                    h->pos, h->slot, h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->err,
+                    h->keys, h->st, h->params, h->out_tokens, h->out_count};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     for (int l = 0; l < LAYERS; l++)
         for (Weights *w : {&h->w_qkv[l], &h->w_o[l], &h->w_gu[l], &h->w_down[l]}) {
-            if (w->hi) cudaFree(w->hi);
-            if (w->lo) cudaFree(w->lo);
+            if (w->own_q) cudaFree(w->own_q);
+            if (w->own_s) cudaFree(w->own_s);
         }
     for (cudaEvent_t e : h->ev)
         if (e) cudaEventDestroy(e);

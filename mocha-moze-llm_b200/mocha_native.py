@@ -83,6 +83,8 @@ _SIGS = {
     "mocha_q8b_bench_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_uint, C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "mocha_q8b_sample_check": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.POINTER(MochaSampling), C.c_void_p, C.c_void_p]),
+    "mocha_tq_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_int]),
     "mocha_tc_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
 }
