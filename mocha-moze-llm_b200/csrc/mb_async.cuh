@@ -74,6 +74,24 @@ MB_DEV void prefetch_map(const CUtensorMap *map)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// L2 prefetch of one box of a tiled tensor map (no shared memory, no barrier).
+MB_DEV void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------
+// A kernel launched with programmatic stream serialisation may start before the
+// kernel ahead of it in the stream has finished; griddep_wait() returns once that
+// kernel (and, transitively, everything before it) has completed and its memory is
+// visible.  griddep_launch() lets the next kernel start its own prologue.  Both are
+// no-ops for ordinary launches.
+MB_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MB_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- TMEM -------------------------------------------------------------------------
 
 // Whole-warp call: allocates `cols` (power of two >= 32) TMEM columns and writes the

@@ -35,6 +35,7 @@
 #include "sampling.cuh"
 #include "sampling_dev.cuh"
 #include "tc_gemm.cuh"
+#include "mb_async.cuh"
 #include "tc_q8gemm.cuh"
 
 namespace qb {
@@ -53,6 +54,15 @@ constexpr int QKV_THREADS = (DIM + 2 * KV) / 2;  // one thread per RoPE pair / V
 constexpr int SLICE = 4096;             // sampler stage 1: ids per CTA
 constexpr int NSLICE = (VOCAB + SLICE - 1) / SLICE;
 constexpr int SAMPLE_THREADS = 1024;
+
+// Every kernel of the batched pipeline is launched with programmatic stream
+// serialisation: it lets the next kernel launch at once and waits for the previous
+// one before it touches any activation.
+MB_DEV void pdl_enter()
+{
+    mb::as::griddep_launch();
+    mb::as::griddep_wait();
+}
 
 // KV cache: [slot][layer][kv head][position][64] fp32.
 __host__ __device__ __forceinline__ size_t kv_off(int slot, int layer, int kvh, int pos)
@@ -91,6 +101,7 @@ MB_DEV void norm_store(const float (&v)[4], float *red, const float *__restrict_
 __global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const float *__restrict__ gain, float *x,
                                                    Limbs out)
 {
+    pdl_enter();
     __shared__ float red[32];
     const int t = blockIdx.x, i0 = threadIdx.x * 4;
     const int token = rows.tok[t];
@@ -106,6 +117,7 @@ __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__r
                                                       long long sstride, const float *__restrict__ gain, Limbs out,
                                                       const int *__restrict__ dst_row)
 {
+    pdl_enter();
     __shared__ float red[32];
     const int t = blockIdx.x, i0 = threadIdx.x * 4;
     float4 acc = *reinterpret_cast<const float4 *>(part + (size_t)t * DIM + i0);
@@ -131,6 +143,7 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
                                                           const float *__restrict__ rope_sin, float *q, float *kc,
                                                           float *vc, int layer)
 {
+    pdl_enter();
     const int t = blockIdx.x, j = threadIdx.x;
     const int pos = rows.pos[t], slot = rows.slot[t];
     int kind, head, i;
@@ -180,6 +193,7 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
 __global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q, Rows rows, const float *__restrict__ kc,
                                                     const float *__restrict__ vc, int layer, float *__restrict__ part)
 {
+    pdl_enter();
     const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
     const int pos = rows.pos[t], slot = rows.slot[t];
     const int k0 = c * CHUNK;
@@ -240,6 +254,7 @@ __global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q,
 // GEMM (one warp, two dims per lane: the head is one 64-group).
 __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out)
 {
+    pdl_enter();
     const int h = blockIdx.x, t = blockIdx.y, d = 2 * threadIdx.x;
     const int nc = rows.pos[t] / CHUNK + 1;
     const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
@@ -262,6 +277,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ p
 __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride,
                                                 int8_t *hq, float *hs)
 {
+    pdl_enter();
     const int t = blockIdx.y, i = (blockIdx.x * 256 + threadIdx.x) * 2;
     if (i >= HIDDEN) return;
     const float *p = part + (size_t)t * GU_ROWS;
@@ -293,6 +309,7 @@ __global__ void __launch_bounds__(256) k_attn_block(const float *__restrict__ q,
                                                     const float *__restrict__ kc, const float *__restrict__ vc,
                                                     int layer, Limbs out)
 {
+    pdl_enter();
     extern __shared__ float4 smem4[];
     float *sQ = reinterpret_cast<float *>(smem4);
     float *sK = sQ + QB * QB_LD;
@@ -541,6 +558,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
                                                               const sampling::Params *prm,
                                                               unsigned long long *__restrict__ out)
 {
+    pdl_enter();
     __shared__ unsigned long long keys[SLICE];
     __shared__ int hist[sampling::kHistory];
     const int r = blockIdx.y, lo = blockIdx.x * SLICE;
@@ -590,6 +608,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned lon
                                                               int *next_tok, int *next_pos, int *next_slot,
                                                               int *out_tokens, int *out_count, int out_stride)
 {
+    pdl_enter();
     constexpr int kMerge = 4096;  // >= NSLICE * kMaxK = 2432
     __shared__ unsigned long long keys[kMerge];
     const int r = blockIdx.x;
@@ -676,6 +695,24 @@ namespace {
 
 #define QB_TRY(x) MB_CHECK(x)
 
+// Launch with programmatic stream serialisation (see pdl_enter).
+template <typename... KArgs, typename... Args>
+int pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QB_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+    return 0;
+}
+
 int check_err(mocha_q8b *h)
 {
     int e = 0;
@@ -751,11 +788,11 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, bool block)
             QB_TRY(cudaFuncSetAttribute(k_attn_block, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QB_SMEM));
             attr_done[h->device & 63] = true;
         }
-        k_attn_block<<<dim3(n / QB, HEADS), 256, QB_SMEM, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->la);
+        if (pdl(k_attn_block, dim3(n / QB, HEADS), 256, QB_SMEM, h->stream, h->q, rows, h->kc, h->vc, layer, h->la)) return 1;
         return 0;
     }
-    k_attn_chunk<<<dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream>>>(h->q, rows, h->kc, h->vc, layer, h->apart);
-    k_attn_combine<<<dim3(HEADS, n), 32, 0, h->stream>>>(h->apart, rows, h->la);
+    if (pdl(k_attn_chunk, dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream, h->q, rows, h->kc, h->vc, layer, h->apart)) return 1;
+    if (pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la)) return 1;
     return 0;
 }
 
@@ -778,23 +815,23 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
 {
     const PlanSet &ps = decode_set ? h->dec : h->pre;
     cudaStream_t s = h->stream;
-    k_embed_norm<<<n, NT, 0, s>>>(h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->lx);
+    if (pdl(k_embed_norm, n, NT, 0, s, h->m.embed, rows, h->m.layer[0].attn_norm, h->x, h->lx)) return 1;
     mb::tc::Split sp;
     for (int l = 0; l < LAYERS; l++) {
         const Layer &L = h->m.layer[l];
         if (mb::tq::launch(ps.qkv[l], n, s, &sp)) return 1;
-        k_qkv_post<<<n, QKV_THREADS, 0, s>>>(h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
-                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l);
+        if (pdl(k_qkv_post, n, QKV_THREADS, 0, s, h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
+                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l)) return 1;
         if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
-        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr);
+        if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr)) return 1;
         if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;
-        k_swiglu<<<dim3((HIDDEN + 511) / 512, n), 256, 0, s>>>(h->part, sp.splits, sp.split_stride, h->lhq, h->lhs);
+        if (pdl(k_swiglu, dim3((HIDDEN + 511) / 512, n), 256, 0, s, h->part, sp.splits, sp.split_stride, h->lhq, h->lhs)) return 1;
         if (mb::tq::launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
-        k_residual_norm<<<n, NT, 0, s>>>(h->x, h->part, sp.splits, sp.split_stride,
+        if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride,
                                           last ? h->m.final_norm : h->m.layer[l + 1].attn_norm,
-                                          last ? h->lhead : h->lx, last ? proj_dst : nullptr);
+                                          last ? h->lhead : h->lx, last ? proj_dst : nullptr)) return 1;
     }
     if (np > 0 && mb::tq::launch(h->head, np, s)) return 1;
     QB_TRY(cudaGetLastError());
@@ -805,10 +842,10 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
 // projected row r (the identity map in decode steps).
 int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src)
 {
-    k_bs_stage1<<<dim3(NSLICE, np), SAMPLE_THREADS, 0, h->stream>>>(h->logits, proj_src, rows, h->slots, h->st,
-                                                                   h->params, h->keys);
-    k_bs_stage2<<<np, SAMPLE_THREADS, 0, h->stream>>>(h->keys, proj_src, rows, h->slots, h->st, h->params, h->ntok,
-                                                      h->npos, h->nslot, h->out_tokens, h->out_count, h->out_stride);
+    if (pdl(k_bs_stage1, dim3(NSLICE, np), SAMPLE_THREADS, 0, h->stream, h->logits, proj_src, rows, h->slots, h->st,
+                                                                   h->params, h->keys)) return 1;
+    if (pdl(k_bs_stage2, np, SAMPLE_THREADS, 0, h->stream, h->keys, proj_src, rows, h->slots, h->st, h->params, h->ntok,
+                                                      h->npos, h->nslot, h->out_tokens, h->out_count, h->out_stride)) return 1;
     QB_TRY(cudaGetLastError());
     return 0;
 }

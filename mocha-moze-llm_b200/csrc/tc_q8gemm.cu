@@ -62,11 +62,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q8(const __grid_constant__
         *abort = 0;
         as::fence_barrier_init();
     }
+    as::griddep_launch();
+    if (threadIdx.x == 32) {
+        // weights do not depend on the kernel ahead: start pulling this CTA's first tile
+        // into L2 while that kernel finishes
+        const int tile = blockIdx.x;
+        if (tile < tiles) {
+            const int mt = tile % m_tiles, z = tile / (m_tiles * n_tiles);
+            const int s0 = z * p.kstages, ns = min(p.kstages, stages_total - s0);
+            for (int k = 0; k < ns && k < 8; k++) as::tma_prefetch_2d(&p.a, (s0 + k) * kBK, mt * kBM);
+        }
+    }
     if (warp == 1) as::tmem_alloc(tmem_slot, kTmemCols);
     as::tc_fence_before();
     __syncthreads();
     as::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    as::griddep_wait();  // activations, scales and the partial buffer belong to earlier kernels
 
     if (warp == 0 && lane == 0) {
         // TMA producer: every stage of every tile of this CTA through the ring
@@ -316,8 +328,17 @@ int launch(const Gemm &g, int n, cudaStream_t s, tc::Split *used)
     const int m_tiles = p.M / kBM, n_tiles = (n + kTokens - 1) / kTokens;
     const int tiles = m_tiles * n_tiles * sp.splits;
     const int grid = tiles < kSMs ? tiles : kSMs;
-    k_gemm_q8<<<grid, kThreads, kSmem, s>>>(p, m_tiles, n_tiles, tiles);
-    MB_CHECK(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MB_CHECK(cudaLaunchKernelEx(&cfg, k_gemm_q8, p, m_tiles, n_tiles, tiles));
     return 0;
 }
 
