@@ -38,6 +38,8 @@ PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
 # batched serving workload: 512 sequences, 128-token prompts, 384 generated, 64 per GPU at a time
 SERVE_SEQS, SERVE_PROMPT, SERVE_NEW, SERVE_BATCH = 512, 128, 384, 64
+# GGUF decode workloads: (architecture, prompt tokens, generated tokens, weight bytes per token, KV bytes per position)
+GGUF_WORKLOADS = (("llama1b", 32, 128, 799_862_784, 65_536), ("qwen15b", 64, 256, 980_097_536, 57_344))
 
 
 def dist_env():
@@ -228,6 +230,56 @@ def bench_batched(group, data, args, parts):
             "nseq": len(mine), "wall": wall, "launches": launches}
 
 
+def bench_gguf(group, args):
+    """b=1 greedy decode of the two GGUF models (random-init, Q4_K_M mix) on this rank."""
+    import numpy as np
+
+    import mocha_gguf_model
+    import mocha_native
+    out = {}
+    for arch, plen, nnew, wbytes, kvpos in GGUF_WORKLOADS:
+        if group.rank == 0:
+            mocha_gguf_model.model_path(arch)
+        group.barrier()
+        data = np.fromfile(mocha_gguf_model.model_path(arch), dtype=np.uint8)
+        h = mocha_native.GgufHandle(group.local, data)
+        prompt = np.random.default_rng(11 + group.rank).integers(0, h.info.vocab, plen).tolist()
+        first, _ = h.generate(prompt, 1)
+        tok = first[0] if first else prompt[-1]
+        pos0, pos_end = plen - 1, plen - 1 + nnew
+        ms = h.bench_decode(tok, pos0, pos_end, args.warmup * nnew, args.steps * nnew)
+        t0 = time.perf_counter()
+        h.generate(prompt, nnew)
+        wall = time.perf_counter() - t0
+        launches = mocha_native.load().mocha_gguf_launches_per_step(h.h)
+        h.close()
+        del data
+        out[arch] = {"ms": ms, "wall": wall, "launches": launches}
+    return out
+
+
+def gguf_objects(gathered, args, world):
+    hbm_peak, hbm_kind = peaks()
+    res = {}
+    for arch, plen, nnew, wbytes, kvpos in GGUF_WORKLOADS:
+        ms = max(g["gguf"][arch]["ms"] for g in gathered)
+        per_tok = ms / 1e3 / (args.steps * nnew)
+        mean_pos1 = (plen + plen - 1 + nnew) / 2
+        algo = wbytes + kvpos * mean_pos1
+        achieved = algo / per_tok / 1e9
+        wall = max(g["gguf"][arch]["wall"] for g in gathered)
+        res[arch] = {
+            "value": world / per_tok, "unit": "tok/s", "us_per_token": per_tok * 1e6,
+            "config": {"workload": f"{arch} GGUF Q4_K_M-mix random-init, b=1 greedy, {plen}-token prompt + "
+                                   f"{nnew} generated per GPU"},
+            "e2e": {"value": world * nnew / wall, "unit": "tok/s",
+                    "path": "mocha_gguf_generate (host prompt in, host tokens out), prompt pass included"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": hbm_kind, "algorithmic_bytes_per_token": algo},
+            "gpu_launches_per_token": gathered[0]["gguf"][arch]["launches"]}
+    return res
+
+
 def prefill_object(gathered, args, world):
     tf_peak, tf_kind = peak_tflops()
     pre_ms = max(g["prefill_ms"] for g in gathered) / args.steps
@@ -293,8 +345,8 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the prefill and batched-serving objects")
     ap.add_argument("--serve-seqs", type=int, default=SERVE_SEQS, help="batched job size (smaller for profiling)")
     ap.add_argument("--serve-new", type=int, default=SERVE_NEW, help="tokens per sequence of the batched job")
-    ap.add_argument("--parts", default="decode,prefill,batched",
-                    help="comma list of workloads to run (profiling runs select one); the default runs all three")
+    ap.add_argument("--parts", default="decode,prefill,batched,gguf",
+                    help="comma list of workloads to run (profiling runs select one); the default runs all four")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -332,6 +384,9 @@ def main():
         h.close()
     run_batched = not args.no_batched and bool(parts & {"prefill", "batched"})
     extra = bench_batched(group, data, args, parts) if run_batched else {}
+    del data
+    if "gguf" in parts:
+        extra["gguf"] = bench_gguf(group, args)
     gathered = group.gather({"ms": ms, "e2e": e2e_wall, "clocks": clocks, **extra})
     if rank != 0:
         group.close()
@@ -373,6 +428,8 @@ def main():
         out["prefill"] = prefill_object(gathered, args, world)
     if run_batched and "batched" in parts:
         out["batched"] = batched_object(gathered, args, world)
+    if "gguf" in parts:
+        out["gguf"] = gguf_objects(gathered, args, world)
     if not args.no_cpu_baseline and "decode" in parts:
         out["cpu_baseline"] = cpu_baseline(path, mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED))
     print(json.dumps(out))
