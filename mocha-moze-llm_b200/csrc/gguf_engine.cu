@@ -164,28 +164,34 @@ size_t tensor_bytes(const TensorInfo &t)
 
 // ---- device kernels ---------------------------------------------------------------
 
-constexpr int kNormThreads = 1024;
-
-// y = x * (1/sqrt(mean(x^2) + eps)) * g  (ggml_rms_norm followed by the gain)
-__global__ void __launch_bounds__(kNormThreads) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ g,
-                                                          int n, float eps, float *__restrict__ y)
-{
-    __shared__ float red[32];
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-    ss = mb::warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float sum = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) sum += red[w];
-    const float s = 1.0f / sqrtf(sum / n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = x[i] * s * g[i];
-}
 
 struct RopeArgs {
     const float *cos_t, *sin_t;  // [context][head_dim/2]
     int head_dim, heads, kv_heads, neox, context;
 };
+
+// The per-token kernels are launched with programmatic stream serialisation: each lets
+// the next one launch at once and waits for the previous one before reading anything.
+__device__ __forceinline__ void pdl_enter()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+int pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : 1;
+}
 
 // QKV biases, RoPE on q and k, and the KV-cache write for this position.
 __global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ v,
@@ -193,6 +199,7 @@ __global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, const f
                            RopeArgs ra, const int *__restrict__ pos_ptr, float *__restrict__ kc,
                            float *__restrict__ vc, int layer)
 {
+    pdl_enter();
     const int pos = *pos_ptr;
     const int half = ra.head_dim / 2;
     const int npairs = (ra.heads + ra.kv_heads) * half;
@@ -239,6 +246,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     k_attention(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, RopeArgs ra,
                 const int *__restrict__ pos_ptr, int layer, float *__restrict__ out)
 {
+    pdl_enter();
     __shared__ float qs[kMaxHeadDim];
     __shared__ float wm[kAttnWarps], wl[kAttnWarps];
     __shared__ float wacc[kAttnWarps][kMaxHeadDim];
@@ -285,6 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads)
 
 __global__ void k_swiglu(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ h, int n)
 {
+    pdl_enter();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float x = g[i];
         h[i] = (x / (1.0f + expf(-x))) * u[i];
@@ -353,30 +362,40 @@ int enqueue_forward(mocha_gguf *m, bool project)
 {
     const mocha_gguf_info &in = m->info;
     const cudaStream_t s = m->stream;
-    const int dim = in.dim, kvd = in.kv_heads * in.head_dim;
     int rc = gguf::enqueue_dequant_row(m->embd, m->state, m->x, s);
+    auto multi = [&](std::initializer_list<std::pair<const gguf::DevMat *, float *>> mats, const float *x,
+                     const float *gain, bool accumulate) {
+        gguf::MultiGemv g{};
+        int i = 0, rows = 0;
+        for (auto &mt : mats) {
+            g.m[i] = *mt.first;
+            g.y[i] = mt.second;
+            rows += mt.first->rows;
+            g.row_end[i] = rows;
+            i++;
+        }
+        g.n = i;
+        g.cols = mats.begin()->first->cols;
+        g.accumulate = accumulate ? 1 : 0;
+        g.x = x;
+        g.gain = gain;
+        g.eps = in.eps;
+        return gguf::enqueue_gemv_multi(g, s);
+    };
     for (int l = 0; l < in.layers && !rc; l++) {
         const Layer &L = m->layers[l];
-        k_rmsnorm<<<1, kNormThreads, 0, s>>>(m->x, L.attn_norm, dim, in.eps, m->xn);
-        rc = rc || gguf::enqueue_gemv(L.q, m->xn, 1, dim, m->q, dim, s) ||
-             gguf::enqueue_gemv(L.k, m->xn, 1, dim, m->k, kvd, s) ||
-             gguf::enqueue_gemv(L.v, m->xn, 1, dim, m->v, kvd, s);
-        if (rc) break;
-        k_qkv_post<<<8, 256, 0, s>>>(m->q, m->k, m->v, L.bq, L.bk, L.bv, m->rope, m->state + 1, m->kc, m->vc, l);
-        k_attention<<<in.heads, kAttnThreads, 0, s>>>(m->q, m->kc, m->vc, m->rope, m->state + 1, l, m->att);
-        rc = gguf::enqueue_gemv(L.o, m->att, 1, dim, m->x, dim, s, true);
-        if (rc) break;
-        k_rmsnorm<<<1, kNormThreads, 0, s>>>(m->x, L.ffn_norm, dim, in.eps, m->xn);
-        rc = gguf::enqueue_gemv(L.gate, m->xn, 1, dim, m->g, in.ffn, s) ||
-             gguf::enqueue_gemv(L.up, m->xn, 1, dim, m->u, in.ffn, s);
-        if (rc) break;
-        k_swiglu<<<(in.ffn + 255) / 256, 256, 0, s>>>(m->g, m->u, m->h, in.ffn);
-        rc = gguf::enqueue_gemv(L.down, m->h, 1, in.ffn, m->x, dim, s, true);
+        // RMSNorm folded into the fused q|k|v GEMV
+        rc = multi({{&L.q, m->q}, {&L.k, m->k}, {&L.v, m->v}}, m->x, L.attn_norm, false) ||
+             pdl(k_qkv_post, dim3(8), dim3(256), s, m->q, m->k, m->v, L.bq, L.bk, L.bv, m->rope, m->state + 1, m->kc,
+                 m->vc, l) ||
+             pdl(k_attention, dim3(in.heads), dim3(kAttnThreads), s, m->q, m->kc, m->vc, m->rope, m->state + 1, l,
+                 m->att) ||
+             multi({{&L.o, m->x}}, m->att, nullptr, true) ||
+             multi({{&L.gate, m->g}, {&L.up, m->u}}, m->x, L.ffn_norm, false) ||
+             pdl(k_swiglu, dim3((in.ffn + 255) / 256), dim3(256), s, m->g, m->u, m->h, in.ffn) ||
+             multi({{&L.down, m->x}}, m->h, nullptr, true);
     }
-    if (!rc && project) {
-        k_rmsnorm<<<1, kNormThreads, 0, s>>>(m->x, m->out_norm, dim, in.eps, m->xn);
-        rc = gguf::enqueue_gemv(m->embd, m->xn, 1, dim, m->logits, in.vocab, s);
-    }
+    if (!rc && project) rc = multi({{&m->embd, m->logits}}, m->x, m->out_norm, false);
     return rc || launch_ok("gguf forward");
 }
 
@@ -605,7 +624,7 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
     if (capture(m, &m->g_forward[0], 0) || capture(m, &m->g_forward[1], 1) || capture(m, &m->g_prefill, 2) ||
         capture(m, &m->g_decode, 3))
         return 1;
-    m->launches_per_token = 1 + (unsigned long long)in.layers * 12 + 2 + 3;
+    m->launches_per_token = 1 + (unsigned long long)in.layers * 7 + 1 + 3;
     TRY(cudaStreamSynchronize(m->stream));
     return 0;
 }

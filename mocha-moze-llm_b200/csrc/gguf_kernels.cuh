@@ -49,6 +49,19 @@ int enqueue_dequant(const DevMat &m, float *out, cudaStream_t s);
 int enqueue_gemv(const DevMat &m, const float *x, int vectors, int x_stride_f, float *y, int y_stride_f,
                  cudaStream_t s, bool accumulate = false);
 
+// Fused GEMV of up to three matrices with the same input (q/k/v, gate/up):
+// y[i][r] (+)= W_i[r] . xn for r < rows_i, where xn = x, or the RMSNorm of x with `gain`
+// and `eps` when gain is non-null.  row_end[i] = rows of matrices 0..i together.
+struct MultiGemv {
+    DevMat m[3];
+    float *y[3];
+    int row_end[3];
+    int n, cols, accumulate;
+    const float *x, *gain;
+    float eps;
+};
+int enqueue_gemv_multi(const MultiGemv &g, cudaStream_t s);
+
 // out[c] = exact dequantised weight (row *row_index, read on the device), c < cols.
 int enqueue_dequant_row(const DevMat &m, const int *row_index, float *out, cudaStream_t s);
 
