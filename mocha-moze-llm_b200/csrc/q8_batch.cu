@@ -296,6 +296,235 @@ __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, 
                                hs + (size_t)t * (HIDDEN / GROUP) + i / GROUP, threadIdx.x & 31);
 }
 
+// ---- prompt attention on the tensor cores ---------------------------------------------
+//
+// One CTA per (block of 128 consecutive rows of one slot at positions p0..p0+127, p0 a
+// multiple of 128; query head h).  For every chunk of 64 keys 0..p0+127:
+//   K (and V, transposed) are read from the fp32 cache and written as bf16 pairs
+//   (hi = bf16(v), lo = bf16(v - hi)) in the 128-byte-swizzled K-major layout;
+//   S = Q K^T (q already carries the 0.125) comes from three tcgen05 MMAs
+//   (hi*hi + hi*lo + lo*hi) into TMEM; each of the 128 threads owns one query row:
+//   it reads its 64 scores, applies the causal mask and the online softmax, and writes
+//   its P row as a bf16 pair; O_c = P V comes from three more MMAs; the thread folds
+//   O_c into its fp32 output row.  The output row is one 64-group of the O GEMM input:
+//   it leaves as int8 limbs.
+constexpr int TQ = 128;           // queries per CTA
+constexpr int TK = 64;            // keys per chunk
+constexpr uint32_t kTileQ = TQ * HEAD_DIM * 2;   // 16 KiB: one bf16 [128][64] tile
+constexpr uint32_t kTileK = TK * HEAD_DIM * 2;   // 8 KiB: one bf16 [64][64] tile
+constexpr size_t TC_SMEM = 1024 + 2 * kTileQ /*Q*/ + 2 * kTileK /*K*/ + 2 * kTileK /*Vt*/ + 2 * kTileQ /*P*/ + 64;
+
+// byte offset of element (r, c) of a [rows][64] bf16 tile in the SW128 K-major layout
+MB_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2); }
+
+MB_DEV void put8(uint8_t *tile, int r, int c0, const float (&v)[8], uint8_t *tile_lo)
+{
+    __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) mb::tc::split_bf16(v[i], hi[i], lo[i]);
+    const uint32_t off = sw128_off(r, c0);
+    *reinterpret_cast<uint4 *>(tile + off) = *reinterpret_cast<const uint4 *>(hi);
+    *reinterpret_cast<uint4 *>(tile_lo + off) = *reinterpret_cast<const uint4 *>(lo);
+}
+
+__global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, Rows rows,
+                                                  const float *__restrict__ kc, const float *__restrict__ vc,
+                                                  int layer, Limbs out, int *err)
+{
+    pdl_enter();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *q_hi = sm, *q_lo = q_hi + kTileQ, *k_hi = q_lo + kTileQ, *k_lo = k_hi + kTileK;
+    uint8_t *v_hi = k_lo + kTileK, *v_lo = v_hi + kTileK, *p_hi = v_lo + kTileK, *p_lo = p_hi + kTileQ;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(p_lo + kTileQ);  // [0] S done, [1] O done, [2] drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 3);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int h = blockIdx.y, g = h / GQA, t0 = blockIdx.x * TQ;
+    const int slot = rows.slot[t0], p0 = rows.pos[t0];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        mb::as::mbar_init(&bar[0], 1);
+        mb::as::mbar_init(&bar[1], 1);
+        mb::as::mbar_init(&bar[2], 1);
+        *abort = 0;
+        mb::as::fence_barrier_init();
+    }
+    if (warp == 0) mb::as::tmem_alloc(tmem_slot, 128);
+    // Q tile: 128 rows x 8 chunks of 8 dims
+    for (int ci = tid; ci < TQ * 8; ci += TQ) {
+        const int r = ci >> 3, c0 = (ci & 7) * 8;
+        const float4 *src = reinterpret_cast<const float4 *>(q + (size_t)(t0 + r) * DIM + h * HEAD_DIM + c0);
+        const float4 a = src[0], b = src[1];
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        put8(q_hi, r, c0, v, q_lo);
+    }
+    mb::as::tc_fence_before();
+    __syncthreads();
+    mb::as::tc_fence_after();
+    const uint32_t tmem = *tmem_slot, tm_s = tmem, tm_o = tmem + 64;
+    constexpr uint32_t idesc = mb::as::idesc_bf16_f32(TQ, TK);
+    const int row = tid, qpos = p0 + row;  // this thread's query
+    float o[HEAD_DIM];
+#pragma unroll
+    for (int d = 0; d < HEAD_DIM; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const int nchunks = (p0 + TQ - 1) / TK + 1;
+    bool ok = true;
+    for (int c = 0; c < nchunks; c++) {
+        const int k0 = c * TK;
+        const size_t base = kv_off(slot, layer, g, k0);
+        // K: [key][dim]; V transposed: [dim][key] (lanes take consecutive dims: coalesced reads)
+        for (int ci = tid; ci < TK * 8; ci += TQ) {
+            const int key = ci >> 3, c0 = (ci & 7) * 8;
+            const float4 *src = reinterpret_cast<const float4 *>(kc + base + (size_t)key * HEAD_DIM + c0);
+            const float4 a = src[0], b = src[1];
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            put8(k_hi, key, c0, v, k_lo);
+        }
+        for (int ci = tid; ci < HEAD_DIM * 8; ci += TQ) {
+            const int d = ci & 63, kg = ci >> 6;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = vc[base + (size_t)(kg * 8 + i) * HEAD_DIM + d];
+            put8(v_hi, d, kg * 8, v, v_lo);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mb::as::tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            mb::as::tc_fence_after();
+            const uint32_t qa = mb::as::smem_u32(q_hi), qb = mb::as::smem_u32(q_lo);
+            const uint32_t ka = mb::as::smem_u32(k_hi), kb = mb::as::smem_u32(k_lo);
+#pragma unroll
+            for (int kk = 0; kk < HEAD_DIM / 16; kk++) {
+                const uint32_t off = kk * 32;
+                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(ka + off), idesc, kk > 0);
+                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(kb + off), idesc, true);
+                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qb + off), mb::as::sw128_desc(ka + off), idesc, true);
+            }
+            mb::as::mma_commit(&bar[0]);
+        }
+        ok = mb::as::mbar_wait(&bar[0], c & 1, abort);
+        mb::as::tc_fence_after();
+        if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
+            if (tid == 0) atomicCAS(err, 0, 31);
+            ok = false;
+            break;
+        }
+        // scores of this row, causal mask, online softmax
+        float sc[TK];
+        {
+            uint32_t r16[16];
+#pragma unroll
+            for (int j = 0; j < TK / 16; j++) {
+                mb::as::tmem_ld16(tm_s + ((uint32_t)(warp * 32) << 16) + j * 16, r16);
+                mb::as::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) sc[j * 16 + i] = __uint_as_float(r16[i]);
+            }
+        }
+        float mx = m;
+#pragma unroll
+        for (int j = 0; j < TK; j++) {
+            if (k0 + j > qpos) sc[j] = -INFINITY;
+            mx = fmaxf(mx, sc[j]);
+        }
+        const float scale = expf(m - mx);
+        float sum = 0.f;
+#pragma unroll
+        for (int j0 = 0; j0 < TK; j0 += 8) {
+            float pv[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                pv[i] = expf(sc[j0 + i] - mx);
+                sum += pv[i];
+            }
+            put8(p_hi, row, j0, pv, p_lo);
+        }
+        l = l * scale + sum;
+        m = mx;
+#pragma unroll
+        for (int d = 0; d < HEAD_DIM; d++) o[d] *= scale;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mb::as::tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            mb::as::tc_fence_after();
+            const uint32_t pa = mb::as::smem_u32(p_hi), pb = mb::as::smem_u32(p_lo);
+            const uint32_t va = mb::as::smem_u32(v_hi), vb = mb::as::smem_u32(v_lo);
+#pragma unroll
+            for (int kk = 0; kk < TK / 16; kk++) {
+                const uint32_t off = kk * 32;
+                mb::as::mma_bf16(tm_o, mb::as::sw128_desc(pa + off), mb::as::sw128_desc(va + off), idesc, kk > 0);
+                mb::as::mma_bf16(tm_o, mb::as::sw128_desc(pa + off), mb::as::sw128_desc(vb + off), idesc, true);
+                mb::as::mma_bf16(tm_o, mb::as::sw128_desc(pb + off), mb::as::sw128_desc(va + off), idesc, true);
+            }
+            mb::as::mma_commit(&bar[1]);
+        }
+        ok = mb::as::mbar_wait(&bar[1], c & 1, abort);
+        mb::as::tc_fence_after();
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) atomicCAS(err, 0, 32);
+            ok = false;
+            break;
+        }
+        {
+            uint32_t r16[16];
+#pragma unroll
+            for (int j = 0; j < HEAD_DIM / 16; j++) {
+                mb::as::tmem_ld16(tm_o + ((uint32_t)(warp * 32) << 16) + j * 16, r16);
+                mb::as::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) o[j * 16 + i] += __uint_as_float(r16[i]);
+            }
+        }
+        mb::as::tc_fence_before();
+        __syncthreads();  // K, V and P may be rewritten
+    }
+    if (!ok && tid == 0) {
+        // every MMA issued so far has finished before TMEM and shared memory go away
+        mb::as::mma_commit(&bar[2]);
+        const volatile int never = 0;
+        mb::as::mbar_wait(&bar[2], 0, &never);
+    }
+    if (ok) {
+        // the row's 64 outputs are one group: limbs without any cross-thread reduction
+        const float inv = 1.f / l;
+        float mxa = 0.f;
+#pragma unroll
+        for (int d = 0; d < HEAD_DIM; d++) {
+            o[d] *= inv;
+            mxa = fmaxf(mxa, fabsf(o[d]));
+        }
+        const float sinv = mxa > 0.f ? 127.f / mxa : 0.f;
+        int8_t *dst = out.q + (size_t)(t0 + row) * 3 * DIM + h * HEAD_DIM;
+#pragma unroll
+        for (int d0 = 0; d0 < HEAD_DIM; d0 += 4) {
+            float q0[4], q1[4], q2[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float qv = o[d0 + e] * sinv;
+                q0[e] = fminf(fmaxf(rintf(qv), -127.f), 127.f);
+                const float r1 = (qv - q0[e]) * 254.f;
+                q1[e] = fminf(fmaxf(rintf(r1), -127.f), 127.f);
+                q2[e] = fminf(fmaxf(rintf((r1 - q1[e]) * 254.f), -127.f), 127.f);
+            }
+            *reinterpret_cast<char4 *>(dst + d0) = make_char4((int8_t)q0[0], (int8_t)q0[1], (int8_t)q0[2], (int8_t)q0[3]);
+            *reinterpret_cast<char4 *>(dst + DIM + d0) =
+                make_char4((int8_t)q1[0], (int8_t)q1[1], (int8_t)q1[2], (int8_t)q1[3]);
+            *reinterpret_cast<char4 *>(dst + 2 * DIM + d0) =
+                make_char4((int8_t)q2[0], (int8_t)q2[1], (int8_t)q2[2], (int8_t)q2[3]);
+        }
+        out.s[(size_t)(t0 + row) * (DIM / GROUP) + h] = mxa / 127.f;
+    }
+    mb::as::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        mb::as::tc_fence_after();
+        mb::as::tmem_free(tmem, 128);
+    }
+}
+
 // Prompt attention for a block of 64 consecutive rows of one slot (positions
 // p0..p0+63, p0 a multiple of 64) and one query head: key chunks of 64 staged in
 // shared memory, online softmax, fp32 throughout.  Thread (ty, tx) owns query rows
@@ -780,9 +1009,17 @@ size_t plan_floats(const PlanSet &ps)
 // Attention for rows [0, n): the query-block kernel when every 64-row block is one
 // slot at consecutive positions starting at a multiple of 64 (prompt passes whose
 // per-slot length is a multiple of 64), else the per-row chunk kernels.
-int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, bool block)
+int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
 {
-    static bool attr_done[64] = {};
+    static bool attr_done[64] = {}, tc_done[64] = {};
+    if (block == 2) {
+        if (!tc_done[h->device & 63]) {
+            QB_TRY(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+            tc_done[h->device & 63] = true;
+        }
+        return pdl(k_attn_tc, dim3(n / TQ, HEADS), TQ, TC_SMEM, h->stream, h->q, rows, h->kc, h->vc, layer, h->la,
+                   h->err);
+    }
     if (block) {
         if (!attr_done[h->device & 63]) {
             QB_TRY(cudaFuncSetAttribute(k_attn_block, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QB_SMEM));
@@ -796,22 +1033,27 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, bool block)
     return 0;
 }
 
-// True when rows (host arrays) qualify for the query-block attention kernel.
-bool block_rows(int n, const int *pos, const int *slots)
+// Attention kernel for rows (host arrays): 2 when every block of 128 rows is one slot
+// at consecutive positions from a multiple of 128 (tensor cores), 1 for blocks of 64
+// (CUDA cores), 0 for per-row chunks.
+int block_kind(int n, const int *pos, const int *slots)
 {
-    if (n % QB) return false;
-    for (int b = 0; b < n; b += QB) {
-        if (pos[b] % QB) return false;
-        for (int i = 1; i < QB; i++)
-            if (slots[b + i] != slots[b] || pos[b + i] != pos[b] + i) return false;
-    }
-    return true;
+    auto blocks_of = [&](int b) {
+        if (n % b) return false;
+        for (int r = 0; r < n; r += b) {
+            if (pos[r] % b) return false;
+            for (int i = 1; i < b; i++)
+                if (slots[r + i] != slots[r] || pos[r + i] != pos[r] + i) return false;
+        }
+        return true;
+    };
+    return blocks_of(TQ) ? 2 : (blocks_of(QB) ? 1 : 0);
 }
 
 // The whole transformer for rows [0, n) plus the head for `np` projected rows
 // (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of the head limbs).
 int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np,
-                    bool block_attention)
+                    int block_attention)
 {
     const PlanSet &ps = decode_set ? h->dec : h->pre;
     cudaStream_t s = h->stream;
@@ -889,7 +1131,7 @@ int capture_step(mocha_q8b *h, int n)
     cudaGraph_t g;
     QB_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     const Rows r{h->ntok, h->npos, h->nslot};
-    int rc = enqueue_forward(h, r, n, true, h->ident, n, false);
+    int rc = enqueue_forward(h, r, n, true, h->ident, n, 0);
     if (!rc) rc = enqueue_sample(h, r, n, h->ident);
     const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
     if (rc || e != cudaSuccess) {
@@ -1069,7 +1311,7 @@ extern "C" int mocha_q8b_forward(mocha_q8b *h, int n, const int *tokens, const i
     QB_TRY(cudaSetDevice(h->device));
     if (upload_rows(h, n, tokens, pos, slots) || set_projection(h, n, n_project, project_rows)) return 1;
     const Rows r{h->tok, h->pos, h->slot};
-    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project, block_rows(n, pos, slots))) return 1;
+    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project, block_kind(n, pos, slots))) return 1;
     if (logits && n_project)
         QB_TRY(cudaMemcpyAsync(logits, h->logits, sizeof(float) * VOCAB * n_project, cudaMemcpyDeviceToHost,
                                h->stream));
@@ -1155,7 +1397,8 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
         if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, b, src.data())) return 1;
         QB_TRY(cudaEventRecord(h->ev[0], h->stream));
         const Rows pr{h->tok, h->pos, h->slot};
-        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b, prompt_len % QB == 0) ||
+        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b,
+                            prompt_len % TQ == 0 ? 2 : (prompt_len % QB == 0 ? 1 : 0)) ||
             enqueue_sample(h, pr, b, h->proj_src))
             return 1;
         QB_TRY(cudaEventRecord(h->ev[1], h->stream));
@@ -1260,7 +1503,7 @@ extern "C" int mocha_q8b_bench_prefill(mocha_q8b *h, int n, unsigned seed, int w
     const int last = n - 1;
     if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, 1, &last)) return 1;
     const Rows r{h->tok, h->pos, h->slot};
-    const bool block = n % QB == 0;
+    const int block = n % TQ == 0 ? 2 : (n % QB == 0 ? 1 : 0);
     for (int i = 0; i < warmup; i++)
         if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block)) return 1;
     QB_TRY(cudaEventRecord(h->ev[0], h->stream));

@@ -46,6 +46,16 @@ def test_prefill_logits(batch, oracle):
     print("prefill 40 max abs logit error", err)
 
 
+def test_prefill_tensor_core_attention(batch, oracle):
+    """A 256-token prompt runs its attention on the tensor cores (blocks of 128 rows)."""
+    prompt = np.random.default_rng(17).integers(0, VOCAB, 256).tolist()
+    got = batch.prefill(4, prompt)
+    ref = oracle_prompt_logits(oracle, prompt)
+    err = close(got, ref)
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+    print("prefill 256 (tcgen05 attention) max abs logit error", err)
+
+
 def test_rows_of_several_slots(batch, oracle):
     rng = np.random.default_rng(12)
     p1 = rng.integers(0, VOCAB, 9).tolist()
