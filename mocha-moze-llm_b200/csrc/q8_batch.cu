@@ -74,6 +74,18 @@ struct Rows {
     const int *tok, *pos, *slot;
 };
 
+// bf16 pairs of the KV cache for the tensor-core prompt attention: K as
+// [slot][layer][kv head][pos][64] (the fp32 cache's indexing) and V transposed as
+// [slot][layer][kv head][64][pos].
+struct KvShadow {
+    bf16 *k_hi, *k_lo, *vt_hi, *vt_lo;
+};
+
+__host__ __device__ __forceinline__ size_t vt_off(int slot, int layer, int kvh, int d, int pos)
+{
+    return ((((size_t)slot * LAYERS + layer) * KV_HEADS + kvh) * HEAD_DIM + d) * CONTEXT + pos;
+}
+
 // ---- row kernels ----------------------------------------------------------------------
 
 // Limbs of a DIM-wide GEMM input: int8 [rows * 3][DIM] and group scales [rows][DIM/64].
@@ -141,7 +153,7 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
                                                           const float *__restrict__ bias, Rows rows,
                                                           const float *__restrict__ rope_cos,
                                                           const float *__restrict__ rope_sin, float *q, float *kc,
-                                                          float *vc, int layer)
+                                                          float *vc, int layer, KvShadow sh)
 {
     pdl_enter();
     const int t = blockIdx.x, j = threadIdx.x;
@@ -173,6 +185,9 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
         float *v = vc + kv_off(slot, layer, head, pos);
         v[i] = d0;
         v[i + 32] = d1;
+        mb::tc::split_bf16(d0, sh.vt_hi[vt_off(slot, layer, head, i, pos)], sh.vt_lo[vt_off(slot, layer, head, i, pos)]);
+        mb::tc::split_bf16(d1, sh.vt_hi[vt_off(slot, layer, head, i + 32, pos)],
+                           sh.vt_lo[vt_off(slot, layer, head, i + 32, pos)]);
         return;
     }
     const float cs = __ldg(rope_cos + pos * 32 + i), sn = __ldg(rope_sin + pos * 32 + i);
@@ -182,9 +197,11 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
         q[(size_t)t * DIM + head * HEAD_DIM + i] = a * 0.125f;
         q[(size_t)t * DIM + head * HEAD_DIM + i + 32] = b * 0.125f;
     } else {
-        float *k = kc + kv_off(slot, layer, head, pos);
-        k[i] = a;
-        k[i + 32] = b;
+        const size_t o = kv_off(slot, layer, head, pos);
+        kc[o + i] = a;
+        kc[o + i + 32] = b;
+        mb::tc::split_bf16(a, sh.k_hi[o + i], sh.k_lo[o + i]);
+        mb::tc::split_bf16(b, sh.k_hi[o + i + 32], sh.k_lo[o + i + 32]);
     }
 }
 
@@ -252,11 +269,11 @@ __global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q,
 
 // Combine the chunks of one (row, head) into the attention output, as limbs for the O
 // GEMM (one warp, two dims per lane: the head is one 64-group).
-__global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out)
+__global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out, int per)
 {
     pdl_enter();
     const int h = blockIdx.x, t = blockIdx.y, d = 2 * threadIdx.x;
-    const int nc = rows.pos[t] / CHUNK + 1;
+    const int nc = rows.pos[t] / per + 1;  // partials of `per` keys each
     const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
     float m = -INFINITY;
     for (int c = 0; c < nc; c++) m = fmaxf(m, p[c * PART]);
@@ -299,20 +316,27 @@ __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, 
 // ---- prompt attention on the tensor cores ---------------------------------------------
 //
 // One CTA per (block of 128 consecutive rows of one slot at positions p0..p0+127, p0 a
-// multiple of 128; query head h).  For every chunk of 64 keys 0..p0+127:
-//   K (and V, transposed) are read from the fp32 cache and written as bf16 pairs
-//   (hi = bf16(v), lo = bf16(v - hi)) in the 128-byte-swizzled K-major layout;
-//   S = Q K^T (q already carries the 0.125) comes from three tcgen05 MMAs
-//   (hi*hi + hi*lo + lo*hi) into TMEM; each of the 128 threads owns one query row:
-//   it reads its 64 scores, applies the causal mask and the online softmax, and writes
-//   its P row as a bf16 pair; O_c = P V comes from three more MMAs; the thread folds
-//   O_c into its fp32 output row.  The output row is one 64-group of the O GEMM input:
-//   it leaves as int8 limbs.
+// multiple of 128; query head h; span z of up to 256 keys).  Keys come as bf16 pairs
+// from the cache shadow (written by k_qkv_post) through TMA into a two-stage ring; for
+// each chunk of 64 keys, S = Q K^T (q carries the 0.125) is three tcgen05 MMAs
+// (hi*hi + hi*lo + lo*hi) into TMEM; each of the 128 threads owns one query row: causal
+// mask and online softmax over its 64 scores, P written as a bf16 pair in the
+// 128-byte-swizzled layout; O_c = P V is three more MMAs; the thread folds O_c into its
+// fp32 row.  The span's (max, sum, 64 weighted sums) go to the partial buffer and
+// k_attn_combine merges the spans.
 constexpr int TQ = 128;           // queries per CTA
 constexpr int TK = 64;            // keys per chunk
+constexpr int TSPAN = 256;        // keys per CTA
+constexpr int TSPLIT = CONTEXT / TSPAN;
 constexpr uint32_t kTileQ = TQ * HEAD_DIM * 2;   // 16 KiB: one bf16 [128][64] tile
 constexpr uint32_t kTileK = TK * HEAD_DIM * 2;   // 8 KiB: one bf16 [64][64] tile
-constexpr size_t TC_SMEM = 1024 + 2 * kTileQ /*Q*/ + 2 * kTileK /*K*/ + 2 * kTileK /*Vt*/ + 2 * kTileQ /*P*/ + 64;
+constexpr uint32_t kStageKV = 4 * kTileK;        // K hi, K lo, Vt hi, Vt lo
+constexpr size_t TC_SMEM = 1024 + 2 * kTileQ /*Q*/ + 2 * kStageKV + 2 * kTileQ /*P*/ + 128;
+
+struct AttnMaps {
+    CUtensorMap k_hi, k_lo;    // [slot*LAYERS*KV_HEADS*CONTEXT][64], box {64, 64}
+    CUtensorMap vt_hi, vt_lo;  // [slot*LAYERS*KV_HEADS*64][CONTEXT], box {64, 64}
+};
 
 // byte offset of element (r, c) of a [rows][64] bf16 tile in the SW128 K-major layout
 MB_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2); }
@@ -328,29 +352,44 @@ MB_DEV void put8(uint8_t *tile, int r, int c0, const float (&v)[8], uint8_t *til
 }
 
 __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, Rows rows,
-                                                  const float *__restrict__ kc, const float *__restrict__ vc,
-                                                  int layer, Limbs out, int *err)
+                                                  const __grid_constant__ AttnMaps maps, int layer,
+                                                  float *__restrict__ part, int *err)
 {
     pdl_enter();
+    const int h = blockIdx.y, g = h / GQA, t0 = blockIdx.x * TQ, z = blockIdx.z;
+    const int slot = rows.slot[t0], p0 = rows.pos[t0];
+    const int key_begin = z * TSPAN, key_end = min(key_begin + TSPAN, p0 + TQ);
+    if (key_begin >= key_end) return;  // this span lies after the block's last query
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *q_hi = sm, *q_lo = q_hi + kTileQ, *k_hi = q_lo + kTileQ, *k_lo = k_hi + kTileK;
-    uint8_t *v_hi = k_lo + kTileK, *v_lo = v_hi + kTileK, *p_hi = v_lo + kTileK, *p_lo = p_hi + kTileQ;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(p_lo + kTileQ);  // [0] S done, [1] O done, [2] drain
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 3);
+    uint8_t *q_hi = sm, *q_lo = q_hi + kTileQ, *kv = q_lo + kTileQ;
+    uint8_t *p_hi = kv + 2 * kStageKV, *p_lo = p_hi + kTileQ;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(p_lo + kTileQ);  // [0,1] stage full, [2] S, [3] O, [4] drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 5);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    const int h = blockIdx.y, g = h / GQA, t0 = blockIdx.x * TQ;
-    const int slot = rows.slot[t0], p0 = rows.pos[t0];
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int nch = (key_end - key_begin + TK - 1) / TK;
+    const int krow0 = (((slot * LAYERS + layer) * KV_HEADS + g) * CONTEXT);  // K map row of key 0
+    const int vrow0 = (((slot * LAYERS + layer) * KV_HEADS + g) * HEAD_DIM);  // Vt map row of dim 0
+    int issued = 0, landed_n = 0;  // thread 0: chunks whose copies were issued / have landed
+    auto issue = [&](int c) {  // TMA of chunk c into stage c & 1 (thread 0)
+        issued = c + 1;
+        const int st = c & 1, k0 = key_begin + c * TK;
+        uint8_t *b = kv + st * kStageKV;
+        mb::as::mbar_expect_tx(&bar[st], kStageKV);
+        mb::as::tma_load_2d(b, &maps.k_hi, 0, krow0 + k0, &bar[st]);
+        mb::as::tma_load_2d(b + kTileK, &maps.k_lo, 0, krow0 + k0, &bar[st]);
+        mb::as::tma_load_2d(b + 2 * kTileK, &maps.vt_hi, k0, vrow0, &bar[st]);
+        mb::as::tma_load_2d(b + 3 * kTileK, &maps.vt_lo, k0, vrow0, &bar[st]);
+    };
     if (tid == 0) {
-        mb::as::mbar_init(&bar[0], 1);
-        mb::as::mbar_init(&bar[1], 1);
-        mb::as::mbar_init(&bar[2], 1);
+        for (int i = 0; i < 5; i++) mb::as::mbar_init(&bar[i], 1);
         *abort = 0;
         mb::as::fence_barrier_init();
+        issue(0);
+        if (nch > 1) issue(1);
     }
     if (warp == 0) mb::as::tmem_alloc(tmem_slot, 128);
-    // Q tile: 128 rows x 8 chunks of 8 dims
     for (int ci = tid; ci < TQ * 8; ci += TQ) {
         const int r = ci >> 3, c0 = (ci & 7) * 8;
         const float4 *src = reinterpret_cast<const float4 *>(q + (size_t)(t0 + r) * DIM + h * HEAD_DIM + c0);
@@ -358,88 +397,77 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         put8(q_hi, r, c0, v, q_lo);
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mb::as::tc_fence_before();
     __syncthreads();
     mb::as::tc_fence_after();
     const uint32_t tmem = *tmem_slot, tm_s = tmem, tm_o = tmem + 64;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     constexpr uint32_t idesc = mb::as::idesc_bf16_f32(TQ, TK);
-    const int row = tid, qpos = p0 + row;  // this thread's query
+    const int row = tid, qpos = p0 + row;
     float o[HEAD_DIM];
 #pragma unroll
     for (int d = 0; d < HEAD_DIM; d++) o[d] = 0.f;
     float m = -INFINITY, l = 0.f;
-    const int nchunks = (p0 + TQ - 1) / TK + 1;
     bool ok = true;
-    for (int c = 0; c < nchunks; c++) {
-        const int k0 = c * TK;
-        const size_t base = kv_off(slot, layer, g, k0);
-        // K: [key][dim]; V transposed: [dim][key] (lanes take consecutive dims: coalesced reads)
-        for (int ci = tid; ci < TK * 8; ci += TQ) {
-            const int key = ci >> 3, c0 = (ci & 7) * 8;
-            const float4 *src = reinterpret_cast<const float4 *>(kc + base + (size_t)key * HEAD_DIM + c0);
-            const float4 a = src[0], b = src[1];
-            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            put8(k_hi, key, c0, v, k_lo);
-        }
-        for (int ci = tid; ci < HEAD_DIM * 8; ci += TQ) {
-            const int d = ci & 63, kg = ci >> 6;
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = vc[base + (size_t)(kg * 8 + i) * HEAD_DIM + d];
-            put8(v_hi, d, kg * 8, v, v_lo);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mb::as::tc_fence_before();
-        __syncthreads();
+    for (int c = 0; c < nch; c++) {
+        const int st = c & 1, k0 = key_begin + c * TK;
+        uint8_t *kvs = kv + st * kStageKV;
         if (tid == 0) {
-            mb::as::tc_fence_after();
-            const uint32_t qa = mb::as::smem_u32(q_hi), qb = mb::as::smem_u32(q_lo);
-            const uint32_t ka = mb::as::smem_u32(k_hi), kb = mb::as::smem_u32(k_lo);
+            const bool landed = mb::as::mbar_wait(&bar[st], (c >> 1) & 1, abort);
+            if (landed) {
+                landed_n = c + 1;
+                mb::as::tc_fence_after();
+                const uint32_t qa = mb::as::smem_u32(q_hi), qb = mb::as::smem_u32(q_lo);
+                const uint32_t ka = mb::as::smem_u32(kvs), kb = ka + kTileK;
 #pragma unroll
-            for (int kk = 0; kk < HEAD_DIM / 16; kk++) {
-                const uint32_t off = kk * 32;
-                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(ka + off), idesc, kk > 0);
-                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(kb + off), idesc, true);
-                mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qb + off), mb::as::sw128_desc(ka + off), idesc, true);
+                for (int kk = 0; kk < HEAD_DIM / 16; kk++) {
+                    const uint32_t off = kk * 32;
+                    mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(ka + off), idesc, kk > 0);
+                    mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qa + off), mb::as::sw128_desc(kb + off), idesc, true);
+                    mb::as::mma_bf16(tm_s, mb::as::sw128_desc(qb + off), mb::as::sw128_desc(ka + off), idesc, true);
+                }
+                mb::as::mma_commit(&bar[2]);
+            } else {
+                *abort = 1;
             }
-            mb::as::mma_commit(&bar[0]);
         }
-        ok = mb::as::mbar_wait(&bar[0], c & 1, abort);
+        ok = mb::as::mbar_wait(&bar[2], c & 1, abort);
         mb::as::tc_fence_after();
         if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
             if (tid == 0) atomicCAS(err, 0, 31);
             ok = false;
             break;
         }
-        // scores of this row, causal mask, online softmax
-        float sc[TK];
-        {
-            uint32_t r16[16];
-#pragma unroll
-            for (int j = 0; j < TK / 16; j++) {
-                mb::as::tmem_ld16(tm_s + ((uint32_t)(warp * 32) << 16) + j * 16, r16);
-                mb::as::tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; i++) sc[j * 16 + i] = __uint_as_float(r16[i]);
-            }
-        }
+        // pass 1: row max of the masked scores; pass 2: exponentials, P row, sum
         float mx = m;
 #pragma unroll
-        for (int j = 0; j < TK; j++) {
-            if (k0 + j > qpos) sc[j] = -INFINITY;
-            mx = fmaxf(mx, sc[j]);
+        for (int j = 0; j < TK / 16; j++) {
+            uint32_t r16[16];
+            mb::as::tmem_ld16(tm_s + lane_base + j * 16, r16);
+            mb::as::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                if (k0 + j * 16 + i <= qpos) mx = fmaxf(mx, __uint_as_float(r16[i]));
         }
-        const float scale = expf(m - mx);
+        const float scale = __expf(m - mx);
         float sum = 0.f;
 #pragma unroll
-        for (int j0 = 0; j0 < TK; j0 += 8) {
-            float pv[8];
+        for (int j = 0; j < TK / 16; j++) {
+            uint32_t r16[16];
+            mb::as::tmem_ld16(tm_s + lane_base + j * 16, r16);
+            mb::as::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                pv[i] = expf(sc[j0 + i] - mx);
-                sum += pv[i];
+            for (int hh = 0; hh < 2; hh++) {
+                float pv[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int key = k0 + j * 16 + hh * 8 + i;
+                    pv[i] = key <= qpos ? __expf(__uint_as_float(r16[hh * 8 + i]) - mx) : 0.f;
+                    sum += pv[i];
+                }
+                put8(p_hi, row, j * 16 + hh * 8, pv, p_lo);
             }
-            put8(p_hi, row, j0, pv, p_lo);
         }
         l = l * scale + sum;
         m = mx;
@@ -451,7 +479,7 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         if (tid == 0) {
             mb::as::tc_fence_after();
             const uint32_t pa = mb::as::smem_u32(p_hi), pb = mb::as::smem_u32(p_lo);
-            const uint32_t va = mb::as::smem_u32(v_hi), vb = mb::as::smem_u32(v_lo);
+            const uint32_t va = mb::as::smem_u32(kvs + 2 * kTileK), vb = va + kTileK;
 #pragma unroll
             for (int kk = 0; kk < TK / 16; kk++) {
                 const uint32_t off = kk * 32;
@@ -459,63 +487,42 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
                 mb::as::mma_bf16(tm_o, mb::as::sw128_desc(pa + off), mb::as::sw128_desc(vb + off), idesc, true);
                 mb::as::mma_bf16(tm_o, mb::as::sw128_desc(pb + off), mb::as::sw128_desc(va + off), idesc, true);
             }
-            mb::as::mma_commit(&bar[1]);
+            mb::as::mma_commit(&bar[3]);
         }
-        ok = mb::as::mbar_wait(&bar[1], c & 1, abort);
+        ok = mb::as::mbar_wait(&bar[3], c & 1, abort);
         mb::as::tc_fence_after();
         if (__syncthreads_or(!ok)) {
             if (tid == 0) atomicCAS(err, 0, 32);
             ok = false;
             break;
         }
-        {
+#pragma unroll
+        for (int j = 0; j < HEAD_DIM / 16; j++) {
             uint32_t r16[16];
+            mb::as::tmem_ld16(tm_o + lane_base + j * 16, r16);
+            mb::as::tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < HEAD_DIM / 16; j++) {
-                mb::as::tmem_ld16(tm_o + ((uint32_t)(warp * 32) << 16) + j * 16, r16);
-                mb::as::tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; i++) o[j * 16 + i] += __uint_as_float(r16[i]);
-            }
+            for (int i = 0; i < 16; i++) o[j * 16 + i] += __uint_as_float(r16[i]);
         }
         mb::as::tc_fence_before();
-        __syncthreads();  // K, V and P may be rewritten
+        __syncthreads();  // stage st, S and P are free again
+        if (tid == 0 && c + 2 < nch) issue(c + 2);
     }
     if (!ok && tid == 0) {
-        // every MMA issued so far has finished before TMEM and shared memory go away
-        mb::as::mma_commit(&bar[2]);
+        // every MMA issued so far has finished, and the copies in flight have landed,
+        // before TMEM and shared memory go away
+        mb::as::mma_commit(&bar[4]);
         const volatile int never = 0;
-        mb::as::mbar_wait(&bar[2], 0, &never);
+        mb::as::mbar_wait(&bar[4], 0, &never);
+        for (int k = landed_n; k < issued; k++) mb::as::mbar_wait(&bar[k & 1], (k >> 1) & 1, &never);
     }
     if (ok) {
-        // the row's 64 outputs are one group: limbs without any cross-thread reduction
-        const float inv = 1.f / l;
-        float mxa = 0.f;
+        float *out = part + (((size_t)(t0 + row) * HEADS + h) * NCHUNK + z) * PART;
+        // a partial is PART = 66 floats: its payload is 8-byte aligned, so float2 stores
+        out[0] = m;
+        out[1] = l;
 #pragma unroll
-        for (int d = 0; d < HEAD_DIM; d++) {
-            o[d] *= inv;
-            mxa = fmaxf(mxa, fabsf(o[d]));
-        }
-        const float sinv = mxa > 0.f ? 127.f / mxa : 0.f;
-        int8_t *dst = out.q + (size_t)(t0 + row) * 3 * DIM + h * HEAD_DIM;
-#pragma unroll
-        for (int d0 = 0; d0 < HEAD_DIM; d0 += 4) {
-            float q0[4], q1[4], q2[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float qv = o[d0 + e] * sinv;
-                q0[e] = fminf(fmaxf(rintf(qv), -127.f), 127.f);
-                const float r1 = (qv - q0[e]) * 254.f;
-                q1[e] = fminf(fmaxf(rintf(r1), -127.f), 127.f);
-                q2[e] = fminf(fmaxf(rintf((r1 - q1[e]) * 254.f), -127.f), 127.f);
-            }
-            *reinterpret_cast<char4 *>(dst + d0) = make_char4((int8_t)q0[0], (int8_t)q0[1], (int8_t)q0[2], (int8_t)q0[3]);
-            *reinterpret_cast<char4 *>(dst + DIM + d0) =
-                make_char4((int8_t)q1[0], (int8_t)q1[1], (int8_t)q1[2], (int8_t)q1[3]);
-            *reinterpret_cast<char4 *>(dst + 2 * DIM + d0) =
-                make_char4((int8_t)q2[0], (int8_t)q2[1], (int8_t)q2[2], (int8_t)q2[3]);
-        }
-        out.s[(size_t)(t0 + row) * (DIM / GROUP) + h] = mxa / 127.f;
+        for (int d = 0; d < HEAD_DIM; d += 2) *reinterpret_cast<float2 *>(out + 2 + d) = make_float2(o[d], o[d + 1]);
     }
     mb::as::tc_fence_before();
     __syncthreads();
@@ -902,6 +909,8 @@ struct mocha_q8b {
     int8_t *lhq = nullptr;          // SwiGLU output limbs [rows * 3][HIDDEN]
     float *lhs = nullptr;           // and their scales [rows][HIDDEN / 64]
     float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    qb::KvShadow kvs{};
+    qb::AttnMaps amaps{};
     int *tok = nullptr, *pos = nullptr, *slot = nullptr;            // prompt rows [max_rows]
     int *ntok = nullptr, *npos = nullptr, *nslot = nullptr;         // decode rows [slots]
     int *proj_src = nullptr, *proj_dst = nullptr, *ident = nullptr;  // [slots], [max_rows], [slots]
@@ -1017,8 +1026,10 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
             QB_TRY(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
             tc_done[h->device & 63] = true;
         }
-        return pdl(k_attn_tc, dim3(n / TQ, HEADS), TQ, TC_SMEM, h->stream, h->q, rows, h->kc, h->vc, layer, h->la,
-                   h->err);
+        if (pdl(k_attn_tc, dim3(n / TQ, HEADS, TSPLIT), TQ, TC_SMEM, h->stream, h->q, rows, h->amaps, layer, h->apart,
+                h->err))
+            return 1;
+        return pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la, TSPAN);
     }
     if (block) {
         if (!attr_done[h->device & 63]) {
@@ -1029,7 +1040,7 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
         return 0;
     }
     if (pdl(k_attn_chunk, dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream, h->q, rows, h->kc, h->vc, layer, h->apart)) return 1;
-    if (pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la)) return 1;
+    if (pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la, CHUNK)) return 1;
     return 0;
 }
 
@@ -1063,7 +1074,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
         const Layer &L = h->m.layer[l];
         if (mb::tq::launch(ps.qkv[l], n, s, &sp)) return 1;
         if (pdl(k_qkv_post, n, QKV_THREADS, 0, s, h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
-                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l)) return 1;
+                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l, h->kvs)) return 1;
         if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
         if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr)) return 1;
@@ -1233,7 +1244,18 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
         dalloc(&h->params, 1) || dalloc(&h->out_count, slots))
         return fail();
     const size_t kv = kv_off(slots, 0, 0, 0);
-    if (dalloc(&h->kc, kv) || dalloc(&h->vc, kv)) return fail();
+    if (dalloc(&h->kc, kv) || dalloc(&h->vc, kv) || dalloc(&h->kvs.k_hi, kv) || dalloc(&h->kvs.k_lo, kv) ||
+        dalloc(&h->kvs.vt_hi, kv) || dalloc(&h->kvs.vt_lo, kv))
+        return fail();
+    if (mb::tc::make_map_bf16(&h->amaps.k_hi, h->kvs.k_hi, (long long)slots * LAYERS * KV_HEADS * CONTEXT, HEAD_DIM,
+                              TK) ||
+        mb::tc::make_map_bf16(&h->amaps.k_lo, h->kvs.k_lo, (long long)slots * LAYERS * KV_HEADS * CONTEXT, HEAD_DIM,
+                              TK) ||
+        mb::tc::make_map_bf16(&h->amaps.vt_hi, h->kvs.vt_hi, (long long)slots * LAYERS * KV_HEADS * HEAD_DIM, CONTEXT,
+                              HEAD_DIM) ||
+        mb::tc::make_map_bf16(&h->amaps.vt_lo, h->kvs.vt_lo, (long long)slots * LAYERS * KV_HEADS * HEAD_DIM, CONTEXT,
+                              HEAD_DIM))
+        return fail();
     if (cudaMemset(h->kc, 0, sizeof(float) * kv) || cudaMemset(h->vc, 0, sizeof(float) * kv) ||
         cudaMemset(h->err, 0, sizeof(int)) || cudaMemset(h->out_count, 0, sizeof(int) * slots) ||
         cudaMemset(h->st, 0, sizeof(sampling::SeqState) * slots))
@@ -1278,7 +1300,8 @@ extern "C" int mocha_q8b_close(mocha_q8b *h)
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->g_step) cudaGraphExecDestroy(h->g_step);
     void *ptrs[] = {h->d_file, h->bqkv, h->x, h->q, h->part, h->apart, h->logits, h->lx.q, h->lx.s, h->la.q,
-                    h->la.s, h->lhq, h->lhs, h->lhead.q, h->lhead.s, h->kc, h->vc, h->rope_cos, h->rope_sin, h->tok,
+                    h->la.s, h->lhq, h->lhs, h->lhead.q, h->lhead.s, h->kc, h->vc, h->kvs.k_hi, h->kvs.k_lo,
+                    h->kvs.vt_hi, h->kvs.vt_lo, h->rope_cos, h->rope_sin, h->tok,
                     h->pos, h->slot, h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->err,
                     h->keys, h->st, h->params, h->out_tokens, h->out_count};
     for (void *p : ptrs)

@@ -249,6 +249,11 @@ int setup_attr()
 
 }  // namespace
 
+int make_map_bf16(CUtensorMap *map, const void *base, long long rows, long long inner, int box_rows)
+{
+    return make_map(map, base, rows, inner, box_rows);
+}
+
 int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int M, int K,
               const __nv_bfloat16 *x_hi, const __nv_bfloat16 *x_lo, int n_max, float *d, long long ldd, int splits,
               int *err)

@@ -68,6 +68,10 @@ int gemm_plan(Gemm *g, const __nv_bfloat16 *w_hi, const __nv_bfloat16 *w_lo, int
 // for a fixed n.
 int gemm_launch(const Gemm &g, int n, cudaStream_t s, Split *used = nullptr);
 
+// Tensor map of a row-major bf16 [rows][inner] array with boxes of {64, box_rows} and
+// 128-byte swizzle (inner % 64 == 0).  Returns 0 on success.
+int make_map_bf16(CUtensorMap *map, const void *base, long long rows, long long inner, int box_rows);
+
 // Weights: bf16 pair of q*s for a grouped-Q8 matrix (int8 [M][K], fp32 scale per 64).
 int split_weights(const int8_t *q, const float *scales, size_t count, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
                   cudaStream_t s);
