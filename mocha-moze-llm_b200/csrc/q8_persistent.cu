@@ -2,29 +2,44 @@
 //
 // One cooperative launch of 148 CTAs (one per SM) runs the whole token.
 //
-// Weights: warp 0 of every CTA streams that CTA's weights -- laid out at set-up as
-// one contiguous region per CTA, in consumption order -- through a 4-slot
-// shared-memory ring with cp.async.bulk copies completed on mbarriers.  Each chunk
-// carries a 16-byte header (kind, layer, row range) and its rows' biases; chunks that
-// start a normalised phase also receive the RMSNorm gain by a second bulk copy (an
-// L2 hit: every CTA reads the same gain).  Weights do not depend on activations, so
-// the stream runs ahead of the dependency chain by up to the ring depth.
+// Weights: every CTA streams its own weights -- laid out at set-up as one contiguous
+// region per CTA, in consumption order -- through a 4-slot shared-memory ring with
+// cp.async.bulk copies completed on mbarriers; thread 0 starts the copy of chunk
+// k + 4 as soon as the consumers give slot k back (the first four at the start).  Each chunk
+// carries a 16-byte header (kind, layer, range) and its rows' scales and biases;
+// chunks that start a normalised phase also receive the RMSNorm gain by a second bulk
+// copy (an L2 hit: every CTA reads the same gain).  Weights do not depend on
+// activations, so the stream runs ahead of the dependency chain by up to the ring
+// depth.
 //
-// Activations: the 16 consumer warps exchange every cross-CTA value as a 64-bit data
+// Matrix-vector products run on the int8 tensor cores (mma.sync m16n8k32): the
+// stream stores every matrix as 16-row tiles already in the A-fragment order of that
+// instruction (a lane's 16 bytes per 32-column step), and the activation enters as
+// three int8 limbs per 64-column group, x = s (a0 + a1/254 + a2/254^2) with
+// s = max|x| / 127 -- the B fragment's columns 0..2.  The int32 products of one group
+// are exact; they are combined as (254 D0 + D1 + D2/254) * s/254 and scaled by the
+// weight group's fp32 scale.  The (tile, group) units of a chunk are split evenly over
+// the 16 consumer warps and the per-warp row sums added in warp order.
+//
+// Activations: the 16 warps exchange every cross-CTA value as a 64-bit data
 // word (float | tag << 32, tag = epoch << 8 | layer << 3 | phase) written with one
-// relaxed store and polled directly by its readers.  There are no counters, fences or
-// second loads between phases; each reader waits exactly for the words it needs.
+// relaxed store and polled directly by its readers; words read by every CTA are
+// written to four replicas.  There are no counters, fences or second loads between
+// phases; each reader waits exactly for the words it needs.
 // Per layer: QKV (+bias, split-half RoPE, KV write) -> attention split over the
 // positions of each query head (K/V of past positions are prefetched with cp.async
-// before the query exists) -> O + residual -> RMSNorm -> gate/up + SwiGLU ->
-// down + residual.  The vocabulary head is fused with the repetition penalty, the
-// control mask and a per-CTA top-k; the last CTA to finish (one atomic ticket)
-// merges the candidates, draws the token and advances the epoch.
+// before the query exists) -> O + residual -> RMSNorm -> gate/up + SwiGLU on this
+// CTA's own slice of the hidden units -> the down projection of that slice for all
+// 896 rows (split-K) -> each CTA sums the 148 partials of its own rows + residual.
+// The vocabulary head is fused with the repetition penalty, the control mask and a
+// per-CTA top-k; the last CTA to finish (one atomic ticket) merges the candidates,
+// draws the token and advances the epoch.
 //
 // Every wait is bounded (~2 s of clock cycles); on expiry the kernel records an
 // error word (device and mapped host memory), drains its own bulk copies and exits.
-// The arithmetic is the reference's (src/minimind.cu:67-123, src/minimind.cpp:51-82):
-// fp32 activations, int8 weights widened exactly, one fp32 scale per 64 weights.
+// The arithmetic follows the reference (src/minimind.cu:67-123, src/minimind.cpp:51-82):
+// fp32 activations between the matrix products, int8 weights, one fp32 scale per 64
+// weights; the products themselves use the exact integer limb form above.
 #include <float.h>
 #include <math.h>
 #include <stdlib.h>
@@ -42,39 +57,69 @@ namespace {
 using namespace q8;
 constexpr int kNT = kConsumerWarps * 32;  // consumer threads
 constexpr long long kTimeoutCycles = 4000000000LL;
+constexpr long long kErrorPollCycles = 50000;  // spin before a wait starts reading the error flag
 constexpr int kQkvPairs = (DIM + 2 * KV) / 2;  // 576
-constexpr int kGateupPerChunk = 17;            // pairs: 34 rows of 896 + header < kGainOff
-constexpr int kHeadPerChunk = 34;              // rows
+constexpr int kSteps = DIM / 32;               // 32-column MMA steps of a 896-wide row
+constexpr int kGroups = DIM / GROUP;           // 14 scale groups of a 896-wide row
+constexpr int kTileBytes = kSteps * 32 * 16;   // one 16-row tile of a 896-wide matrix
+constexpr int kHalfBytes = kSteps * 32 * 8;    // one 8-row tile (rows 8..15 absent)
+constexpr int kGateupPerChunk = 16;            // hidden units per gate/up chunk (two tiles)
+constexpr int kHeadPerChunk = 32;              // vocabulary rows per head chunk (two tiles)
 constexpr int kHeadSlice = 1040;               // >= ceil(VOCAB / kCTAs)
+constexpr int kDownTiles = DIM / 16;           // 56 row tiles of the down projection
 constexpr int kPartWords = HEADS * kMaxSplit * ATTN_PARTIAL;
+constexpr int kGpStride = kConsumerWarps + 1;  // padded: conflict-free row sums
+constexpr int kKStride = HEAD_DIM + 4;         // cached key row in shared memory: conflict-free float4 reads
+constexpr int kPvGroups = kNT / HEAD_DIM;      // position groups of the P.V product
+constexpr int kStrideKv = replica_stride(2 * KV);
+constexpr int kStridePart = replica_stride(kPartWords);
+constexpr int kStrideDim = replica_stride(DIM);
+constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
+static_assert(DIM % 64 == 0 && kCTAs % 4 == 0, "layout");
 
-enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_H = 3, PH_X = 4 };
+enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_D = 3, PH_X = 4 };
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
     __align__(16) float xs[DIM];  // residual (x_in, then x_mid) of the current layer
     __align__(16) float ns[DIM];  // normalised input / attention output
     union __align__(16) {
-        float hs[HIDDEN];          // down-projection input
         float part[kPartWords];    // gathered attention partials
         struct {
-            float k[kAttnLenMax][HEAD_DIM];
+            float k[kAttnLenMax][kKStride];
             float v[kAttnLenMax][HEAD_DIM];
             float q[HEAD_DIM];
             float e[kAttnLenMax + 1];
+            float pv[kPvGroups][HEAD_DIM];
         } att;
         float hl[kHeadSlice];      // this CTA's slice of the logits
     } u;
-    float red[kConsumerWarps][8];
+    __align__(16) uint2 bf[kSteps][32];  // B fragments of the current 896-wide input (lanes 12..31 zero)
+    __align__(16) uint2 bfh[2][32];      // B fragments of the SwiGLU slice (lanes 12..31 zero)
+    float gp[5 * 16][kGpStride];   // per-warp partial row sums of the current job (<= 5 tiles)
+    float sxs[kGroups];            // input scale / 254 per group
+    __align__(16) float hst[2][32];  // this CTA's SwiGLU outputs at their column in each down step
+    float sh;                      // their scale / 254
+    __align__(16) float red[kConsumerWarps][8];  // also read as 64-bit keys (block_max)
     float rc[HEAD_DIM / 2], rs[HEAD_DIM / 2];  // RoPE cos/sin at pos
-    Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors (producer)
-    unsigned long long full[kSlots], empty[kSlots];
+    Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors
+    unsigned long long full[kSlots];
     int flag;
     int iters;  // poll iterations of the last traced gather
     int token, pos;
-    volatile int issued;         // chunks the producer has started copying
-    volatile int producer_done;  // the producer has left its loop
+    int issued;                  // chunks whose bulk copy has been started
 };
+static_assert(sizeof(Smem) <= 232448, "shared memory per CTA");
+
+// Hidden units whose gate/up rows and down-projection columns CTA c owns: the
+// 32-unit block [32c, 32c + 32) and, for the last 16 CTAs, an 8-unit piece of the four
+// spare blocks, [4736 + 8j, 4736 + 8j + 8) for CTA 132 + j (4864 = 148 * 32 + 16 * 8).
+// Down-projection step 0 covers the CTA's block, step 1 the spare block holding its
+// piece (the other 24 columns enter as zeros).
+constexpr int kSpareFirst = kCTAs - (HIDDEN - 32 * kCTAs) / 8;  // 132
+static_assert(32 * kCTAs + 8 * (kCTAs - kSpareFirst) == HIDDEN, "hidden slices");
+__host__ __device__ inline bool has_spare(int c) { return c >= kSpareFirst; }
+__host__ __device__ inline int spare_lo(int c) { return 32 * kCTAs + 8 * (c - kSpareFirst); }
 
 // ---- low-level primitives --------------------------------------------------
 
@@ -135,17 +180,26 @@ MB_DEV void fail(Sync *sy, unsigned *host_error, unsigned code)
     __threadfence_system();
 }
 
+// A wait that has spun for `spun` cycles gives up when another CTA has recorded an
+// error -- read only once the wait is long, since the flag costs an L2 round trip --
+// or when the bound expires (recorded here with `code`).
+MB_DEV bool give_up(Sync *sy, unsigned *host_error, long long spun, unsigned code)
+{
+    if (spun < kErrorPollCycles) return false;
+    if (spun > kTimeoutCycles) {
+        fail(sy, host_error, code);
+        return true;
+    }
+    return ld_volatile(&sy->error) != 0;
+}
+
 MB_DEV bool mbar_wait(unsigned long long *bar, uint32_t parity, Sync *sy, unsigned *host_error)
 {
     if (mbar_test(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
         if (mbar_test(bar, parity)) return true;
-        if (ld_volatile(&sy->error)) return false;
-        if (clock64() - t0 > kTimeoutCycles) {
-            fail(sy, host_error, 2);
-            return false;
-        }
+        if (give_up(sy, host_error, clock64() - t0, 2)) return false;
     }
 }
 
@@ -178,6 +232,13 @@ MB_DEV void dw_store(unsigned long long *p, float v, uint32_t tag)
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
+// the same word into every replica of an array whose copies are `stride` words apart
+MB_DEV void dw_store_rep(unsigned long long *p, int stride, float v, uint32_t tag)
+{
+#pragma unroll
+    for (int r = 0; r < kReplicas; r++) dw_store(p + r * stride, v, tag);
+}
+
 MB_DEV unsigned long long dw_load(const unsigned long long *p)
 {
     unsigned long long w;
@@ -194,6 +255,10 @@ struct Ctx {
     Sync *sy;
     unsigned *host_error;
     int ct, cw, lane;
+    int rep;                        // replica this CTA reads
+    const uint8_t *stream, *blob;   // this step's weight stream and the model file (gains)
+    uint32_t nchunks;               // chunks this CTA streams in this step
+    uint64_t policy;                // L2 evict-first for the stream
 };
 
 // 32-byte relaxed load of four data words (one L2 request instead of four)
@@ -248,12 +313,7 @@ MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag
         it++;
         if (t0 == 0) {
             t0 = clock64();
-        } else if (clock64() - t0 > kTimeoutCycles) {
-            fail(c.sy, c.host_error, 1);
-            ok = 0;
-            break;
-        }
-        if (ld_volatile(&c.sy->error)) {
+        } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
             ok = 0;
             break;
         }
@@ -273,70 +333,272 @@ MB_DEV bool gather(Ctx &c, const unsigned long long *src, int n, uint32_t tag, f
     return gather_if<E>(c, src, n, tag, dst, All{}, iters);
 }
 
-// y = (x * s) * g, s = 1/sqrt(sum(x^2)/DIM + eps); identical bits in every CTA
-MB_DEV void rmsnorm(Ctx &c, const float *xs, const float *gain, float *ns)
+// ---- int8 tensor-core matrix-vector products ------------------------------------
+
+MB_DEV void mma_s8(int (&d)[4], const uint4 &a, const uint2 &b)
 {
-    float ss = 0.f;
-    for (int i = c.ct; i < DIM; i += kNT) ss = fmaf(xs[i], xs[i], ss);
-    ss = mb::warp_sum(ss);
-    if (c.lane == 0) c.S.red[c.cw][0] = ss;
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y));
+}
+
+// The three int8 limbs of four values already multiplied by 127 / max|x|, packed one
+// limb per word: q = a0 + a1/254 + a2/254^2 + e, |e| <= 1/(2*254^2).  Rounding is to
+// nearest even through kMagic; |q| <= 127 (to within rounding) keeps every limb in
+// [-127, 127].
+MB_DEV void limbs4(const float (&q)[4], uint32_t &p0, uint32_t &p1, uint32_t &p2)
+{
+    uint32_t b[3][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float t0 = __fadd_rn(q[j], kMagic);
+        const float a0 = __fsub_rn(t0, kMagic);
+        const float r1 = __fmul_rn(__fsub_rn(q[j], a0), 254.f);
+        const float t1 = __fadd_rn(r1, kMagic);
+        const float a1 = __fsub_rn(t1, kMagic);
+        const float r2 = __fmul_rn(__fsub_rn(r1, a1), 254.f);
+        const float t2 = __fadd_rn(r2, kMagic);
+        b[0][j] = __float_as_uint(t0);
+        b[1][j] = __float_as_uint(t1);
+        b[2][j] = __float_as_uint(t2);
+    }
+    // low byte of each word (two's complement of the integer), four per word
+    p0 = __byte_perm(__byte_perm(b[0][0], b[0][1], 0x0040), __byte_perm(b[0][2], b[0][3], 0x0040), 0x5410);
+    p1 = __byte_perm(__byte_perm(b[1][0], b[1][1], 0x0040), __byte_perm(b[1][2], b[1][3], 0x0040), 0x5410);
+    p2 = __byte_perm(__byte_perm(b[2][0], b[2][1], 0x0040), __byte_perm(b[2][2], b[2][3], 0x0040), 0x5410);
+}
+
+// Column block of quantizer thread t < 224 of a 896-wide input: step ks = t >> 3, lane
+// column tig = (t >> 1) & 3, half h = t & 1 own columns 32 ks + 16 h + 4 tig + {0..3},
+// which are B-fragment register h of lanes 4n + tig (limb n).  The 16 threads of a
+// 64-column group form an aligned 16-lane block.
+MB_DEV int quant_col(int t) { return 32 * (t >> 3) + 16 * (t & 1) + 4 * ((t >> 1) & 3); }
+
+// Four values n[] of thread t (group max m already reduced over its 16 lanes) -> limbs
+// into S.bf and, from the group's first thread, the group scale / 254.
+MB_DEV void put_limbs(Smem &S, int t, const float (&n)[4], float m)
+{
+    const int ks = t >> 3, tig = (t >> 1) & 3, h = t & 1;
+    const float inv = m > 0.f ? 127.f / m : 0.f;
+    const float q[4] = {n[0] * inv, n[1] * inv, n[2] * inv, n[3] * inv};
+    uint32_t p0, p1, p2;
+    limbs4(q, p0, p1, p2);
+    if ((t & 15) == 0) S.sxs[ks >> 1] = m / (127.f * 254.f);
+    uint32_t *b = reinterpret_cast<uint32_t *>(&S.bf[ks][0]);
+    b[2 * tig + h] = p0;
+    b[2 * (4 + tig) + h] = p1;
+    b[2 * (8 + tig) + h] = p2;
+}
+
+MB_DEV float group_max16(float m)
+{
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+// RMSNorm of S.xs with `gain`, in the reference's rounding ((x * s) * g, s =
+// 1/sqrt(sum x^2 / DIM + eps)), quantized straight into S.bf / S.sxs; with keep the
+// normalised vector also goes to S.ns.  Consumer threads ct < 256 (warps 0..7) work;
+// every consumer thread calls it (two consumer barriers).
+MB_DEV void norm_quantize(Smem *Sp, int ct, const float *gain, int keep)
+{
+    Smem &S = *Sp;
+    const int t = min(ct, 223), col = quant_col(t), lane = ct & 31;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), g = x;
+    float pm = 0.f;
+    if (ct < 256) {
+        x = *reinterpret_cast<const float4 *>(S.xs + col);
+        g = *reinterpret_cast<const float4 *>(gain + col);
+        float ss = 0.f;
+        if (ct < 224) ss = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
+        pm = fmaxf(fmaxf(fabsf(x.x * g.x), fabsf(x.y * g.y)), fmaxf(fabsf(x.z * g.z), fabsf(x.w * g.w)));
+        ss = mb::warp_sum(ss);
+        pm = group_max16(pm);
+        if (lane == 0 && ct < 224) S.red[ct >> 5][0] = ss;
+    }
     cbar();
-    float sum = 0.f;
+    if (ct < 224) {
+        float sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) sum += c.S.red[w][0];
-    const float s = 1.0f / sqrtf(sum / DIM + RMS_EPS);
-    for (int i = c.ct; i < DIM; i += kNT) ns[i] = xs[i] * s * gain[i];
+        for (int w = 0; w < 7; w++) sum += S.red[w][0];
+        const float s = 1.0f / sqrtf(sum / DIM + RMS_EPS);
+        const float n[4] = {(x.x * s) * g.x, (x.y * s) * g.y, (x.z * s) * g.z, (x.w * s) * g.w};
+        if (keep) *reinterpret_cast<float4 *>(S.ns + col) = make_float4(n[0], n[1], n[2], n[3]);
+        put_limbs(S, t, n, pm * s);
+    }
     cbar();
 }
 
-// 16 int8 weights . 16 fp32 inputs held in registers (two accumulation chains)
-MB_DEV float dot16r(const int4 w, const float *xr)
+// Combine of the attention splits gathered in S.u.part (per head: running max, sum of
+// weights, 64 accumulators per split), quantized straight into S.bf / S.sxs.  Thread
+// t < 224 owns four consecutive output columns, all of one head.
+MB_DEV void combine_quantize(Smem *Sp, int ct, int splits)
 {
-    const uint32_t u[4] = {(uint32_t)w.x ^ 0x80808080u, (uint32_t)w.y ^ 0x80808080u, (uint32_t)w.z ^ 0x80808080u,
-                           (uint32_t)w.w ^ 0x80808080u};
-    float a0 = 0.f, a1 = 0.f;
+    Smem &S = *Sp;
+    if (ct < 256) {
+        const int t = min(ct, 223), col = quant_col(t), hd = col / HEAD_DIM, d = col % HEAD_DIM;
+        const float *p = S.u.part + (size_t)hd * kMaxSplit * ATTN_PARTIAL;
+        float mx = -INFINITY;
+        for (int s = 0; s < splits; s++) mx = fmaxf(mx, p[s * ATTN_PARTIAL]);
+        float lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < splits; s++) {
+            const float wgt = expf(p[s * ATTN_PARTIAL] - mx);
+            lsum = fmaf(wgt, p[s * ATTN_PARTIAL + 1], lsum);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        a0 = fmaf(mb::s8_lane(u[i], 0x7540), xr[4 * i + 0], a0);
-        a1 = fmaf(mb::s8_lane(u[i], 0x7541), xr[4 * i + 1], a1);
-        a0 = fmaf(mb::s8_lane(u[i], 0x7542), xr[4 * i + 2], a0);
-        a1 = fmaf(mb::s8_lane(u[i], 0x7543), xr[4 * i + 3], a1);
+            for (int j = 0; j < 4; j++) acc[j] = fmaf(wgt, p[s * ATTN_PARTIAL + 2 + d + j], acc[j]);
+        }
+        const float n[4] = {acc[0] / lsum, acc[1] / lsum, acc[2] / lsum, acc[3] / lsum};
+        float m = fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3])));
+        m = group_max16(m);
+        if (ct < 224) put_limbs(S, t, n, m);
     }
-    return a0 + a1;
+    cbar();
 }
 
-// A 896-wide row: lane owns 16-weight chunks lane and lane+32 (< 56); its 32 inputs
-// live in registers for every row of the phase.
-MB_DEV void load_x896(const float *ns, int lane, float *xr)
+// S.hst[ks][0..32) for ks < nks (one scale for all) -> S.bfh and S.sh; warp 0.
+MB_DEV void quantize_slice(Ctx &c, int nks)
 {
-    const float4 *n4 = reinterpret_cast<const float4 *>(ns);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float4 v = n4[lane * 4 + i];
-        xr[4 * i] = v.x;
-        xr[4 * i + 1] = v.y;
-        xr[4 * i + 2] = v.z;
-        xr[4 * i + 3] = v.w;
+    if (c.cw == 0) {
+        const int t = c.lane & 15, ks = t >> 3, tig = (t >> 1) & 3, h = t & 1;
+        const bool live = c.lane < 16 && ks < nks;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) v = *reinterpret_cast<const float4 *>(&c.S.hst[ks][16 * h + 4 * tig]);
+        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        m = mb::warp_max(m);
+        const float inv = m > 0.f ? 127.f / m : 0.f;
+        const float q[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
+        uint32_t p0, p1, p2;
+        limbs4(q, p0, p1, p2);
+        if (live) {
+            uint32_t *b = reinterpret_cast<uint32_t *>(&c.S.bfh[ks][0]);
+            b[2 * tig + h] = p0;
+            b[2 * (4 + tig) + h] = p1;
+            b[2 * (8 + tig) + h] = p2;
+        }
+        if (c.lane == 0) c.S.sh = m / (127.f * 254.f);
     }
+    cbar();
+}
+
+// D fragments of one group -> the limb combination (254 D0 + D1 + D2/254) of rows g
+// (v0) and g + 8 (v1); valid in lanes with tig == 0 (limb 2 comes from lane + 1).
+MB_DEV void combine(const int (&d)[4], float &v0, float &v1)
+{
+    const int e0 = __shfl_down_sync(0xffffffffu, d[0], 1), e2 = __shfl_down_sync(0xffffffffu, d[2], 1);
+    v0 = fmaf((float)e0, 1.f / 254.f, (float)(d[0] * 254 + d[1]));
+    v1 = fmaf((float)e2, 1.f / 254.f, (float)(d[2] * 254 + d[3]));
+}
+
+// The 16-row tiles of up to three chunks of 896-wide rows: tile t is tile t & 1 of
+// chunk t >> 1 (fragments [tile][kSteps][32 lanes][16 B], then the tile rows' scales
+// [16][kGroups] per tile), or, when half, the one 8-row tile of chunk 0 ([kSteps][32][8 B],
+// registers a0 and a2; scales [8][kGroups]).
+struct Tiles {
+    const uint8_t *frag[3];
+    const float *sc[3];
+    int T, half;
+};
+
+// Units (tile, group), U = kGroups * T, warp cw takes [U cw/16, U (cw+1)/16); its row
+// sums go to S.gp[row][cw] and row_sum() adds the warps of a row in order.
+MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
+{
+    Smem &S = *Sp;
+    constexpr int MAXU = 5;  // units per warp for T <= 5
+    const int U = kGroups * tl.T;
+    const int u0 = U * cw / kConsumerWarps, n = U * (cw + 1) / kConsumerWarps - u0;
+    const int g = lane >> 2, tig = lane & 3;
+    const int t0 = u0 / kGroups;
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float4 v = lane < 24 ? n4[(lane + 32) * 4 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        xr[16 + 4 * i] = v.x;
-        xr[16 + 4 * i + 1] = v.y;
-        xr[16 + 4 * i + 2] = v.z;
-        xr[16 + 4 * i + 3] = v.w;
+    for (int i = 0; i < MAXU; i++) {
+        if (i < n) {
+            const int u = u0 + i, t = u / kGroups, grp = u - t * kGroups, ch = t >> 1;
+            const uint8_t *fr = ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2];
+            const float *sc = ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2];
+            fr += (t & 1) * kTileBytes;
+            sc += (t & 1) * 16 * kGroups;
+            int d[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int ks = 2 * grp + h;
+                uint4 a;
+                if (tl.half) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(fr + ((size_t)ks * 32 + lane) * 8);
+                    a = make_uint4(v.x, 0u, v.y, 0u);
+                } else {
+                    a = *reinterpret_cast<const uint4 *>(fr + ((size_t)ks * 32 + lane) * 16);
+                }
+                mma_s8(d, a, S.bf[ks][lane]);
+            }
+            float v0, v1;
+            combine(d, v0, v1);
+            if (tig == 0) {
+                const float f = S.sxs[grp];
+                const float p0 = v0 * (sc[g * kGroups + grp] * f);
+                const float p1 = tl.half ? 0.f : v1 * (sc[(g + 8) * kGroups + grp] * f);
+                if (t == t0) {
+                    acc[0][0] += p0;
+                    acc[0][1] += p1;
+                } else {
+                    acc[1][0] += p0;
+                    acc[1][1] += p1;
+                }
+            }
+        }
+    }
+    if (tig == 0 && n > 0) {
+        const int t1 = (u0 + n - 1) / kGroups;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            if (t0 + j <= t1) {
+                S.gp[16 * (t0 + j) + g][cw] = acc[j][0];
+                if (!tl.half) S.gp[16 * (t0 + j) + g + 8][cw] = acc[j][1];
+            }
+        }
     }
 }
 
-MB_DEV float row896(const uint8_t *w_row, const float *s_row, const float *xr, int lane)
+// Row `row` of a job of T tiles: the partial sums of the warps whose units cover its
+// tile, in warp order (after a consumer barrier).  All 16 entries are loaded first.
+MB_DEV float row_sum(const Ctx &c, int T, int row)
 {
-    const int4 a = *reinterpret_cast<const int4 *>(w_row + lane * 16);
-    float acc = dot16r(a, xr) * s_row[lane >> 2];
-    if (lane < 24) {
-        const int4 b = *reinterpret_cast<const int4 *>(w_row + (lane + 32) * 16);
-        acc = fmaf(dot16r(b, xr + 16), s_row[(lane + 32) >> 2], acc);
+    const int U = kGroups * T, t = row >> 4;
+    float v[kConsumerWarps];
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) v[w] = c.S.gp[row][w];
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) {
+        const int u0 = U * w / kConsumerWarps, u1 = U * (w + 1) / kConsumerWarps;
+        if (u0 < u1 && u0 < kGroups * (t + 1) && u1 > kGroups * t) s += v[w];
     }
-    return mb::warp_sum(acc);
+    return s;
+}
+
+// Down projection, one 32-column step of this CTA's hidden units for all 896 rows
+// ([kDownTiles][32 lanes][16 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
+// partials (v * weight scale) are added to acc[tile][row g | row g + 8].
+MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, int ks, float (&acc)[4][2])
+{
+    const int t0 = kDownTiles * c.cw / kConsumerWarps, n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
+    const uint2 b = c.S.bfh[ks][c.lane];
+    const int g = c.lane >> 2;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        if (i < n) {
+            int d[4] = {0, 0, 0, 0};
+            mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)(t0 + i) * 32 + c.lane) * 16), b);
+            float v0, v1;
+            combine(d, v0, v1);
+            const int r0 = 16 * (t0 + i) + g;
+            acc[i][0] = fmaf(v0, sw[r0], acc[i][0]);
+            acc[i][1] = fmaf(v1, sw[r0 + 8], acc[i][1]);
+        }
+    }
 }
 
 MB_DEV size_t kv_index(int layer, int kvh, int pos)
@@ -379,23 +641,72 @@ struct Cursor {
     uint32_t k;  // chunks consumed
 };
 
+// Row tiles of a 896-wide chunk: QKV and O chunks are one 8-row tile, gate/up chunks
+// two full tiles (8 gate + 8 up rows each), head chunks up to two full tiles, or one
+// 8-row tile for a short last chunk.
+MB_DEV void chunk_tiles(uint32_t kind, uint32_t count, int &T, bool &half)
+{
+    if (kind == QKV || kind == OPROJ) {
+        T = 1;
+        half = true;
+    } else if (kind == GATEUP) {
+        T = (int)count / 8;
+        half = false;
+    } else {
+        half = count <= 8;
+        T = half ? 1 : (int)(count + 15) / 16;
+    }
+}
+
 // Wait for the next chunk; returns the slot (header first) or null on failure.
+// Every chunk's range is checked against the bounds its consumers assume.
 MB_DEV const uint8_t *take(Ctx &c, Cursor &cur, uint32_t kind)
 {
     const uint32_t slot = cur.k % kSlots, use = cur.k / kSlots;
     if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return nullptr;
     const uint8_t *w = c.S.ring[slot];
-    if (reinterpret_cast<const ChunkHdr *>(w)->kind != kind) {
+    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(w);
+    bool ok = h->kind == kind && h->count >= 1;
+    if (kind == QKV) ok = ok && h->count <= 4;
+    if (kind == OPROJ) ok = ok && h->count <= 8;
+    if (kind == GATEUP) ok = ok && (h->count == 8 || h->count == (uint32_t)kGateupPerChunk);
+    if (kind == HEAD) ok = ok && h->count <= (uint32_t)kHeadPerChunk;
+    if (kind == DOWN) ok = ok && h->count <= 2 && h->first < h->count;
+    if (!ok) {
         if (c.ct == 0) fail(c.sy, c.host_error, 4);
         return nullptr;
     }
     return w;
 }
 
+// The chunk `ahead` places past the cursor (ahead < kSlots: its copy was started when
+// the chunk before the cursor was given back), after it has landed.
+MB_DEV const uint8_t *peek(Ctx &c, const Cursor &cur, int ahead)
+{
+    const uint32_t k = cur.k + (uint32_t)ahead, slot = k % kSlots, use = k / kSlots;
+    if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return nullptr;
+    return c.S.ring[slot];
+}
+
+// Thread ct == 0, after a consumer barrier: start the bulk copy of chunk k (if any)
+// into slot k % kSlots, whose previous chunk every consumer has finished reading.
+MB_DEV void issue(Ctx &c, uint32_t k)
+{
+    if (k >= c.nchunks) return;
+    const Chunk ch = c.S.desc[k];
+    const uint32_t slot = k % kSlots;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(&c.S.full[slot], ch.bytes + (ch.gain_off ? kGainBytes : 0));
+    bulk_load(c.S.ring[slot], c.stream + ch.off, ch.bytes, &c.S.full[slot], c.policy);
+    if (ch.gain_off) bulk_load_plain(c.S.ring[slot] + kGainOff, c.blob + ch.gain_off, kGainBytes, &c.S.full[slot]);
+    c.S.issued = (int)k + 1;
+}
+
+// Release the chunk at the cursor and refill its slot with the chunk kSlots ahead.
 MB_DEV void give_back(Ctx &c, Cursor &cur)
 {
     cbar();
-    if (c.ct == 0) mbar_arrive(&c.S.empty[cur.k % kSlots]);
+    if (c.ct == 0) issue(c, cur.k + kSlots);
     cur.k++;
 }
 
@@ -410,15 +721,11 @@ MB_DEV int next_is(Ctx &c, const Cursor &cur, int remaining, uint32_t kind, uint
     return h->kind == kind && h->layer == layer ? 1 : 0;
 }
 
-// Error exit of the consumers: wait (bounded) until the producer has stopped and
-// every bulk copy it started into this CTA's ring has landed, so no copy is still
-// writing shared memory when the CTA exits.
+// Error exit: wait (bounded) until every bulk copy started into this CTA's ring has
+// landed, so no copy is still writing shared memory when the CTA exits.
 MB_DEV void drain(Ctx &c, const Cursor &cur)
 {
     if (c.ct == 0) {
-        const long long t0 = clock64();
-        while (!c.S.producer_done && clock64() - t0 < kTimeoutCycles) {
-        }
         const int issued = c.S.issued;
         for (int k = (int)cur.k; k < issued; k++) {
             const long long t1 = clock64();
@@ -484,15 +791,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const bool project = a.mode == FORWARD_PROJECT || a.mode == DECODE;
     const bool decode = a.mode == DECODE;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSlots; s++) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], 1);
-        }
+        for (int s = 0; s < kSlots; s++) mbar_init(&S.full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.token = ld_volatile((const unsigned *)&a.b.st->token);
         S.pos = ld_volatile((const unsigned *)&a.b.st->pos);
         S.issued = 0;
-        S.producer_done = 0;
         S.flag = 0;
         const bool bad = S.token < 0 || S.token >= VOCAB || S.pos < 0 || S.pos >= CONTEXT || epoch == 0 ||
                          epoch >= (1u << 24) || (a.mode == PREFILL && S.pos + 1 >= CONTEXT) ||
@@ -507,39 +810,43 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const uint32_t c0 = a.P->chunk_begin[cta], c1 = a.P->chunk_begin[cta + 1];
 
     const uint32_t c_end = project ? c1 : a.P->head_begin[cta];  // head chunks only when projecting
-    if (threadIdx.x < 32) {  // ---- producer warp: stream this CTA's weights
-        for (uint32_t j = threadIdx.x; j < c_end - c0 && j < (uint32_t)kMaxChunksPerCta; j += 32)
-            S.desc[j] = a.P->chunks[c0 + j];
-        __syncwarp();
-        if (threadIdx.x == 0) {
-            const uint64_t policy = mb::evict_first_policy();
-            uint32_t k = 0;
-            for (uint32_t i = 0; i < c_end - c0; i++) {
-                const Chunk ch = S.desc[i];
-                const uint32_t slot = k % kSlots, use = k / kSlots;
-                if (use > 0 && !mbar_wait(&S.empty[slot], (use - 1) & 1, a.sy, a.host_error)) break;
-                if (ld_volatile(&a.sy->error)) break;
-                mbar_expect_tx(&S.full[slot], ch.bytes + (ch.gain_off ? kGainBytes : 0));
-                bulk_load(S.ring[slot], a.P->stream + ch.off, ch.bytes, &S.full[slot], policy);
-                if (ch.gain_off)
-                    bulk_load_plain(S.ring[slot] + kGainOff, a.P->blob + ch.gain_off, kGainBytes, &S.full[slot]);
-                k++;
-                S.issued = (int)k;
-            }
-            __threadfence_block();
-            S.producer_done = 1;
-        }
-        return;
-    }
-
-    Ctx c{S, a.sy, a.host_error, (int)threadIdx.x - 32, ((int)threadIdx.x - 32) >> 5, (int)threadIdx.x & 31};
+    for (uint32_t j = threadIdx.x; j < c_end - c0 && j < (uint32_t)kMaxChunksPerCta; j += kThreads)
+        S.desc[j] = a.P->chunks[c0 + j];
+    __syncthreads();
+    Ctx c{S,
+          a.sy,
+          a.host_error,
+          (int)threadIdx.x,
+          (int)threadIdx.x >> 5,
+          (int)threadIdx.x & 31,
+          cta % kReplicas,
+          a.P->stream,
+          a.P->blob,
+          c_end - c0,
+          mb::evict_first_policy()};
+    // the first kSlots chunks; every later one is started when a slot is given back
+    if (c.ct == 0)
+        for (uint32_t k = 0; k < (uint32_t)kSlots; k++) issue(c, k);
     const int pos = S.pos;
     Cursor cur{0};
     int remaining = (int)(c_end - c0);  // chunks this CTA still has to take
     const Model *M = a.M;
     const Scratch &scr = a.scr;
-    float xr[32];
+    // the copies of the broadcast arrays this CTA reads
+    const unsigned long long *xin_r = scr.xin + c.rep * kStrideDim;
+    const unsigned long long *xmid_r = scr.xmid + c.rep * kStrideDim;
+    const unsigned long long *part_r = scr.part + c.rep * kStridePart;
+    const unsigned long long *kv_r = scr.kv + c.rep * kStrideKv;
+    const int nks = has_spare(cta) ? 2 : 1;  // down-projection steps of this CTA
+    const int xlo = (int)((long long)DIM * cta / kCTAs), xn = (int)((long long)DIM * (cta + 1) / kCTAs) - xlo;
+    // B-fragment columns 3..7 stay zero; columns 0..2 are rewritten by every quantize
+    for (int i = c.ct; i < kSteps * 32; i += kNT) S.bf[i >> 5][i & 31] = make_uint2(0u, 0u);
+    for (int i = c.ct; i < 2 * 32; i += kNT) {
+        S.bfh[i >> 5][i & 31] = make_uint2(0u, 0u);
+        S.hst[i >> 5][i & 31] = 0.f;  // columns of the spare step owned by other CTAs stay zero
+    }
     stamp(a, cta, c.ct, 0);
+    stamp_value(a, cta, c.ct, 303, clock64());
 
     // per-step constants: RoPE at pos, the attention split owned by this CTA
     if (c.ct < HEAD_DIM / 2) {
@@ -579,51 +886,52 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             asm volatile("cp.async.commit_group;" ::: "memory");
         }
         // ---- QKV + bias + RoPE + KV write
-        if (l > 0 && !gather<1>(c, scr.xin, DIM, make_tag(epoch, l - 1, PH_X), S.xs)) return drain(c, cur);
+        if (l > 0 && !gather<1>(c, xin_r, DIM, make_tag(epoch, l - 1, PH_X), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * 12 + 0);
         {
             const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
+            if (l == 12) stamp_value(a, cta, c.ct, 305, clock64());
+            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), 0);
+            if (l == 12) stamp_value(a, cta, c.ct, 306, clock64());
             const int npair = hd.count;
-            const uint8_t *rows = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(rows + (size_t)2 * npair * DIM);
-            const float *bias = sc + 2 * npair * (DIM / GROUP);
-            if (c.cw < npair) {
-                load_x896(S.ns, c.lane, xr);
-                const int pair = hd.first + c.cw;
-                const float d0 = row896(rows + (size_t)(2 * c.cw) * DIM, sc + (2 * c.cw) * 14, xr, c.lane);
-                const float d1 = row896(rows + (size_t)(2 * c.cw + 1) * DIM, sc + (2 * c.cw + 1) * 14, xr, c.lane);
-                if (c.lane == 0) {
-                    const uint32_t tag = make_tag(epoch, l, PH_QKV);
-                    int kind, t;
-                    if (pair < DIM / 2) { kind = 0; t = pair; }
-                    else if (pair < DIM / 2 + KV / 2) { kind = 1; t = pair - DIM / 2; }
-                    else { kind = 2; t = pair - DIM / 2 - KV / 2; }
-                    const int head = t / 32, i = t % 32, r0 = head * HEAD_DIM + i;
-                    const float v0 = d0 + bias[2 * c.cw], v1 = d1 + bias[2 * c.cw + 1];
-                    if (kind == 2) {
-                        float *v = a.b.vc + kv_index(l, head, pos);
-                        v[i] = v0;
-                        v[i + 32] = v1;
-                        dw_store(scr.kv + (head * 2 + 1) * HEAD_DIM + i, v0, tag);
-                        dw_store(scr.kv + (head * 2 + 1) * HEAD_DIM + i + 32, v1, tag);
+            const uint8_t *frag = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
+            const float *bias = sc + 8 * kGroups;
+            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
+            cbar();
+            if (l == 12) stamp_value(a, cta, c.ct, 307, clock64());
+            if (c.ct < npair) {
+                const int pair = hd.first + c.ct;
+                const uint32_t tag = make_tag(epoch, l, PH_QKV);
+                int kind, t;
+                if (pair < DIM / 2) { kind = 0; t = pair; }
+                else if (pair < DIM / 2 + KV / 2) { kind = 1; t = pair - DIM / 2; }
+                else { kind = 2; t = pair - DIM / 2 - KV / 2; }
+                const int head = t / 32, i = t % 32, r0 = head * HEAD_DIM + i;
+                const float v0 = row_sum(c, 1, 2 * c.ct) + bias[2 * c.ct];
+                const float v1 = row_sum(c, 1, 2 * c.ct + 1) + bias[2 * c.ct + 1];
+                if (kind == 2) {
+                    float *v = a.b.vc + kv_index(l, head, pos);
+                    v[i] = v0;
+                    v[i + 32] = v1;
+                    dw_store_rep(scr.kv + (head * 2 + 1) * HEAD_DIM + i, kStrideKv, v0, tag);
+                    dw_store_rep(scr.kv + (head * 2 + 1) * HEAD_DIM + i + 32, kStrideKv, v1, tag);
+                } else {
+                    const float cs = S.rc[i], sn = S.rs[i];
+                    // unfused products, as the reference CPU evaluates them (src/minimind.cpp:64-66)
+                    const float lo = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+                    const float hi = __fadd_rn(__fmul_rn(v1, cs), __fmul_rn(v0, sn));
+                    if (kind == 0) {
+                        dw_store(scr.q + r0, lo, tag);
+                        dw_store(scr.q + r0 + 32, hi, tag);
                     } else {
-                        const float cs = S.rc[i], sn = S.rs[i];
-                        // unfused products, as the reference CPU evaluates them (src/minimind.cpp:64-66)
-                        const float lo = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
-                        const float hi = __fadd_rn(__fmul_rn(v1, cs), __fmul_rn(v0, sn));
-                        if (kind == 0) {
-                            dw_store(scr.q + r0, lo, tag);
-                            dw_store(scr.q + r0 + 32, hi, tag);
-                        } else {
-                            float *k = a.b.kc + kv_index(l, head, pos);
-                            k[i] = lo;
-                            k[i + 32] = hi;
-                            dw_store(scr.kv + (head * 2) * HEAD_DIM + i, lo, tag);
-                            dw_store(scr.kv + (head * 2) * HEAD_DIM + i + 32, hi, tag);
-                        }
+                        float *k = a.b.kc + kv_index(l, head, pos);
+                        k[i] = lo;
+                        k[i + 32] = hi;
+                        dw_store_rep(scr.kv + (head * 2) * HEAD_DIM + i, kStrideKv, lo, tag);
+                        dw_store_rep(scr.kv + (head * 2) * HEAD_DIM + i + 32, kStrideKv, hi, tag);
                     }
                 }
             }
@@ -642,8 +950,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             int ok = 1;
             if (c.ct < HEAD_DIM) {
                 const unsigned long long *qa = scr.q + h * HEAD_DIM + c.ct;
-                const unsigned long long *ka = scr.kv + (kvh * 2) * HEAD_DIM + c.ct;
-                const unsigned long long *va = scr.kv + (kvh * 2 + 1) * HEAD_DIM + c.ct;
+                const unsigned long long *ka = kv_r + (kvh * 2) * HEAD_DIM + c.ct;
+                const unsigned long long *va = kv_r + (kvh * 2 + 1) * HEAD_DIM + c.ct;
                 unsigned long long w = dw_load(qa);
                 unsigned long long wk = has_cur ? dw_load(ka) : ready;
                 unsigned long long wv = has_cur ? dw_load(va) : ready;
@@ -652,12 +960,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     if ((uint32_t)(w >> 32) != tag) w = dw_load(qa);
                     if ((uint32_t)(wk >> 32) != tag) wk = dw_load(ka);
                     if ((uint32_t)(wv >> 32) != tag) wv = dw_load(va);
-                    if (ld_volatile(&c.sy->error)) {
-                        ok = 0;
-                        break;
-                    }
-                    if (clock64() - t0 > kTimeoutCycles) {
-                        fail(c.sy, c.host_error, 1);
+                    if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
                         ok = 0;
                         break;
                     }
@@ -670,12 +973,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             cp_async_wait_all();
             if (!cbar_and(ok)) return drain(c, cur);
-            // scores: warp per position, lanes over the 64 dims
-            for (int p = c.cw; p < np; p += kConsumerWarps) {
-                float z = S.u.att.q[c.lane] * S.u.att.k[p][c.lane];
-                z = fmaf(S.u.att.q[c.lane + 32], S.u.att.k[p][c.lane + 32], z);
-                z = mb::warp_sum(z);
-                if (c.lane == 0) S.u.att.e[p] = z * 0.125f;
+            // scores: warp cw takes positions 8*cw + (lane & 7), lane >> 3 picks the
+            // quarter of the 64 dims (float4 columns 4m + quarter); key rows are
+            // kKStride floats apart so the eight lanes of a phase hit distinct banks
+            {
+                const int p = 8 * c.cw + (c.lane & 7), qd = c.lane >> 3;
+                float z = 0.f;
+                if (p < np) {
+                    const float4 *k4 = reinterpret_cast<const float4 *>(S.u.att.k[p]);
+                    const float4 *q4 = reinterpret_cast<const float4 *>(S.u.att.q);
+#pragma unroll
+                    for (int m = 0; m < 4; m++) {
+                        const float4 kk = k4[4 * m + qd], qq = q4[4 * m + qd];
+                        z = fmaf(qq.x, kk.x, z);
+                        z = fmaf(qq.y, kk.y, z);
+                        z = fmaf(qq.z, kk.z, z);
+                        z = fmaf(qq.w, kk.w, z);
+                    }
+                }
+                z += __shfl_xor_sync(0xffffffffu, z, 8);
+                z += __shfl_xor_sync(0xffffffffu, z, 16);
+                if (qd == 0 && p < np) S.u.att.e[p] = z * 0.125f;
             }
             cbar();
             if (c.cw == 0) {
@@ -695,15 +1013,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 }
             }
             cbar();
+            // P.V: thread (d, g) sums positions g, g + 8, ...; groups added in order
+            {
+                const int d = c.ct % HEAD_DIM, g = c.ct / HEAD_DIM;
+                float acc = 0.f;
+                for (int p = g; p < np; p += kPvGroups) acc = fmaf(S.u.att.e[p], S.u.att.v[p][d], acc);
+                S.u.att.pv[g][d] = acc;
+            }
+            cbar();
             if (c.ct < HEAD_DIM) {
                 float acc = 0.f;
-                for (int p = 0; p < np; p++) acc = fmaf(S.u.att.e[p], S.u.att.v[p][c.ct], acc);
+#pragma unroll
+                for (int g = 0; g < kPvGroups; g++) acc += S.u.att.pv[g][c.ct];
                 const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
                 unsigned long long *out = scr.part + ((size_t)h * kMaxSplit + unit.split) * ATTN_PARTIAL;
-                dw_store(out + 2 + c.ct, acc, ptag);
+                dw_store_rep(out + 2 + c.ct, kStridePart, acc, ptag);
                 if (c.ct == 0) {
-                    dw_store(out, S.red[0][0], ptag);
-                    dw_store(out + 1, S.red[0][1], ptag);
+                    dw_store_rep(out, kStridePart, S.red[0][0], ptag);
+                    dw_store_rep(out + 1, kStridePart, S.red[0][1], ptag);
                 }
             }
             cbar();
@@ -711,36 +1038,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * 12 + 2);
 
         // ---- O projection + residual: combine every head's splits, then the rows
-        if (!gather_if<(kPartWords / 4 + kNT - 1) / kNT>(c, scr.part, kPartWords, make_tag(epoch, l, PH_ATTN), S.u.part,
+        if (!gather_if<(kPartWords / 4 + kNT - 1) / kNT>(c, part_r, kPartWords, make_tag(epoch, l, PH_ATTN), S.u.part,
                                                        UsedSplit{splits}))
             return drain(c, cur);
-        for (int idx = c.ct; idx < DIM; idx += kNT) {
-            const int h = idx / HEAD_DIM, d = idx % HEAD_DIM;
-            const float *p = S.u.part + (size_t)h * kMaxSplit * ATTN_PARTIAL;
-            float mx = -INFINITY;
-            for (int s = 0; s < splits; s++) mx = fmaxf(mx, p[s * ATTN_PARTIAL]);
-            float lsum = 0.f, acc = 0.f;
-            for (int s = 0; s < splits; s++) {
-                const float wgt = expf(p[s * ATTN_PARTIAL] - mx);
-                lsum = fmaf(wgt, p[s * ATTN_PARTIAL + 1], lsum);
-                acc = fmaf(wgt, p[s * ATTN_PARTIAL + 2 + d], acc);
-            }
-            S.ns[idx] = acc / lsum;
-        }
-        cbar();
+        combine_quantize(&S, c.ct, splits);
         stamp(a, cta, c.ct, 2 + l * 12 + 3);
         {
             const uint8_t *w = take(c, cur, OPROJ);
             if (!w) return drain(c, cur);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            const int nrow = hd.count;
-            const uint8_t *rows = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * DIM);
-            if (c.cw < nrow) {
-                load_x896(S.ns, c.lane, xr);
-                const int row = hd.first + c.cw;
-                const float d = row896(rows + (size_t)c.cw * DIM, sc + c.cw * 14, xr, c.lane);
-                if (c.lane == 0) dw_store(scr.xmid + row, S.xs[row] + d, make_tag(epoch, l, PH_O));
+            const int R = hd.count;
+            const uint8_t *frag = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
+            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
+            cbar();
+            if (c.ct < R) {
+                const int row = hd.first + c.ct;
+                dw_store_rep(scr.xmid + row, kStrideDim, S.xs[row] + row_sum(c, 1, c.ct), make_tag(epoch, l, PH_O));
             }
             give_back(c, cur);
             remaining--;
@@ -750,89 +1064,146 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         // ---- RMSNorm -> gate/up -> SwiGLU
         if (c.ct == 0) S.iters = 0;
         cbar();
-        if (!gather<1>(c, scr.xmid, DIM, make_tag(epoch, l, PH_O), S.xs, &S.iters)) return drain(c, cur);
+        if (!gather<1>(c, xmid_r, DIM, make_tag(epoch, l, PH_O), S.xs, &S.iters)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * 12 + 5);
         stamp_value(a, cta, c.ct, 2 + l * 12 + 11, (unsigned long long)S.iters);
         {
-            bool first = true;
-            for (;;) {
-                const int more = next_is(c, cur, remaining, GATEUP, l);
-                if (more < 0) return drain(c, cur);
-                if (!more) break;
-                const uint8_t *w = take(c, cur, GATEUP);
+            // this layer's gate/up chunks (2 or 3, all resident in the ring together)
+            const uint8_t *gw[3] = {nullptr, nullptr, nullptr};
+            int ngu = 0, T = 0;
+            while (ngu < 3 && ngu < remaining) {
+                const uint8_t *w = peek(c, cur, ngu);
                 if (!w) return drain(c, cur);
-                if (first) {
-                    stamp(a, cta, c.ct, 2 + l * 12 + 9);
-                    rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
-                    load_x896(S.ns, c.lane, xr);
-                    first = false;
-                    stamp(a, cta, c.ct, 2 + l * 12 + 10);
+                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(w);
+                if (h->kind != GATEUP || h->layer != (uint32_t)l) break;
+                if ((h->count != 8 && h->count != 16) || (ngu > 0 && T % 2)) {
+                    if (c.ct == 0) fail(c.sy, c.host_error, 4);
+                    return drain(c, cur);
                 }
+                gw[ngu++] = w;
+                T += h->count / 8;
+            }
+            if (T > 5) {
+                if (c.ct == 0) fail(c.sy, c.host_error, 4);
+                return drain(c, cur);
+            }
+            if (ngu == 0) {
+                if (c.ct == 0) fail(c.sy, c.host_error, 4);
+                return drain(c, cur);
+            }
+            stamp(a, cta, c.ct, 2 + l * 12 + 9);
+            if (l == 12) stamp_value(a, cta, c.ct, 308, clock64());
+            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(gw[0] + kGainOff), 0);
+            if (l == 12) stamp_value(a, cta, c.ct, 309, clock64());
+            stamp(a, cta, c.ct, 2 + l * 12 + 10);
+            Tiles tl{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}, T, 0};
+            for (int i = 0; i < 3; i++) {
+                const uint8_t *w = gw[i] ? gw[i] : gw[0];
+                const int ti = reinterpret_cast<const ChunkHdr *>(w)->count / 8;
+                tl.frag[i] = w + sizeof(ChunkHdr);
+                tl.sc[i] = reinterpret_cast<const float *>(tl.frag[i] + (size_t)ti * kTileBytes);
+            }
+            gemv_mma(&S, c.cw, c.lane, tl);
+            cbar();
+            if (l == 12) stamp_value(a, cta, c.ct, 310, clock64());
+            // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and
+            // its up row 8 below; it lands at its column of down step 0 (own block) or 1
+            if (c.ct < 8 * T) {
+                const int t = c.ct >> 3, j = c.ct & 7;
+                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(gw[t >> 1]);
+                const int unit = (int)h->first + 8 * (t & 1) + j;
+                const float g = row_sum(c, T, 16 * t + j), u = row_sum(c, T, 16 * t + 8 + j);
+                S.hst[(unit >> 5) == cta ? 0 : 1][unit & 31] = (g / (1.0f + expf(-g))) * u;
+            }
+            cbar();
+            if (c.ct == 0)
+                for (int i = 0; i < ngu; i++) issue(c, cur.k + i + kSlots);
+            cur.k += ngu;
+            remaining -= ngu;
+        }
+        stamp(a, cta, c.ct, 2 + l * 12 + 7);
+        if (l == 12) stamp_value(a, cta, c.ct, 311, clock64());
+        quantize_slice(c, nks);
+        if (l == 12) stamp_value(a, cta, c.ct, 312, clock64());
+        {
+            float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+            for (;;) {
+                const uint8_t *w = take(c, cur, DOWN);
+                if (!w) return drain(c, cur);
                 const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-                const int npair = hd.count;
-                const uint8_t *rows = w + sizeof(ChunkHdr);
-                const float *sc = reinterpret_cast<const float *>(rows + (size_t)2 * npair * DIM);
-                const uint32_t tag = make_tag(epoch, l, PH_H);
-                for (int p = c.cw; p < npair; p += kConsumerWarps) {
-                    const float g = row896(rows + (size_t)(2 * p) * DIM, sc + (2 * p) * 14, xr, c.lane);
-                    const float u = row896(rows + (size_t)(2 * p + 1) * DIM, sc + (2 * p + 1) * 14, xr, c.lane);
-                    if (c.lane == 0) dw_store(scr.h + hd.first + p, (g / (1.0f + expf(-g))) * u, tag);
+                const uint8_t *frag = w + sizeof(ChunkHdr);
+                const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
+                down_step(c, frag, sw, (int)hd.first, pacc);
+                const bool last = hd.first + 1 == hd.count;
+                if (last) {
+                    // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
+                    const int t0 = kDownTiles * c.cw / kConsumerWarps;
+                    const int n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
+                    const int g = c.lane >> 2;
+                    const float f = S.sh;
+                    const uint32_t tag = make_tag(epoch, l, PH_D);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        if (i < n && (c.lane & 3) == 0) {
+                            const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
+                            dw_store(scr.pd + (size_t)r0 * kCTAs + cta, pacc[i][0] * f, tag);
+                            dw_store(scr.pd + (size_t)r1 * kCTAs + cta, pacc[i][1] * f, tag);
+                        }
+                    }
                 }
                 give_back(c, cur);
                 remaining--;
+                if (last) break;
             }
         }
         stamp(a, cta, c.ct, 2 + l * 12 + 6);
-
-        // ---- down + residual: the CTA's threads own column chunks, rows reduced
-        if (!gather<(HIDDEN / 4 + kNT - 1) / kNT>(c, scr.h, HIDDEN, make_tag(epoch, l, PH_H), S.u.hs))
-            return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * 12 + 7);
+        // reduce: warp r sums row xlo + r over the 148 CTAs (lane: CTAs 4 lane .. +3 and
+        // 128 + 4 lane .. +3), then the butterfly; plus the residual x_mid
         {
-            const uint8_t *w = take(c, cur, DOWN);
-            if (!w) return drain(c, cur);
-            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            const int nrow = hd.count;
-            constexpr int CH = HIDDEN / 16;  // 304 chunks of 16
-            const uint8_t *rows = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * HIDDEN);
-            const int ci = c.ct;
-            if (ci < CH) {
-                const float4 *h4 = reinterpret_cast<const float4 *>(S.u.hs + ci * 16);
+            int ok = 1;
+            if (c.cw < xn) {
+                const int row = xlo + c.cw;
+                const unsigned long long *src = scr.pd + (size_t)row * kCTAs;
+                const uint32_t tag = make_tag(epoch, l, PH_D);
+                const bool two = 128 + 4 * c.lane < kCTAs;
+                unsigned need = two ? 0xFFu : 0xFu;
+                float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                long long t0 = 0;
+                for (;;) {
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float4 v = h4[i];
-                    xr[4 * i] = v.x;
-                    xr[4 * i + 1] = v.y;
-                    xr[4 * i + 2] = v.z;
-                    xr[4 * i + 3] = v.w;
+                    for (int k = 0; k < 2; k++) {
+                        if (!(need >> (4 * k) & 0xFu)) continue;
+                        unsigned long long w4[4];
+                        dw_load4(src + 128 * k + 4 * c.lane, w4);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            if ((need >> (4 * k + j) & 1u) && (uint32_t)(w4[j] >> 32) == tag) {
+                                v[4 * k + j] = __uint_as_float((uint32_t)w4[j]);
+                                need &= ~(1u << (4 * k + j));
+                            }
+                        }
+                    }
+                    if (!need) break;
+                    if (t0 == 0) {
+                        t0 = clock64();
+                    } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(32);
                 }
+                float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+                sum = mb::warp_sum(sum);
+                if (c.lane == 0) dw_store_rep(scr.xin + row, kStrideDim, S.xs[row] + sum, make_tag(epoch, l, PH_X));
             }
-            for (int r = 0; r < nrow; r++) {
-                float p = 0.f;
-                if (ci < CH)
-                    p = dot16r(*reinterpret_cast<const int4 *>(rows + (size_t)r * HIDDEN + ci * 16), xr) *
-                        sc[r * (HIDDEN / GROUP) + (ci >> 2)];
-                p = mb::warp_sum(p);
-                if (c.lane == 0) S.red[c.cw][r] = p;
-            }
-            cbar();
-            if (c.ct < nrow) {
-                float sum = 0.f;
-#pragma unroll
-                for (int w16 = 0; w16 < kConsumerWarps; w16++) sum += S.red[w16][c.ct];
-                const int row = hd.first + c.ct;
-                dw_store(scr.xin + row, S.xs[row] + sum, make_tag(epoch, l, PH_X));
-            }
-            give_back(c, cur);
-            remaining--;
+            if (!cbar_and(ok)) return drain(c, cur);
         }
         stamp(a, cta, c.ct, 2 + l * 12 + 8);
     }
 
     if (project) {
         // ---- final norm + tied head, logits kept in shared memory for selection
-        if (!gather<1>(c, scr.xin, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
+        if (!gather<1>(c, xin_r, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, 300);
         const int lo = a.P->head_lo[cta], n = a.P->head_lo[cta + 1] - lo;
         bool first = true;
@@ -843,22 +1214,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             const uint8_t *w = take(c, cur, HEAD);
             if (!w) return drain(c, cur);
             if (first) {
-                rmsnorm(c, S.xs, reinterpret_cast<const float *>(w + kGainOff), S.ns);
+                norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), cta == 0);
                 if (cta == 0)
                     for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
-                load_x896(S.ns, c.lane, xr);
                 first = false;
             }
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            const int nrow = hd.count;
-            const uint8_t *rows = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(rows + (size_t)nrow * DIM);
-            for (int r = c.cw; r < nrow; r += kConsumerWarps) {
-                const float d = row896(rows + (size_t)r * DIM, sc + r * 14, xr, c.lane);
-                if (c.lane == 0) {
-                    a.b.logits[hd.first + r] = d;
-                    S.u.hl[hd.first + r - lo] = d;
-                }
+            const int R = hd.count;
+            int T;
+            bool half;
+            chunk_tiles(HEAD, hd.count, T, half);
+            const uint8_t *frag = w + sizeof(ChunkHdr);
+            const float *sc = reinterpret_cast<const float *>(frag + (half ? kHalfBytes : (size_t)T * kTileBytes));
+            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, T, half ? 1 : 0});
+            cbar();
+            if (c.ct < R) {
+                const float d = row_sum(c, T, c.ct);
+                a.b.logits[hd.first + c.ct] = d;
+                S.u.hl[hd.first + c.ct - lo] = d;
             }
             give_back(c, cur);
             remaining--;
@@ -908,6 +1281,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 
     // ---- end of step: the last CTA finishes the token
     stamp(a, cta, c.ct, 301);
+    stamp_value(a, cta, c.ct, 304, clock64());
     cbar();
     if (c.ct == 0) {
         __threadfence();
@@ -975,16 +1349,19 @@ inline void split(int n, int parts, int i, int &lo, int &hi)
 
 size_t smem_bytes() { return sizeof(Smem); }
 
-size_t scratch_words() { return (size_t)DIM + 2 * KV + kPartWords + DIM + DIM + HIDDEN; }
+size_t scratch_words()
+{
+    return (size_t)DIM + (size_t)kReplicas * (kStrideKv + kStridePart + 2 * kStrideDim) + (size_t)DIM * kCTAs;
+}
 
 void carve_scratch(unsigned long long *base, Scratch *scr)
 {
     scr->q = base;
     scr->kv = scr->q + DIM;
-    scr->part = scr->kv + 2 * KV;
-    scr->xmid = scr->part + kPartWords;
-    scr->xin = scr->xmid + DIM;
-    scr->h = scr->xin + DIM;
+    scr->part = scr->kv + kReplicas * kStrideKv;
+    scr->xmid = scr->part + kReplicas * kStridePart;
+    scr->xin = scr->xmid + kReplicas * kStrideDim;
+    scr->pd = scr->xin + kReplicas * kStrideDim;
 }
 
 int init_device()
@@ -1003,82 +1380,151 @@ int init_device()
     return 0;
 }
 
+// One 32-column step of a 16-row tile in the A-fragment order of
+// mma.m16n8k32.row (lane l = 4 g + tig: rows g and g + 8, columns 4 tig + {0..3} and
+// 16 + 4 tig + {0..3}); a null row is zero.  Half tiles keep registers a0 and a2 only.
+static void put_step(std::vector<uint8_t> &out, const int8_t *const rows[16], int k0, bool half)
+{
+    for (int l = 0; l < 32; l++) {
+        const int g = l >> 2, tig = l & 3;
+        const int8_t *r0 = rows[g], *r1 = rows[g + 8];
+        uint8_t b[16];
+        for (int j = 0; j < 4; j++) {
+            b[j] = r0 ? (uint8_t)r0[k0 + 4 * tig + j] : 0;
+            b[4 + j] = r1 ? (uint8_t)r1[k0 + 4 * tig + j] : 0;
+            b[8 + j] = r0 ? (uint8_t)r0[k0 + 16 + 4 * tig + j] : 0;
+            b[12 + j] = r1 ? (uint8_t)r1[k0 + 16 + 4 * tig + j] : 0;
+        }
+        if (half) {
+            out.insert(out.end(), b, b + 4);
+            out.insert(out.end(), b + 8, b + 12);
+        } else {
+            out.insert(out.end(), b, b + 16);
+        }
+    }
+}
+
 int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned char *dfile, Plan *hplan,
                Chunk **dchunks, uint8_t **dstream, size_t *stream_bytes, cudaStream_t s)
 {
     std::vector<Chunk> chunks;
     std::vector<uint8_t> stream;
-    stream.reserve((size_t)560 << 20);
+    stream.reserve((size_t)580 << 20);
     const FileTensor *t = hdr->t;
     auto align16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
-    // one chunk: header, int8 rows, fp32 scales, optional fp32 extras (biases)
-    auto emit = [&](uint32_t kind, uint32_t layer, uint32_t first, uint32_t count,
-                    const std::vector<std::pair<const FileTensor *, int>> &rows, const std::vector<float> &extra,
-                    uint32_t gain_off) {
+    using Row = std::pair<const FileTensor *, int>;  // (matrix, row); null matrix = zero row
+    auto row_ptr = [&](const Row &r) -> const int8_t * {
+        return r.first ? reinterpret_cast<const int8_t *>(hfile + r.first->data) + (size_t)r.second * r.first->cols
+                       : nullptr;
+    };
+    auto scale = [&](const Row &r, int group) -> float {
+        if (!r.first) return 0.f;
+        const float *sc = reinterpret_cast<const float *>(hfile + r.first->scales);
+        return sc[(size_t)r.second * (r.first->cols / GROUP) + group];
+    };
+    auto begin = [&](uint32_t kind, uint32_t layer, uint32_t first, uint32_t count) {
         Chunk ch{};
         ch.off = stream.size();
-        ch.gain_off = gain_off;
         const ChunkHdr hd{kind, layer, first, count};
         const uint8_t *hb = reinterpret_cast<const uint8_t *>(&hd);
         stream.insert(stream.end(), hb, hb + sizeof hd);
-        for (auto &r : rows) {
-            const uint8_t *src = hfile + r.first->data + (size_t)r.second * r.first->cols;
-            stream.insert(stream.end(), src, src + r.first->cols);
-        }
-        for (auto &r : rows) {
-            const size_t g = r.first->cols / GROUP;
-            const uint8_t *src = hfile + r.first->scales + (size_t)r.second * g * 4;
-            stream.insert(stream.end(), src, src + g * 4);
-        }
-        const uint8_t *eb = reinterpret_cast<const uint8_t *>(extra.data());
-        stream.insert(stream.end(), eb, eb + extra.size() * 4);
+        return ch;
+    };
+    auto put_floats = [&](const std::vector<float> &v) {
+        const uint8_t *b = reinterpret_cast<const uint8_t *>(v.data());
+        stream.insert(stream.end(), b, b + v.size() * 4);
+    };
+    auto finish = [&](Chunk ch, uint32_t gain_off) {
         stream.resize(align16(stream.size()), 0);
         ch.bytes = (uint32_t)(stream.size() - ch.off);
+        ch.gain_off = gain_off;
         const uint32_t limit = gain_off ? (uint32_t)kGainOff : (uint32_t)kSlotBytes;
         if (ch.bytes > limit || (gain_off && gain_off % 16)) return false;
         chunks.push_back(ch);
         return true;
     };
+    // A chunk of 896-wide rows: tiles of 16 rows (tile_rows.size() a multiple of 16, or 8
+    // for a half tile), then the tile rows' 14 scales each, then extras.
+    auto emit896 = [&](uint32_t kind, uint32_t layer, uint32_t first, uint32_t count,
+                       const std::vector<Row> &tile_rows, const std::vector<float> &extra, uint32_t gain_off) {
+        const bool half = tile_rows.size() == 8;
+        if (!half && tile_rows.size() % 16) return false;
+        Chunk ch = begin(kind, layer, first, count);
+        const int T = half ? 1 : (int)tile_rows.size() / 16;
+        for (int ti = 0; ti < T; ti++) {
+            const int8_t *rows[16];
+            for (int j = 0; j < 16; j++) rows[j] = half && j >= 8 ? nullptr : row_ptr(tile_rows[16 * ti + j]);
+            for (int ks = 0; ks < kSteps; ks++) put_step(stream, rows, 32 * ks, half);
+        }
+        std::vector<float> sc;
+        for (const Row &r : tile_rows)
+            for (int g = 0; g < kGroups; g++) sc.push_back(scale(r, g));
+        put_floats(sc);
+        put_floats(extra);
+        return finish(ch, gain_off);
+    };
+    const Row none{nullptr, 0};
     for (int c = 0; c < kCTAs; c++) {
         hplan->chunk_begin[c] = (uint32_t)chunks.size();
         for (int l = 0; l < LAYERS; l++) {
             const FileTensor *lt = t + 1 + l * STRIDE;
             int lo, hi;
-            std::vector<std::pair<const FileTensor *, int>> rows;
-            std::vector<float> bias;
+            // QKV: pair p -> tile rows 2j (dimension i) and 2j + 1 (dimension i + 32)
+            std::vector<Row> rows(8, none);
+            std::vector<float> bias(8, 0.f);
             split(kQkvPairs, kCTAs, c, lo, hi);
+            if (hi - lo > 4) return 1;
             for (int p = lo; p < hi; p++) {
                 const FileTensor *m, *b;
                 int tt;
                 if (p < DIM / 2) { m = &lt[WQ]; b = &lt[BQ]; tt = p; }
                 else if (p < DIM / 2 + KV / 2) { m = &lt[WK]; b = &lt[BK]; tt = p - DIM / 2; }
                 else { m = &lt[WV]; b = &lt[BV]; tt = p - DIM / 2 - KV / 2; }
-                const int r0 = (tt / 32) * HEAD_DIM + tt % 32;
-                rows.push_back({m, r0});
-                rows.push_back({m, r0 + 32});
+                const int r0 = (tt / 32) * HEAD_DIM + tt % 32, j = p - lo;
+                rows[2 * j] = {m, r0};
+                rows[2 * j + 1] = {m, r0 + 32};
                 const float *bv = reinterpret_cast<const float *>(hfile + b->data);
-                bias.push_back(bv[r0]);
-                bias.push_back(bv[r0 + 32]);
+                bias[2 * j] = bv[r0];
+                bias[2 * j + 1] = bv[r0 + 32];
             }
-            if (!emit(QKV, l, lo, hi - lo, rows, bias, lt[ATTN_NORM].data)) return 1;
-            rows.clear();
+            if (!emit896(QKV, l, lo, hi - lo, rows, bias, lt[ATTN_NORM].data)) return 1;
+            // O: this CTA's residual rows
+            rows.assign(8, none);
             split(DIM, kCTAs, c, lo, hi);
-            for (int r = lo; r < hi; r++) rows.push_back({&lt[WO], r});
-            if (!emit(OPROJ, l, lo, hi - lo, rows, {}, 0)) return 1;
-            split(HIDDEN, kCTAs, c, lo, hi);
-            for (int p0 = lo; p0 < hi; p0 += kGateupPerChunk) {
-                const int p1 = p0 + kGateupPerChunk < hi ? p0 + kGateupPerChunk : hi;
+            if (hi - lo > 8) return 1;
+            for (int r = lo; r < hi; r++) rows[r - lo] = {&lt[WO], r};
+            if (!emit896(OPROJ, l, lo, hi - lo, rows, {}, 0)) return 1;
+            // gate/up: tiles of 8 gate rows then the 8 up rows of the same hidden units;
+            // the CTA's block in two chunks, then its spare piece (one tile)
+            std::vector<std::pair<int, int>> pieces = {{32 * c, 16}, {32 * c + 16, 16}};
+            if (has_spare(c)) pieces.push_back({spare_lo(c), 8});
+            for (size_t i = 0; i < pieces.size(); i++) {
+                const int h0 = pieces[i].first, n = pieces[i].second;
                 rows.clear();
-                for (int p = p0; p < p1; p++) {
-                    rows.push_back({&lt[WGATE], p});
-                    rows.push_back({&lt[WUP], p});
+                for (int ti = 0; ti < n / 8; ti++) {
+                    for (int j = 0; j < 8; j++) rows.push_back({&lt[WGATE], h0 + 8 * ti + j});
+                    for (int j = 0; j < 8; j++) rows.push_back({&lt[WUP], h0 + 8 * ti + j});
                 }
-                if (!emit(GATEUP, l, p0, p1 - p0, rows, {}, p0 == lo ? lt[FFN_NORM].data : 0)) return 1;
+                if (!emit896(GATEUP, l, h0, n, rows, {}, i == 0 ? lt[FFN_NORM].data : 0)) return 1;
             }
-            rows.clear();
-            split(DIM, kCTAs, c, lo, hi);
-            for (int r = lo; r < hi; r++) rows.push_back({&lt[WDOWN], r});
-            if (!emit(DOWN, l, lo, hi - lo, rows, {}, 0)) return 1;
+            // down: step 0 = columns of the CTA's block, step 1 = the spare block holding
+            // its piece; each 32-column step lies in one scale group
+            const FileTensor *wd = &lt[WDOWN];
+            const int8_t *dw = reinterpret_cast<const int8_t *>(hfile + wd->data);
+            const int nks = has_spare(c) ? 2 : 1;
+            for (int ks = 0; ks < nks; ks++) {
+                const int k0 = ks == 0 ? 32 * c : spare_lo(c) / 32 * 32;
+                std::vector<float> dsc(DIM);
+                for (int r = 0; r < DIM; r++) dsc[r] = scale({wd, r}, k0 / GROUP);
+                Chunk ch = begin(DOWN, l, ks, nks);
+                for (int ti = 0; ti < kDownTiles; ti++) {
+                    const int8_t *rr[16];
+                    for (int j = 0; j < 16; j++) rr[j] = dw + (size_t)(16 * ti + j) * HIDDEN;
+                    put_step(stream, rr, k0, false);
+                }
+                put_floats(dsc);
+                if (!finish(ch, 0)) return 1;
+            }
         }
         int lo, hi;
         split(VOCAB, kCTAs, c, lo, hi);
@@ -1087,9 +1533,10 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
         if (hi - lo > kHeadSlice) return 1;
         for (int r0 = lo; r0 < hi; r0 += kHeadPerChunk) {
             const int r1 = r0 + kHeadPerChunk < hi ? r0 + kHeadPerChunk : hi;
-            std::vector<std::pair<const FileTensor *, int>> rows;
-            for (int r = r0; r < r1; r++) rows.push_back({&t[0], r});
-            if (!emit(HEAD, LAYERS, r0, r1 - r0, rows, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
+            const int n = r1 - r0, padded = n <= 8 ? 8 : (n + 15) / 16 * 16;
+            std::vector<Row> rows(padded, none);
+            for (int r = r0; r < r1; r++) rows[r - r0] = {&t[0], r};
+            if (!emit896(HEAD, LAYERS, r0, n, rows, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
         }
     }
     hplan->chunk_begin[kCTAs] = (uint32_t)chunks.size();

@@ -11,7 +11,7 @@ namespace q8p {
 
 constexpr int kCTAs = 148;                // one CTA per SM
 constexpr int kConsumerWarps = 16;
-constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 streams weights
+constexpr int kThreads = 32 * kConsumerWarps;  // every thread consumes; thread 0 also issues the weight copies
 constexpr int kSlots = 4;                 // shared-memory ring slots
 constexpr int kSlotBytes = 36864;
 constexpr int kGainBytes = q8::DIM * 4;   // RMSNorm gain delivered with some chunks
@@ -44,7 +44,7 @@ struct Plan {
     uint32_t head_lo[kCTAs + 1];           // contiguous vocabulary rows per CTA
 };
 
-constexpr int kMaxChunksPerCta = 160;
+constexpr int kMaxChunksPerCta = 232;
 
 struct Sync {
     unsigned epoch;  // 1 .. 2^24-1, tags the step's data words
@@ -54,13 +54,19 @@ struct Sync {
 
 // Data words exchanged between CTAs: low 32 bits a float, high 32 bits the tag
 // (epoch << 8 | layer << 3 | phase).  A reader polls a word until its tag matches.
+// Words that many CTAs read are written to kReplicas copies (replica r at
+// base + r * stride) and CTA c reads copy c % kReplicas, so the polling load of one
+// exchange is spread over four times as many L2 lines.
+constexpr int kReplicas = 4;
+constexpr int replica_stride(int words) { return (words + 63) / 64 * 64 + 32; }
+
 struct Scratch {
     unsigned long long *q;        // [DIM] rotated queries
-    unsigned long long *kv;       // [KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
-    unsigned long long *part;     // [HEADS][kMaxSplit][ATTN_PARTIAL] attention partials
-    unsigned long long *xmid;     // [DIM] residual after attention
-    unsigned long long *xin;      // [DIM] residual after the FFN (input of the next layer)
-    unsigned long long *h;        // [HIDDEN] SwiGLU output
+    unsigned long long *kv;       // [kReplicas][KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
+    unsigned long long *part;     // [kReplicas][HEADS][kMaxSplit][ATTN_PARTIAL] attention partials
+    unsigned long long *xmid;     // [kReplicas][DIM] residual after attention
+    unsigned long long *xin;      // [kReplicas][DIM] residual after the FFN (input of the next layer)
+    unsigned long long *pd;       // [DIM][kCTAs] down-projection partial sums: row r, CTA c
     unsigned long long *cand;     // [kCTAs][64] per-CTA candidate keys (plain)
 };
 
