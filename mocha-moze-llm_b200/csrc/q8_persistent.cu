@@ -108,6 +108,8 @@ struct Smem {
     int iters;  // poll iterations of the last traced gather
     int token, pos;
     int issued;                  // chunks whose bulk copy has been started
+    int slot_done[kSlots];       // head phase: tiles of the slot's chunk finished
+    int slot_fill[kSlots];       // the chunk last issued into each slot
 };
 static_assert(sizeof(Smem) <= 232448, "shared memory per CTA");
 
@@ -151,11 +153,6 @@ MB_DEV void mbar_expect_tx(unsigned long long *bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
-}
-
-MB_DEV void mbar_arrive(unsigned long long *bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 MB_DEV bool mbar_test(unsigned long long *bar, uint32_t parity)
@@ -550,6 +547,10 @@ MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
             }
         }
     }
+    if (tig == 0 && n == 0) {  // fewer units than warps (T = 1): an empty contribution
+        S.gp[g][cw] = 0.f;
+        S.gp[g + 8][cw] = 0.f;
+    }
     if (tig == 0 && n > 0) {
         const int t1 = (u0 + n - 1) / kGroups;
 #pragma unroll
@@ -563,19 +564,17 @@ MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
 }
 
 // Row `row` of a job of T tiles: the partial sums of the warps whose units cover its
-// tile, in warp order (after a consumer barrier).  All 16 entries are loaded first.
+// tile -- warps wa..wb, the warps holding the tile's first and last unit -- in warp
+// order (after a consumer barrier).
 MB_DEV float row_sum(const Ctx &c, int T, int row)
 {
     const int U = kGroups * T, t = row >> 4;
-    float v[kConsumerWarps];
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) v[w] = c.S.gp[row][w];
+    const int wa = (kConsumerWarps * (kGroups * t + 1) - 1) / U;
+    const int wb = (kConsumerWarps * (kGroups * t + kGroups) - 1) / U;
+    const float *v = c.S.gp[row];
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) {
-        const int u0 = U * w / kConsumerWarps, u1 = U * (w + 1) / kConsumerWarps;
-        if (u0 < u1 && u0 < kGroups * (t + 1) && u1 > kGroups * t) s += v[w];
-    }
+    for (int w = 0; w < kConsumerWarps; w++) s += (w >= wa && w <= wb) ? v[w] : 0.f;
     return s;
 }
 
@@ -690,7 +689,7 @@ MB_DEV const uint8_t *peek(Ctx &c, const Cursor &cur, int ahead)
 
 // Thread ct == 0, after a consumer barrier: start the bulk copy of chunk k (if any)
 // into slot k % kSlots, whose previous chunk every consumer has finished reading.
-MB_DEV void issue(Ctx &c, uint32_t k)
+MB_DEV void issue(Ctx &c, uint32_t k, bool shared_issuers = false)
 {
     if (k >= c.nchunks) return;
     const Chunk ch = c.S.desc[k];
@@ -699,7 +698,12 @@ MB_DEV void issue(Ctx &c, uint32_t k)
     mbar_expect_tx(&c.S.full[slot], ch.bytes + (ch.gain_off ? kGainBytes : 0));
     bulk_load(c.S.ring[slot], c.stream + ch.off, ch.bytes, &c.S.full[slot], c.policy);
     if (ch.gain_off) bulk_load_plain(c.S.ring[slot] + kGainOff, c.blob + ch.gain_off, kGainBytes, &c.S.full[slot]);
-    c.S.issued = (int)k + 1;
+    if (shared_issuers) {
+        atomicMax(&c.S.issued, (int)k + 1);
+        *(volatile int *)&c.S.slot_fill[slot] = (int)k;
+    } else {
+        c.S.issued = (int)k + 1;
+    }
 }
 
 // Release the chunk at the cursor and refill its slot with the chunk kSlots ahead.
@@ -791,7 +795,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const bool project = a.mode == FORWARD_PROJECT || a.mode == DECODE;
     const bool decode = a.mode == DECODE;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSlots; s++) mbar_init(&S.full[s], 1);
+        for (int s = 0; s < kSlots; s++) {
+            mbar_init(&S.full[s], 1);
+            S.slot_done[s] = 0;
+            S.slot_fill[s] = -1;
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.token = ld_volatile((const unsigned *)&a.b.st->token);
         S.pos = ld_volatile((const unsigned *)&a.b.st->pos);
@@ -846,7 +854,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         S.hst[i >> 5][i & 31] = 0.f;  // columns of the spare step owned by other CTAs stay zero
     }
     stamp(a, cta, c.ct, 0);
-    stamp_value(a, cta, c.ct, 303, clock64());
 
     // per-step constants: RoPE at pos, the attention split owned by this CTA
     if (c.ct < HEAD_DIM / 2) {
@@ -892,16 +899,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            if (l == 12) stamp_value(a, cta, c.ct, 305, clock64());
             norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), 0);
-            if (l == 12) stamp_value(a, cta, c.ct, 306, clock64());
             const int npair = hd.count;
             const uint8_t *frag = w + sizeof(ChunkHdr);
             const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
             const float *bias = sc + 8 * kGroups;
             gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
             cbar();
-            if (l == 12) stamp_value(a, cta, c.ct, 307, clock64());
             if (c.ct < npair) {
                 const int pair = hd.first + c.ct;
                 const uint32_t tag = make_tag(epoch, l, PH_QKV);
@@ -1062,55 +1066,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * 12 + 4);
 
         // ---- RMSNorm -> gate/up -> SwiGLU
-        if (c.ct == 0) S.iters = 0;
-        cbar();
-        if (!gather<1>(c, xmid_r, DIM, make_tag(epoch, l, PH_O), S.xs, &S.iters)) return drain(c, cur);
+        if (!gather<1>(c, xmid_r, DIM, make_tag(epoch, l, PH_O), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * 12 + 5);
-        stamp_value(a, cta, c.ct, 2 + l * 12 + 11, (unsigned long long)S.iters);
         {
-            // this layer's gate/up chunks (2 or 3, all resident in the ring together)
-            const uint8_t *gw[3] = {nullptr, nullptr, nullptr};
+            // this layer's gate/up chunks (2 or 3, all resident in the ring together):
+            // slots cur.k .. cur.k + ngu - 1
             int ngu = 0, T = 0;
             while (ngu < 3 && ngu < remaining) {
-                const uint8_t *w = peek(c, cur, ngu);
-                if (!w) return drain(c, cur);
-                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(w);
+                if (!peek(c, cur, ngu)) return drain(c, cur);
+                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + ngu) % kSlots]);
                 if (h->kind != GATEUP || h->layer != (uint32_t)l) break;
                 if ((h->count != 8 && h->count != 16) || (ngu > 0 && T % 2)) {
                     if (c.ct == 0) fail(c.sy, c.host_error, 4);
                     return drain(c, cur);
                 }
-                gw[ngu++] = w;
+                ngu++;
                 T += h->count / 8;
             }
-            if (T > 5) {
+            if (ngu == 0 || T > 5) {
                 if (c.ct == 0) fail(c.sy, c.host_error, 4);
                 return drain(c, cur);
             }
-            if (ngu == 0) {
-                if (c.ct == 0) fail(c.sy, c.host_error, 4);
-                return drain(c, cur);
-            }
+            const uint32_t s0 = cur.k % kSlots, s1 = (cur.k + 1) % kSlots, s2 = (cur.k + (ngu > 2 ? 2 : 0)) % kSlots;
             stamp(a, cta, c.ct, 2 + l * 12 + 9);
-            if (l == 12) stamp_value(a, cta, c.ct, 308, clock64());
-            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(gw[0] + kGainOff), 0);
-            if (l == 12) stamp_value(a, cta, c.ct, 309, clock64());
+            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(S.ring[s0] + kGainOff), 0);
             stamp(a, cta, c.ct, 2 + l * 12 + 10);
-            Tiles tl{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}, T, 0};
-            for (int i = 0; i < 3; i++) {
-                const uint8_t *w = gw[i] ? gw[i] : gw[0];
-                const int ti = reinterpret_cast<const ChunkHdr *>(w)->count / 8;
-                tl.frag[i] = w + sizeof(ChunkHdr);
-                tl.sc[i] = reinterpret_cast<const float *>(tl.frag[i] + (size_t)ti * kTileBytes);
-            }
+            Tiles tl{{S.ring[s0] + sizeof(ChunkHdr), S.ring[s1] + sizeof(ChunkHdr), S.ring[s2] + sizeof(ChunkHdr)},
+                     {nullptr, nullptr, nullptr},
+                     T,
+                     0};
+            // chunk i holds tiles 2i, 2i + 1 (the last chunk may hold one)
+            tl.sc[0] = reinterpret_cast<const float *>(tl.frag[0] + (size_t)min(2, T) * kTileBytes);
+            tl.sc[1] = reinterpret_cast<const float *>(tl.frag[1] + (size_t)max(1, min(2, T - 2)) * kTileBytes);
+            tl.sc[2] = reinterpret_cast<const float *>(tl.frag[2] + (size_t)max(1, min(2, T - 4)) * kTileBytes);
             gemv_mma(&S, c.cw, c.lane, tl);
             cbar();
-            if (l == 12) stamp_value(a, cta, c.ct, 310, clock64());
             // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and
             // its up row 8 below; it lands at its column of down step 0 (own block) or 1
             if (c.ct < 8 * T) {
                 const int t = c.ct >> 3, j = c.ct & 7;
-                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(gw[t >> 1]);
+                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(t >> 1) == 0 ? s0 : (t >> 1) == 1 ? s1 : s2]);
                 const int unit = (int)h->first + 8 * (t & 1) + j;
                 const float g = row_sum(c, T, 16 * t + j), u = row_sum(c, T, 16 * t + 8 + j);
                 S.hst[(unit >> 5) == cta ? 0 : 1][unit & 31] = (g / (1.0f + expf(-g))) * u;
@@ -1122,9 +1117,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             remaining -= ngu;
         }
         stamp(a, cta, c.ct, 2 + l * 12 + 7);
-        if (l == 12) stamp_value(a, cta, c.ct, 311, clock64());
         quantize_slice(c, nks);
-        if (l == 12) stamp_value(a, cta, c.ct, 312, clock64());
         {
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
             for (;;) {
@@ -1206,36 +1199,107 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         if (!gather<1>(c, xin_r, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, 300);
         const int lo = a.P->head_lo[cta], n = a.P->head_lo[cta + 1] - lo;
-        bool first = true;
-        for (;;) {
-            const int more = next_is(c, cur, remaining, HEAD, LAYERS);
-            if (more < 0) return drain(c, cur);
-            if (!more) break;
-            const uint8_t *w = take(c, cur, HEAD);
-            if (!w) return drain(c, cur);
-            if (first) {
-                norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), cta == 0);
-                if (cta == 0)
-                    for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
-                first = false;
-            }
-            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            const int R = hd.count;
-            int T;
-            bool half;
-            chunk_tiles(HEAD, hd.count, T, half);
-            const uint8_t *frag = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(frag + (half ? kHalfBytes : (size_t)T * kTileBytes));
-            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, T, half ? 1 : 0});
-            cbar();
-            if (c.ct < R) {
-                const float d = row_sum(c, T, c.ct);
-                a.b.logits[hd.first + c.ct] = d;
-                S.u.hl[hd.first + c.ct - lo] = d;
-            }
-            give_back(c, cur);
-            remaining--;
+        // the rest of this CTA's stream is its head chunks: 32 vocabulary rows (two
+        // tiles) each, the last one shorter
+        const int nhc = remaining;
+        if (nhc <= 0 || !peek(c, cur, 0)) {
+            if (c.ct == 0) fail(c.sy, c.host_error, 4);
+            return drain(c, cur);
         }
+        if (c.ct == 0)
+            for (int i = 0; i < kSlots; i++) S.slot_fill[(cur.k + i) % kSlots] = (int)(cur.k + i);
+        norm_quantize(&S, c.ct, reinterpret_cast<const float *>(S.ring[cur.k % kSlots] + kGainOff), cta == 0);
+        if (cta == 0)
+            for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
+        // Warp w takes tiles w, w + 16, ... in order (tile t = tile t & 1 of chunk t >> 1),
+        // each over all 896 columns, so its lanes hold complete row sums; the warp that
+        // finishes the last tile of a chunk starts the copy of the chunk kSlots ahead
+        // into its slot.  A chunk's copy waits only for tiles earlier in every warp's
+        // order, so the warps never wait on each other in a cycle.  A warp's next chunk
+        // is 2 * kSlots chunks on, two fills of the same slot later, and a parity wait is
+        // only exact once the chunk's own copy has been issued (the fill before it then
+        // has landed and been read): the warp first waits for that on slot_fill.
+        int ok = 1;
+        {
+            const int g = c.lane >> 2, tig = c.lane & 3;
+            for (int t = c.cw; t < 2 * nhc; t += kConsumerWarps) {
+                const uint32_t k = cur.k + (uint32_t)(t >> 1), slot = k % kSlots;
+                if (*(volatile int *)&S.slot_fill[slot] < (int)k) {
+                    const long long t0 = clock64();
+                    while (*(volatile int *)&S.slot_fill[slot] < (int)k) {
+                        if (give_up(c.sy, c.host_error, clock64() - t0, 2)) {
+                            ok = 0;
+                            break;
+                        }
+                    }
+                    if (!ok) break;
+                }
+                if (!mbar_wait(&S.full[slot], (k / kSlots) & 1, c.sy, c.host_error)) {
+                    ok = 0;
+                    break;
+                }
+                const uint8_t *w = S.ring[slot];
+                const ChunkHdr *hd = reinterpret_cast<const ChunkHdr *>(w);
+                const int rows = (int)hd->count;
+                if (hd->kind != HEAD || rows < 1 || rows > kHeadPerChunk) {
+                    if (c.lane == 0) fail(c.sy, c.host_error, 4);
+                    ok = 0;
+                    break;
+                }
+                const bool half = rows <= 8;
+                const int tin = half ? 1 : (rows + 15) / 16, ti = t & 1;
+                if (ti < tin) {
+                    const uint8_t *frag = w + sizeof(ChunkHdr);
+                    const float *sc = reinterpret_cast<const float *>(frag + (half ? kHalfBytes : tin * kTileBytes)) +
+                                      ti * 16 * kGroups;
+                    frag += ti * kTileBytes;
+                    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 2
+                    for (int grp = 0; grp < kGroups; grp++) {
+                        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int ks = 2 * grp + h;
+                            uint4 av;
+                            if (half) {
+                                const uint2 v = *reinterpret_cast<const uint2 *>(frag + ((size_t)ks * 32 + c.lane) * 8);
+                                av = make_uint4(v.x, 0u, v.y, 0u);
+                            } else {
+                                av = *reinterpret_cast<const uint4 *>(frag + ((size_t)ks * 32 + c.lane) * 16);
+                            }
+                            mma_s8(d, av, S.bf[ks][c.lane]);
+                        }
+                        float v0, v1;
+                        combine(d, v0, v1);
+                        const float f = S.sxs[grp];
+                        acc0 = fmaf(v0, sc[g * kGroups + grp] * f, acc0);
+                        if (!half) acc1 = fmaf(v1, sc[(g + 8) * kGroups + grp] * f, acc1);
+                    }
+                    if (tig == 0) {
+                        const int r0 = 16 * ti + g, r1 = r0 + 8;
+                        if (r0 < rows) {
+                            a.b.logits[hd->first + r0] = acc0;
+                            S.u.hl[hd->first + r0 - lo] = acc0;
+                        }
+                        if (!half && r1 < rows) {
+                            a.b.logits[hd->first + r1] = acc1;
+                            S.u.hl[hd->first + r1 - lo] = acc1;
+                        }
+                    }
+                    __syncwarp();
+                    if (c.lane == 0) {
+                        __threadfence_block();
+                        if (atomicAdd(&S.slot_done[slot], 1) + 1 == tin) {
+                            S.slot_done[slot] = 0;
+                            issue(c, k + kSlots, true);
+                        }
+                    }
+                }
+            }
+        }
+        if (!cbar_and(ok)) return drain(c, cur);
+        cur.k += nhc;
+        remaining = 0;
         cbar();
         if (decode) {
             // penalty (distinct ids of the history window) and control mask on this
@@ -1281,7 +1345,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 
     // ---- end of step: the last CTA finishes the token
     stamp(a, cta, c.ct, 301);
-    stamp_value(a, cta, c.ct, 304, clock64());
     cbar();
     if (c.ct == 0) {
         __threadfence();
