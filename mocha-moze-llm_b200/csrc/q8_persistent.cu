@@ -269,10 +269,10 @@ MB_DEV void dw_load4(const unsigned long long *p, unsigned long long (&v)[4])
 
 // Poll the data words src[0..n) (n a multiple of 4, src 32-byte aligned) that `want`
 // selects until each carries `tag`, storing their floats to dst.  Thread ct owns the
-// 4-word groups ct, ct+kNT, ...; each request covers a whole group, only groups with
-// missing words are polled again, and a short sleep between rounds keeps 148 CTAs
-// from saturating the L2 slices that hold the words.  Every consumer thread returns
-// the same verdict.
+// 4-word groups ct, ct+kNT, ...; each request covers a whole group and only groups
+// with missing words are polled again, back to back: the exchange is bound by how
+// soon a reader sees the last word, not by the polling traffic (the words have four
+// replicas).  Every consumer thread returns the same verdict.
 template <int E, typename Want>
 MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, Want want,
                       int *iters = nullptr)
@@ -314,7 +314,6 @@ MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag
             ok = 0;
             break;
         }
-        __nanosleep(64);
     }
     if (iters) atomicMax(iters, it);
     return cbar_and(ok) != 0;
@@ -1183,7 +1182,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                         ok = 0;
                         break;
                     }
-                    __nanosleep(32);
                 }
                 float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
                 sum = mb::warp_sum(sum);
