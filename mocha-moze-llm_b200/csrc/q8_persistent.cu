@@ -70,7 +70,6 @@ constexpr int kDownTiles = DIM / 16;           // 56 row tiles of the down proje
 constexpr int kPartWords = HEADS * kMaxSplit * ATTN_PARTIAL;
 constexpr int kGpStride = kConsumerWarps + 1;  // padded: conflict-free row sums
 constexpr int kKStride = HEAD_DIM + 4;         // cached key row in shared memory: conflict-free float4 reads
-constexpr int kPvGroups = kNT / HEAD_DIM;      // position groups of the P.V product
 constexpr int kStrideKv = replica_stride(2 * KV);
 constexpr int kStridePart = replica_stride(kPartWords);
 constexpr int kStrideDim = replica_stride(DIM);
@@ -89,8 +88,7 @@ struct Smem {
             float k[kAttnLenMax][kKStride];
             float v[kAttnLenMax][HEAD_DIM];
             float q[HEAD_DIM];
-            float e[kAttnLenMax + 1];
-            float pv[kPvGroups][HEAD_DIM];
+            float wp[kConsumerWarps][HEAD_DIM + 4];  // per-warp partials: max, sum of weights, 64 accumulators
         } att;
         float hl[kHeadSlice];      // this CTA's slice of the logits
     } u;
@@ -976,13 +974,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             cp_async_wait_all();
             if (!cbar_and(ok)) return drain(c, cur);
-            // scores: warp cw takes positions 8*cw + (lane & 7), lane >> 3 picks the
-            // quarter of the 64 dims (float4 columns 4m + quarter); key rows are
-            // kKStride floats apart so the eight lanes of a phase hit distinct banks
-            {
+            // Online softmax per warp: warp cw owns positions 8 cw .. 8 cw + 7 (lane & 7
+            // picks the position, lane >> 3 the quarter of the 64 dims of its score); it
+            // keeps its own max, sum of weights and 64 accumulators, and 64 threads merge
+            // the warp partials.  Key rows are kKStride floats apart so the eight lanes of
+            // a phase hit distinct banks.
+            const int nw = (np + 7) / 8;  // warps holding positions (np <= 128)
+            if (c.cw < nw) {
                 const int p = 8 * c.cw + (c.lane & 7), qd = c.lane >> 3;
+                const bool valid = p < np;
                 float z = 0.f;
-                if (p < np) {
+                if (valid) {
                     const float4 *k4 = reinterpret_cast<const float4 *>(S.u.att.k[p]);
                     const float4 *q4 = reinterpret_cast<const float4 *>(S.u.att.q);
 #pragma unroll
@@ -996,44 +998,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 }
                 z += __shfl_xor_sync(0xffffffffu, z, 8);
                 z += __shfl_xor_sync(0xffffffffu, z, 16);
-                if (qd == 0 && p < np) S.u.att.e[p] = z * 0.125f;
-            }
-            cbar();
-            if (c.cw == 0) {
-                float m = -INFINITY;
-                for (int p = c.lane; p < np; p += 32) m = fmaxf(m, S.u.att.e[p]);
-                m = mb::warp_max(m);
-                float lsum = 0.f;
-                for (int p = c.lane; p < np; p += 32) {
-                    const float e = expf(S.u.att.e[p] - m);
-                    S.u.att.e[p] = e;
-                    lsum += e;
+                const float sc = valid ? z * 0.125f : -INFINITY;
+                const float m = mb::warp_max(sc);
+                const float e = valid ? expf(sc - m) : 0.f;
+                const float lw = mb::warp_sum(qd == 0 ? e : 0.f);  // each position sits in four lanes
+                float a0 = 0.f, a1 = 0.f;
+                const float *vb = S.u.att.v[8 * c.cw];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float ej = __shfl_sync(0xffffffffu, e, j);  // lane j holds position 8 cw + j
+                    if (8 * c.cw + j < np) {
+                        a0 = fmaf(ej, vb[j * HEAD_DIM + c.lane], a0);
+                        a1 = fmaf(ej, vb[j * HEAD_DIM + 32 + c.lane], a1);
+                    }
                 }
-                lsum = mb::warp_sum(lsum);
+                float *wp = S.u.att.wp[c.cw];
+                wp[2 + c.lane] = a0;
+                wp[2 + 32 + c.lane] = a1;
                 if (c.lane == 0) {
-                    S.red[0][0] = m;
-                    S.red[0][1] = lsum;
+                    wp[0] = m;
+                    wp[1] = lw;
                 }
-            }
-            cbar();
-            // P.V: thread (d, g) sums positions g, g + 8, ...; groups added in order
-            {
-                const int d = c.ct % HEAD_DIM, g = c.ct / HEAD_DIM;
-                float acc = 0.f;
-                for (int p = g; p < np; p += kPvGroups) acc = fmaf(S.u.att.e[p], S.u.att.v[p][d], acc);
-                S.u.att.pv[g][d] = acc;
             }
             cbar();
             if (c.ct < HEAD_DIM) {
-                float acc = 0.f;
-#pragma unroll
-                for (int g = 0; g < kPvGroups; g++) acc += S.u.att.pv[g][c.ct];
+                float mx = -INFINITY;
+                for (int w = 0; w < nw; w++) mx = fmaxf(mx, S.u.att.wp[w][0]);
+                float lsum = 0.f, acc = 0.f;
+                for (int w = 0; w < nw; w++) {
+                    const float f = expf(S.u.att.wp[w][0] - mx);
+                    lsum = fmaf(f, S.u.att.wp[w][1], lsum);
+                    acc = fmaf(f, S.u.att.wp[w][2 + c.ct], acc);
+                }
                 const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
                 unsigned long long *out = scr.part + ((size_t)h * kMaxSplit + unit.split) * ATTN_PARTIAL;
                 dw_store_rep(out + 2 + c.ct, kStridePart, acc, ptag);
                 if (c.ct == 0) {
-                    dw_store_rep(out, kStridePart, S.red[0][0], ptag);
-                    dw_store_rep(out + 1, kStridePart, S.red[0][1], ptag);
+                    dw_store_rep(out, kStridePart, mx, ptag);
+                    dw_store_rep(out + 1, kStridePart, lsum, ptag);
                 }
             }
             cbar();
