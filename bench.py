@@ -32,7 +32,7 @@ PROMPT_LEN, NEW_TOKENS, PROMPT_SEED, MODEL_SEED = 34, 256, 7, 1
 WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per token
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 REF_SAMPLE_TOKENS = 32
-TRAFFIC_PER_TOKEN = 530_606_336  # DRAM read + write per k_step launch (526.93 + 3.67 MB), ncu, position 34
+TRAFFIC_PER_TOKEN = 554_759_680  # DRAM read + write per k_step launch (551.35 + 3.41 MB), ncu, position 40
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt

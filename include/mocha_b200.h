@@ -69,8 +69,12 @@ int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int war
 int mocha_q8_launches_per_step(mocha_q8 *h);
 
 /* Diagnostic: one persistent step (forward + projection) for `token` at `pos` that
- * records %globaltimer stamps at every phase boundary of every CTA into
- * stamps[148][256] (0 = not reached).  Fails on the per-phase graph path. */
+ * records %globaltimer stamps of every CTA into stamps[148][320] (0 = not reached):
+ * [0] start; per layer l at 2 + 12 l: +0 x_in gathered, +1 QKV done, +2 attention
+ * done, +3 attention combined, +4 O done, +5 x_mid gathered, +9 gate/up chunks
+ * resident, +10 gate/up input quantized, +7 SwiGLU done, +6 down partials stored,
+ * +8 own rows reduced; [300] head start, [301] head done, [302] token drawn.
+ * Fails on the per-phase graph path. */
 int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps);
 
 /* Penalty + control mask + top-k candidates (the selection gpu_collect performs)

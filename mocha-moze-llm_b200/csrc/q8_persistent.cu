@@ -103,7 +103,6 @@ struct Smem {
     Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors
     unsigned long long full[kSlots];
     int flag;
-    int iters;  // poll iterations of the last traced gather
     int token, pos;
     int issued;                  // chunks whose bulk copy has been started
     int slot_done[kSlots];       // head phase: tiles of the slot's chunk finished
@@ -272,8 +271,7 @@ MB_DEV void dw_load4(const unsigned long long *p, unsigned long long (&v)[4])
 // soon a reader sees the last word, not by the polling traffic (the words have four
 // replicas).  Every consumer thread returns the same verdict.
 template <int E, typename Want>
-MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, Want want,
-                      int *iters = nullptr)
+MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, Want want)
 {
     const int ng = n >> 2;
     unsigned need[E];
@@ -285,7 +283,7 @@ MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag
 #pragma unroll
             for (int j = 0; j < 4; j++) need[e] |= want(4 * g + j) ? (1u << j) : 0u;
     }
-    int ok = 1, it = 0;
+    int ok = 1;
     long long t0 = 0;
     for (;;) {
         unsigned missing = 0;
@@ -305,7 +303,6 @@ MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag
             missing |= need[e];
         }
         if (!missing) break;
-        it++;
         if (t0 == 0) {
             t0 = clock64();
         } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
@@ -313,7 +310,6 @@ MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag
             break;
         }
     }
-    if (iters) atomicMax(iters, it);
     return cbar_and(ok) != 0;
 }
 
@@ -322,9 +318,9 @@ struct All {
 };
 
 template <int E>
-MB_DEV bool gather(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, int *iters = nullptr)
+MB_DEV bool gather(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst)
 {
-    return gather_if<E>(c, src, n, tag, dst, All{}, iters);
+    return gather_if<E>(c, src, n, tag, dst, All{});
 }
 
 // ---- int8 tensor-core matrix-vector products ------------------------------------

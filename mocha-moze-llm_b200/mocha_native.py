@@ -184,6 +184,14 @@ class Q8Handle:
             raise RuntimeError("mocha_q8_bench_decode failed")
         return ms.value
 
+    def trace_step(self, token: int, pos: int):
+        """%globaltimer stamps [148 CTAs][320] of one persistent step (see mocha_q8_trace_step)."""
+        import numpy as np
+        st = np.zeros((148, 320), dtype=np.uint64)
+        if self.lib.mocha_q8_trace_step(self.h, token, pos, st.ctypes.data) != 0:
+            raise RuntimeError("mocha_q8_trace_step failed")
+        return st
+
 
 class GgufHandle:
     """A GGUF llama / qwen2 model resident on one device (mocha_gguf handle)."""
