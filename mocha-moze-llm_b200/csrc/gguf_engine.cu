@@ -321,6 +321,7 @@ int launch_ok(const char *what)
 struct Layer {
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     gguf::DevMat q{}, k{}, v{}, o{}, gate{}, up{}, down{};
+    gguf::MmaMat mq{}, mk{}, mv{}, mo{}, mgate{}, mup{}, mdown{};  // tensor-core layout
 };
 
 }  // namespace
@@ -332,6 +333,8 @@ struct mocha_gguf {
     std::vector<uint8_t *> allocs;
     std::vector<Layer> layers;
     gguf::DevMat embd{};
+    gguf::MmaMat membd{};  // the tied head in the tensor-core layout
+    bool mma = true;       // GEMVs on the tensor cores (MOCHA_B200_GGUF_GEMV=cuda: CUDA cores)
     const float *out_norm = nullptr;
     RopeArgs rope{};
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
@@ -382,20 +385,44 @@ int enqueue_forward(mocha_gguf *m, bool project)
         g.eps = in.eps;
         return gguf::enqueue_gemv_multi(g, s);
     };
+    auto mmv = [&](std::initializer_list<std::pair<const gguf::MmaMat *, float *>> mats, const float *x,
+                   const float *gain, bool accumulate, const float *up = nullptr) {
+        gguf::MultiGemvMma g{};
+        int i = 0;
+        for (auto &mt : mats) {
+            g.m[i] = *mt.first;
+            g.y[i] = mt.second;
+            i++;
+        }
+        g.n = i;
+        g.cols = mats.begin()->first->cols;
+        g.accumulate = accumulate ? 1 : 0;
+        g.x = x;
+        g.gain = gain;
+        g.up = up;
+        g.eps = in.eps;
+        return gguf::enqueue_gemv_mma(g, s);
+    };
+    const bool tc = m->mma;
     for (int l = 0; l < in.layers && !rc; l++) {
         const Layer &L = m->layers[l];
         // RMSNorm folded into the fused q|k|v GEMV
-        rc = multi({{&L.q, m->q}, {&L.k, m->k}, {&L.v, m->v}}, m->x, L.attn_norm, false) ||
+        rc = (tc ? mmv({{&L.mq, m->q}, {&L.mk, m->k}, {&L.mv, m->v}}, m->x, L.attn_norm, false)
+                 : multi({{&L.q, m->q}, {&L.k, m->k}, {&L.v, m->v}}, m->x, L.attn_norm, false)) ||
              pdl(k_qkv_post, dim3(8), dim3(256), s, m->q, m->k, m->v, L.bq, L.bk, L.bv, m->rope, m->state + 1, m->kc,
                  m->vc, l) ||
              pdl(k_attention, dim3(in.heads), dim3(kAttnThreads), s, m->q, m->kc, m->vc, m->rope, m->state + 1, l,
                  m->att) ||
-             multi({{&L.o, m->x}}, m->att, nullptr, true) ||
-             multi({{&L.gate, m->g}, {&L.up, m->u}}, m->x, L.ffn_norm, false) ||
-             pdl(k_swiglu, dim3((in.ffn + 255) / 256), dim3(256), s, m->g, m->u, m->h, in.ffn) ||
-             multi({{&L.down, m->x}}, m->h, nullptr, true);
+             (tc ? mmv({{&L.mo, m->x}}, m->att, nullptr, true) : multi({{&L.o, m->x}}, m->att, nullptr, true)) ||
+             (tc ? mmv({{&L.mgate, m->g}, {&L.mup, m->u}}, m->x, L.ffn_norm, false)
+                 : multi({{&L.gate, m->g}, {&L.up, m->u}}, m->x, L.ffn_norm, false)) ||
+             (tc ? mmv({{&L.mdown, m->x}}, m->g, nullptr, true, m->u)
+                 : pdl(k_swiglu, dim3((in.ffn + 255) / 256), dim3(256), s, m->g, m->u, m->h, in.ffn) ||
+                       multi({{&L.down, m->x}}, m->h, nullptr, true));
     }
-    if (!rc && project) rc = multi({{&m->embd, m->logits}}, m->x, m->out_norm, false);
+    if (!rc && project)
+        rc = tc ? mmv({{&m->membd, m->logits}}, m->x, m->out_norm, false)
+                : multi({{&m->embd, m->logits}}, m->x, m->out_norm, false);
     return rc || launch_ok("gguf forward");
 }
 
@@ -442,7 +469,7 @@ void release(mocha_gguf *m)
 }
 
 int upload_matrix(mocha_gguf *m, const Gguf &g, const uint8_t *file, const std::string &name, int rows, int cols,
-                  gguf::DevMat *out, uint8_t *staging)
+                  gguf::DevMat *out, uint8_t *staging, gguf::MmaMat *mma = nullptr)
 {
     const auto it = g.tensors.find(name);
     if (it == g.tensors.end()) {
@@ -460,6 +487,13 @@ int upload_matrix(mocha_gguf *m, const Gguf &g, const uint8_t *file, const std::
     if (dev_alloc(m, (void **)&dst, bytes)) return 1;
     TRY(cudaMemcpyAsync(staging, file + g.data_start + t.offset, bytes, cudaMemcpyHostToDevice, m->stream));
     if (gguf::enqueue_repack(t.type, staging, rows, cols, dst, m->stream)) return 1;
+    if (mma) {
+        const size_t mb = gguf::mma_bytes(t.type, rows, cols);
+        uint8_t *mdst = nullptr;
+        if (!mb || dev_alloc(m, (void **)&mdst, mb)) return 1;
+        if (gguf::enqueue_repack_mma(t.type, staging, rows, cols, mdst, m->stream)) return 1;
+        *mma = gguf::MmaMat{t.type, rows, cols, mdst};
+    }
     TRY(cudaStreamSynchronize(m->stream));
     *out = gguf::make_devmat(t.type, rows, cols, dst);
     return 0;
@@ -551,7 +585,10 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
     for (const auto &t : g.tensors) max_raw = max_raw > tensor_bytes(t.second) ? max_raw : tensor_bytes(t.second);
     uint8_t *staging = nullptr;
     TRY(cudaMalloc(&staging, max_raw));
-    int rc = upload_matrix(m, g, file, "token_embd.weight", in.vocab, dim, &m->embd, staging);
+    const char *gemv = getenv("MOCHA_B200_GGUF_GEMV");
+    m->mma = !(gemv && !strcmp(gemv, "cuda"));
+    int rc = upload_matrix(m, g, file, "token_embd.weight", in.vocab, dim, &m->embd, staging,
+                           m->mma ? &m->membd : nullptr);
     rc = rc || upload_f32(m, g, file, "output_norm.weight", dim, &m->out_norm, false);
     m->layers.resize(in.layers);
     for (int l = 0; l < in.layers && !rc; l++) {
@@ -562,13 +599,15 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
              upload_f32(m, g, file, p + "attn_q.bias", dim, &L.bq, true) ||
              upload_f32(m, g, file, p + "attn_k.bias", kvd, &L.bk, true) ||
              upload_f32(m, g, file, p + "attn_v.bias", kvd, &L.bv, true) ||
-             upload_matrix(m, g, file, p + "attn_q.weight", dim, dim, &L.q, staging) ||
-             upload_matrix(m, g, file, p + "attn_k.weight", kvd, dim, &L.k, staging) ||
-             upload_matrix(m, g, file, p + "attn_v.weight", kvd, dim, &L.v, staging) ||
-             upload_matrix(m, g, file, p + "attn_output.weight", dim, dim, &L.o, staging) ||
-             upload_matrix(m, g, file, p + "ffn_gate.weight", in.ffn, dim, &L.gate, staging) ||
-             upload_matrix(m, g, file, p + "ffn_up.weight", in.ffn, dim, &L.up, staging) ||
-             upload_matrix(m, g, file, p + "ffn_down.weight", dim, in.ffn, &L.down, staging);
+             upload_matrix(m, g, file, p + "attn_q.weight", dim, dim, &L.q, staging, m->mma ? &L.mq : nullptr) ||
+             upload_matrix(m, g, file, p + "attn_k.weight", kvd, dim, &L.k, staging, m->mma ? &L.mk : nullptr) ||
+             upload_matrix(m, g, file, p + "attn_v.weight", kvd, dim, &L.v, staging, m->mma ? &L.mv : nullptr) ||
+             upload_matrix(m, g, file, p + "attn_output.weight", dim, dim, &L.o, staging, m->mma ? &L.mo : nullptr) ||
+             upload_matrix(m, g, file, p + "ffn_gate.weight", in.ffn, dim, &L.gate, staging,
+                           m->mma ? &L.mgate : nullptr) ||
+             upload_matrix(m, g, file, p + "ffn_up.weight", in.ffn, dim, &L.up, staging, m->mma ? &L.mup : nullptr) ||
+             upload_matrix(m, g, file, p + "ffn_down.weight", dim, in.ffn, &L.down, staging,
+                           m->mma ? &L.mdown : nullptr);
     }
     cudaFree(staging);
     if (rc) return 1;
@@ -624,7 +663,8 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
     if (capture(m, &m->g_forward[0], 0) || capture(m, &m->g_forward[1], 1) || capture(m, &m->g_prefill, 2) ||
         capture(m, &m->g_decode, 3))
         return 1;
-    m->launches_per_token = 1 + (unsigned long long)in.layers * 7 + 1 + 3;
+    // embedding row, per layer q|k|v, post, attention, O, gate|up, (SwiGLU,) down; head; sampler
+    m->launches_per_token = 1 + (unsigned long long)in.layers * (m->mma ? 6 : 7) + 1 + 3;
     TRY(cudaStreamSynchronize(m->stream));
     return 0;
 }

@@ -65,4 +65,39 @@ int enqueue_gemv_multi(const MultiGemv &g, cudaStream_t s);
 // out[c] = exact dequantised weight (row *row_index, read on the device), c < cols.
 int enqueue_dequant_row(const DevMat &m, const int *row_index, float *out, cudaStream_t s);
 
+// ---- tensor-core layout for the engine's GEMVs (csrc/gguf_mma.cu) ----------------------
+//
+// A matrix (rows a multiple of 16, cols a multiple of 256) repacked into 16-row tiles in
+// the A-fragment order of mma.sync, with the file's bytes per weight.
+struct MmaMat {
+    int type;
+    int rows, cols;
+    const uint8_t *body;
+};
+
+// bytes of one 16-row tile, 0 when type/cols are unsupported
+__host__ __device__ inline size_t mma_tile_bytes(int type, int cols)
+{
+    if (cols <= 0 || cols % 256) return 0;
+    if (type == Q4_K) return (size_t)(cols / 256) * 2304;
+    if (type == Q6_K) return (size_t)(cols / 256) * 3360;
+    if (type == Q8_0) return (size_t)(cols / 32) * 544;
+    return 0;
+}
+inline size_t mma_bytes(int type, int rows, int cols) { return rows % 16 ? 0 : mma_tile_bytes(type, cols) * (rows / 16); }
+
+// Repack `rows` file rows (raw file bytes, on the device) into `dst` (mma_bytes long).
+int enqueue_repack_mma(int type, const uint8_t *raw, int rows, int cols, uint8_t *dst, cudaStream_t s);
+
+// y[i][r] (+)= W_i[r] . xn for up to three matrices with the same input, as MultiGemv.
+struct MultiGemvMma {
+    MmaMat m[3];
+    float *y[3];
+    int n, cols, accumulate;
+    const float *x, *gain;
+    const float *up;  // non-null: the input is silu(x) * up (SwiGLU folded into the down GEMV)
+    float eps;
+};
+int enqueue_gemv_mma(const MultiGemvMma &g, cudaStream_t s);
+
 }  // namespace gguf

@@ -51,6 +51,31 @@ MB_DEV int4 ld_stream16(const void *ptr)
     return r;
 }
 
+MB_DEV uint4 ld_stream16u(const void *ptr)
+{
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(ptr), "l"(evict_first_policy()));
+    return r;
+}
+
+MB_DEV uint2 ld_stream8(const void *ptr)
+{
+    uint2 r;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+        : "=r"(r.x), "=r"(r.y)
+        : "l"(ptr), "l"(evict_first_policy()));
+    return r;
+}
+
+MB_DEV uint32_t ld_stream4(const void *ptr)
+{
+    uint32_t r;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(r) : "l"(ptr), "l"(evict_first_policy()));
+    return r;
+}
+
 MB_DEV float ld_stream_f32(const float *ptr)
 {
     float r;
