@@ -43,6 +43,7 @@ namespace {
 constexpr int kThreads = 512, kWarps = kThreads / 32;
 constexpr int kGrid = mb::kSMs;  // one CTA per SM (512 threads x ~100 registers)
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
+constexpr size_t kPrefetchBytes = 160 * 1024;  // per CTA: 148 CTAs x 160 KB = 24 MB of the 126 MB L2
 
 // fp16 bits -> fp32 (exact for every fp16 value)
 MB_DEV float half_to_float(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu))); }
@@ -399,7 +400,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
         if (a < b) {
             const size_t tb = mma_tile_bytes(g.m[i].type, g.cols);
             const uint8_t *p0 = g.m[i].body + (size_t)(a - start) * tb;
+            // at most kPrefetchBytes per CTA: a head larger than L2 would evict its own lines
             size_t left = (size_t)(b - a) * tb;
+            left = left < kPrefetchBytes ? left : kPrefetchBytes;
             for (const uint8_t *q = p0; left > 0;) {
                 const unsigned n = (unsigned)(left < 32768 ? left : 32768);
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(n) : "memory");
