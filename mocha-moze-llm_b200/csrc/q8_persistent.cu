@@ -624,31 +624,9 @@ MB_DEV void stamp(const Args &a, int cta, int ct, int point)
     }
 }
 
-MB_DEV void stamp_value(const Args &a, int cta, int ct, int point, unsigned long long v)
-{
-    if (a.trace && ct == 0 && point < kTraceStamps) a.trace[cta * kTraceStamps + point] = v;
-}
-
 struct Cursor {
     uint32_t k;  // chunks consumed
 };
-
-// Row tiles of a 896-wide chunk: QKV and O chunks are one 8-row tile, gate/up chunks
-// two full tiles (8 gate + 8 up rows each), head chunks up to two full tiles, or one
-// 8-row tile for a short last chunk.
-MB_DEV void chunk_tiles(uint32_t kind, uint32_t count, int &T, bool &half)
-{
-    if (kind == QKV || kind == OPROJ) {
-        T = 1;
-        half = true;
-    } else if (kind == GATEUP) {
-        T = (int)count / 8;
-        half = false;
-    } else {
-        half = count <= 8;
-        T = half ? 1 : (int)(count + 15) / 16;
-    }
-}
 
 // Wait for the next chunk; returns the slot (header first) or null on failure.
 // Every chunk's range is checked against the bounds its consumers assume.
@@ -705,17 +683,6 @@ MB_DEV void give_back(Ctx &c, Cursor &cur)
     cbar();
     if (c.ct == 0) issue(c, cur.k + kSlots);
     cur.k++;
-}
-
-// Is the next chunk of `kind` in `layer`?  (waits for it to land, then reads its
-// header; -1 on failure)
-MB_DEV int next_is(Ctx &c, const Cursor &cur, int remaining, uint32_t kind, uint32_t layer)
-{
-    if (remaining <= 0) return 0;
-    const uint32_t slot = cur.k % kSlots, use = cur.k / kSlots;
-    if (!mbar_wait(&c.S.full[slot], use & 1, c.sy, c.host_error)) return -1;
-    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(c.S.ring[slot]);
-    return h->kind == kind && h->layer == layer ? 1 : 0;
 }
 
 // Error exit: wait (bounded) until every bulk copy started into this CTA's ring has
