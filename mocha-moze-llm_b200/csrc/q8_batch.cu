@@ -46,7 +46,7 @@ using mb::tq::Gemm;
 
 constexpr int QKV_ROWS = DIM + 2 * KV;  // q | k | v output rows of the fused projection
 constexpr int GU_ROWS = 2 * HIDDEN;     // gate | up
-constexpr int CHUNK = 64;               // keys per attention CTA
+constexpr int CHUNK = 64;               // keys per chunk of the block attention kernel
 constexpr int NCHUNK = CONTEXT / CHUNK;
 constexpr int PART = 2 + HEAD_DIM;      // chunk max, chunk sum, 64 weighted-V sums
 constexpr int NT = DIM / 4;             // row kernels: 4 features per thread
@@ -205,68 +205,6 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
     }
 }
 
-// One KV head, one chunk of up to 64 keys, the 7 query heads that share it: chunk
-// max, sum of exp(s - max) and the exp-weighted V sums.
-__global__ void __launch_bounds__(128) k_attn_chunk(const float *__restrict__ q, Rows rows, const float *__restrict__ kc,
-                                                    const float *__restrict__ vc, int layer, float *__restrict__ part)
-{
-    pdl_enter();
-    const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
-    const int pos = rows.pos[t], slot = rows.slot[t];
-    const int k0 = c * CHUNK;
-    if (k0 > pos) return;
-    const int nk = min(CHUNK, pos + 1 - k0);
-    __shared__ float sq[GQA][HEAD_DIM];
-    __shared__ float sk[CHUNK][HEAD_DIM + 1];
-    __shared__ float sv[CHUNK][HEAD_DIM];
-    __shared__ float sp[GQA][CHUNK];
-    __shared__ float smax[GQA], ssum[GQA];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int idx = tid; idx < GQA * HEAD_DIM; idx += 128)
-        sq[idx / HEAD_DIM][idx % HEAD_DIM] = q[(size_t)t * DIM + g * GQA * HEAD_DIM + idx];
-    const size_t base = kv_off(slot, layer, g, k0);
-    for (int idx = tid; idx < nk * HEAD_DIM; idx += 128) {
-        sk[idx / HEAD_DIM][idx % HEAD_DIM] = kc[base + idx];
-        sv[idx / HEAD_DIM][idx % HEAD_DIM] = vc[base + idx];
-    }
-    __syncthreads();
-    for (int idx = tid; idx < GQA * CHUNK; idx += 128) {
-        const int h = idx / CHUNK, kk = idx % CHUNK;
-        float z = -INFINITY;
-        if (kk < nk) {
-            z = 0.f;
-#pragma unroll 16
-            for (int d = 0; d < HEAD_DIM; d++) z += sq[h][d] * sk[kk][d];
-        }
-        sp[h][kk] = z;
-    }
-    __syncthreads();
-    for (int h = warp; h < GQA; h += 4) {
-        const float m = mb::warp_max(fmaxf(sp[h][lane], sp[h][lane + 32]));
-        const float e0 = lane < nk ? expf(sp[h][lane] - m) : 0.f;
-        const float e1 = lane + 32 < nk ? expf(sp[h][lane + 32] - m) : 0.f;
-        sp[h][lane] = e0;
-        sp[h][lane + 32] = e1;
-        const float s = mb::warp_sum(e0 + e1);
-        if (lane == 0) {
-            smax[h] = m;
-            ssum[h] = s;
-        }
-    }
-    __syncthreads();
-    float *out = part + ((size_t)t * HEADS + g * GQA) * NCHUNK * PART;
-    for (int idx = tid; idx < GQA * HEAD_DIM; idx += 128) {
-        const int h = idx / HEAD_DIM, d = idx % HEAD_DIM;
-        float acc = 0.f;
-        for (int kk = 0; kk < nk; kk++) acc += sp[h][kk] * sv[kk][d];
-        out[((size_t)h * NCHUNK + c) * PART + 2 + d] = acc;
-    }
-    if (tid < GQA) {
-        out[((size_t)tid * NCHUNK + c) * PART] = smax[tid];
-        out[((size_t)tid * NCHUNK + c) * PART + 1] = ssum[tid];
-    }
-}
-
 // Combine the chunks of one (row, head) into the attention output, as limbs for the O
 // GEMM (one warp, two dims per lane: the head is one 64-group).
 __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out, int per)
@@ -287,6 +225,107 @@ __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ p
     const float v[2] = {a0 / l, a1 / l};
     mb::tq::store_limbs<2, 32>(v, out.q + (size_t)t * 3 * DIM, DIM, h * HEAD_DIM + d,
                                out.s + (size_t)t * (DIM / GROUP) + h, threadIdx.x);
+}
+
+// Attention of one row (one query position) for one KV head and the GQA query heads
+// that share it, over keys 0..pos, written as limbs for the O GEMM.  One CTA of 256
+// threads per (KV head, row):
+//   scores  one key per thread: its 64-float key row against the 7 queries in shared
+//           memory, s[h][k] in shared memory (q carries the 0.125);
+//   softmax warp h takes head h: max, exp(s - max) in place, sum;
+//   P V     warp w takes keys w, w + 8, ...; lane l accumulates dims 2l, 2l + 1 of all
+//           7 heads (coalesced 256-byte V rows), the 8 warp partials are added in
+//           warp order;
+//   output  warp h divides by the sum and stores head h (one 64-group) as limbs.
+// Decode rows read their whole KV prefix once per KV head (no partial buffer, no
+// combine launch).
+constexpr int AR_THREADS = 256;
+constexpr int AR_WARPS = AR_THREADS / 32;
+
+__global__ void __launch_bounds__(AR_THREADS) k_attn_row(const float *__restrict__ q, Rows rows,
+                                                         const float *__restrict__ kc, const float *__restrict__ vc,
+                                                         int layer, Limbs out)
+{
+    pdl_enter();
+    const int g = blockIdx.x, t = blockIdx.y;
+    const int pos = rows.pos[t], slot = rows.slot[t];
+    const int nk = min(pos, CONTEXT - 1) + 1;
+    __shared__ __align__(16) float sq[GQA][HEAD_DIM];
+    __shared__ float ss[GQA][CONTEXT];
+    __shared__ __align__(16) float sred[AR_WARPS][GQA * HEAD_DIM];
+    __shared__ float sl[GQA];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < GQA * HEAD_DIM; i += AR_THREADS)
+        sq[i / HEAD_DIM][i % HEAD_DIM] = q[(size_t)t * DIM + g * GQA * HEAD_DIM + i];
+    __syncthreads();
+    const float *kb = kc + kv_off(slot, layer, g, 0);
+    const float *vb = vc + kv_off(slot, layer, g, 0);
+    for (int k = tid; k < nk; k += AR_THREADS) {
+        const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)k * HEAD_DIM);
+        float z[GQA];
+#pragma unroll
+        for (int h = 0; h < GQA; h++) z[h] = 0.f;
+#pragma unroll
+        for (int j = 0; j < HEAD_DIM / 4; j++) {
+            const float4 kv = __ldg(kr + j);
+#pragma unroll
+            for (int h = 0; h < GQA; h++) {
+                const float4 qv = *reinterpret_cast<const float4 *>(&sq[h][4 * j]);
+                z[h] = fmaf(qv.x, kv.x, z[h]);
+                z[h] = fmaf(qv.y, kv.y, z[h]);
+                z[h] = fmaf(qv.z, kv.z, z[h]);
+                z[h] = fmaf(qv.w, kv.w, z[h]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GQA; h++) ss[h][k] = z[h];
+    }
+    __syncthreads();
+    if (warp < GQA) {
+        float m = -INFINITY;
+        for (int k = lane; k < nk; k += 32) m = fmaxf(m, ss[warp][k]);
+        m = mb::warp_max(m);
+        float l = 0.f;
+        for (int k = lane; k < nk; k += 32) {
+            const float e = expf(ss[warp][k] - m);
+            ss[warp][k] = e;
+            l += e;
+        }
+        l = mb::warp_sum(l);
+        if (lane == 0) sl[warp] = l;
+    }
+    __syncthreads();
+    float a[GQA][2];
+#pragma unroll
+    for (int h = 0; h < GQA; h++) a[h][0] = a[h][1] = 0.f;
+#pragma unroll 4
+    for (int k = warp; k < nk; k += AR_WARPS) {
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(vb + (size_t)k * HEAD_DIM) + lane);
+#pragma unroll
+        for (int h = 0; h < GQA; h++) {
+            const float p = ss[h][k];
+            a[h][0] = fmaf(p, v.x, a[h][0]);
+            a[h][1] = fmaf(p, v.y, a[h][1]);
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GQA; h++)
+        *reinterpret_cast<float2 *>(&sred[warp][h * HEAD_DIM + 2 * lane]) = make_float2(a[h][0], a[h][1]);
+    __syncthreads();
+    if (warp < GQA) {
+        float sx = 0.f, sy = 0.f;
+#pragma unroll
+        for (int w = 0; w < AR_WARPS; w++) {
+            const float2 p = *reinterpret_cast<const float2 *>(&sred[w][warp * HEAD_DIM + 2 * lane]);
+            sx += p.x;
+            sy += p.y;
+        }
+        const float l = sl[warp];
+        const float v[2] = {sx / l, sy / l};
+        const int head = g * GQA + warp;
+        mb::tq::store_limbs<2, 32>(v, out.q + (size_t)t * 3 * DIM, DIM, head * HEAD_DIM + 2 * lane,
+                                   out.s + (size_t)t * (DIM / GROUP) + head, lane);
+    }
 }
 
 // h = silu(gate) * up from the gate|up partials, as limbs for the down GEMM; two
@@ -1039,9 +1078,7 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
         if (pdl(k_attn_block, dim3(n / QB, HEADS), 256, QB_SMEM, h->stream, h->q, rows, h->kc, h->vc, layer, h->la)) return 1;
         return 0;
     }
-    if (pdl(k_attn_chunk, dim3(NCHUNK, KV_HEADS, n), 128, 0, h->stream, h->q, rows, h->kc, h->vc, layer, h->apart)) return 1;
-    if (pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la, CHUNK)) return 1;
-    return 0;
+    return pdl(k_attn_row, dim3(KV_HEADS, n), AR_THREADS, 0, h->stream, h->q, rows, h->kc, h->vc, layer, h->la);
 }
 
 // Attention kernel for rows (host arrays): 2 when every block of 128 rows is one slot
@@ -1460,7 +1497,7 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
 extern "C" int mocha_q8b_launches_per_step(mocha_q8b *h)
 {
     if (!h) return -1;
-    return 1 + LAYERS * 10 + 1 + 2;  // embed+norm, 10 per layer, head GEMM, two sampler kernels
+    return 1 + LAYERS * 9 + 1 + 2;  // embed+norm, 9 per layer, head GEMM, two sampler kernels
 }
 
 // Sampler check: the batched sampler on caller-supplied logits (n rows of VOCAB) with
