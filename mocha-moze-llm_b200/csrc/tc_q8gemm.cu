@@ -295,7 +295,10 @@ tc::Split split_for(const Gemm &g, int n)
 {
     const int stages = g.p.K / kBK;
     const int tiles = (g.p.M / kBM) * ((n + kTokens - 1) / kTokens);
-    int splits = g.fixed_splits > 0 ? g.fixed_splits : (kSMs + tiles - 1) / tiles;
+    // as many K splits as keep the tiles within one wave: a second partial wave would
+    // add a tile's fixed costs (scale staging, output stores, a partial to reduce)
+    // without shortening the longest CTA's K walk
+    int splits = g.fixed_splits > 0 ? g.fixed_splits : kSMs / tiles;
     splits = splits < 1 ? 1 : (splits > stages ? stages : splits);
     const int per = (stages + splits - 1) / splits;
     return tc::Split{(stages + per - 1) / per, (long long)n * g.p.ldd};
