@@ -25,6 +25,25 @@ constexpr int kMaxGroups = 76;                  // groups of one split kept in s
 constexpr size_t kSxBytes = (size_t)kMaxGroups * kTokens * 4;
 constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256 + kSxBytes;
 
+// Two IEEE fp32 operations in one instruction (sm_100 paired FP32 lanes):
+// (d0, d1) = (a0 * b0 + c0, a1 * b1 + c1), each rounded to nearest.
+MB_DEV void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1)
+{
+    asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// (d0, d1) = (a0 * b0, a1 * b1), each rounded to nearest.
+MB_DEV void mul2(float &d0, float &d1, float a0, float a1, float b0, float b1)
+{
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 MB_DEV void fail(int *err, volatile int *abort, int code)
 {
     *abort = 1;
@@ -195,12 +214,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q8(const __grid_constant__
                     const float4 f = sx4[t4];
                     const float fs[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
+                    for (int e = 0; e < 4; e += 2) {
                         const int t = 4 * t4 + e;
-                        // 254 * (D0 + D1/254 + D2/254^2); D0*254 + D1 is exact in int32
-                        const int d01 = (int)r[3 * t] * 254 + (int)r[3 * t + 1];
-                        const float v = fmaf((float)(int)r[3 * t + 2], 1.f / 254.f, (float)d01);
-                        acc[t] = fmaf(v, sw * fs[e], acc[t]);
+                        // 254 * (D0 + D1/254 + D2/254^2) for tokens t, t + 1, the float work
+                        // on paired FP32 lanes; D0*254 + D1 is exact in int32
+                        float v0, v1, w0, w1;
+                        const int da = (int)r[3 * t] * 254 + (int)r[3 * t + 1];
+                        const int db = (int)r[3 * t + 3] * 254 + (int)r[3 * t + 4];
+                        fma2(v0, v1, (float)(int)r[3 * t + 2], (float)(int)r[3 * t + 5], 1.f / 254.f, 1.f / 254.f,
+                             (float)da, (float)db);
+                        mul2(w0, w1, sw, sw, fs[e], fs[e + 1]);
+                        fma2(acc[t], acc[t + 1], v0, v1, w0, w1, acc[t], acc[t + 1]);
                     }
                 }
             }
