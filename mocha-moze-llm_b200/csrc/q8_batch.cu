@@ -8,9 +8,11 @@
 // decode step of a batch (one row per slot).  Per layer:
 //
 //   norm+split -> QKV GEMM (q|k|v rows fused, 1152 x 896) -> bias + RoPE + KV write
-//   -> attention over key chunks of 64 -> chunk combine + split -> O GEMM
-//   -> residual + norm + split -> gate|up GEMM (9728 x 896) -> SwiGLU + split
-//   -> down GEMM -> residual + norm (next layer, or the final norm of projected rows)
+//   -> attention (prompt blocks: key spans + span combine; decode rows: one kernel)
+//   + split -> O GEMM -> residual + norm + split
+//   -> gate|up GEMM (9728 x 896, rows interleaved per 64) with SwiGLU + split in its
+//   epilogue (prompt passes) or in its own kernel (decode steps) -> down GEMM -> residual + norm (next layer, or the final norm of
+//   projected rows)
 //
 // then the tied-embedding head GEMM for the projected rows and, in the token loop,
 // the reference sampler for each projected row (penalty over the last 64 tokens,
@@ -328,19 +330,22 @@ __global__ void __launch_bounds__(AR_THREADS) k_attn_row(const float *__restrict
     }
 }
 
-// h = silu(gate) * up from the gate|up partials, as limbs for the down GEMM; two
-// features per thread.  grid (ceil(HIDDEN / 512), rows)
+// h = silu(gate) * up from the gate|up partials (rows interleaved per 64: gate feature
+// f at row 128 (f / 64) + f % 64, up feature f 64 rows further), as limbs for the down
+// GEMM; two features per thread.  grid (ceil(HIDDEN / 512), rows).  Decode steps use
+// it: their gate|up GEMM covers only half the SMs, so the SwiGLU runs better as its own
+// launch over all of them than as a tail of that GEMM.
 __global__ void __launch_bounds__(256) k_swiglu(const float *__restrict__ part, int splits, long long sstride,
                                                 int8_t *hq, float *hs)
 {
     pdl_enter();
     const int t = blockIdx.y, i = (blockIdx.x * 256 + threadIdx.x) * 2;
     if (i >= HIDDEN) return;
-    const float *p = part + (size_t)t * GU_ROWS;
-    float2 g = *reinterpret_cast<const float2 *>(p + i), u = *reinterpret_cast<const float2 *>(p + HIDDEN + i);
+    const float *p = part + (size_t)t * GU_ROWS + (i / 64) * 128 + i % 64;
+    float2 g = *reinterpret_cast<const float2 *>(p), u = *reinterpret_cast<const float2 *>(p + 64);
     for (int s = 1; s < splits; s++) {
-        const float2 gs = *reinterpret_cast<const float2 *>(p + s * sstride + i);
-        const float2 us = *reinterpret_cast<const float2 *>(p + s * sstride + HIDDEN + i);
+        const float2 gs = *reinterpret_cast<const float2 *>(p + s * sstride);
+        const float2 us = *reinterpret_cast<const float2 *>(p + s * sstride + 64);
         g.x += gs.x;
         g.y += gs.y;
         u.x += us.x;
@@ -1028,7 +1033,27 @@ int fuse(mocha_q8b *h, Weights &w, std::initializer_list<std::pair<Mat, int>> pa
     return 0;
 }
 
-int plan_set(mocha_q8b *h, PlanSet &ps, int n_max)
+// gate|up device copy for the SwiGLU GEMM epilogue: blocks of 64 gate rows and the
+// matching 64 up rows alternate (fused row 128b + j = gate row 64b + j, fused row
+// 128b + 64 + j = up row 64b + j), scales likewise.
+int fuse_gate_up(mocha_q8b *h, Weights &w, const Mat &gate, const Mat &up, int cols)
+{
+    const size_t rows = 2 * (size_t)HIDDEN, gs = cols / GROUP;
+    if (dalloc(&w.own_q, rows * cols) || dalloc(&w.own_s, rows * gs)) return 1;
+    const Mat *src[2] = {&gate, &up};
+    for (int i = 0; i < 2; i++) {
+        QB_TRY(cudaMemcpy2DAsync(w.own_q + (size_t)i * 64 * cols, 128 * (size_t)cols, src[i]->w, 64 * (size_t)cols,
+                                 64 * (size_t)cols, HIDDEN / 64, cudaMemcpyDeviceToDevice, h->stream));
+        QB_TRY(cudaMemcpy2DAsync(w.own_s + (size_t)i * 64 * gs, 128 * gs * sizeof(float), src[i]->s,
+                                 64 * gs * sizeof(float), 64 * gs * sizeof(float), HIDDEN / 64,
+                                 cudaMemcpyDeviceToDevice, h->stream));
+    }
+    w.q = w.own_q;
+    w.s = w.own_s;
+    return 0;
+}
+
+int plan_set(mocha_q8b *h, PlanSet &ps, int n_max, bool fused_swiglu)
 {
     for (int l = 0; l < LAYERS; l++) {
         if (mb::tq::plan(&ps.qkv[l], h->w_qkv[l].q, h->w_qkv[l].s, QKV_ROWS, DIM, h->lx.q, h->lx.s, n_max, h->part,
@@ -1037,6 +1062,7 @@ int plan_set(mocha_q8b *h, PlanSet &ps, int n_max)
                          h->err) ||
             mb::tq::plan(&ps.gu[l], h->w_gu[l].q, h->w_gu[l].s, GU_ROWS, DIM, h->lx.q, h->lx.s, n_max, h->part,
                          GU_ROWS, 0, h->err) ||
+            (fused_swiglu && mb::tq::set_swiglu(&ps.gu[l], h->lhq, h->lhs, HIDDEN)) ||
             mb::tq::plan(&ps.down[l], h->w_down[l].q, h->w_down[l].s, DIM, HIDDEN, h->lhq, h->lhs, n_max, h->part,
                          DIM, 0, h->err))
             return 1;
@@ -1115,8 +1141,10 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
         if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
         if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr)) return 1;
-        if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;
-        if (pdl(k_swiglu, dim3((HIDDEN + 511) / 512, n), 256, 0, s, h->part, sp.splits, sp.split_stride, h->lhq, h->lhs)) return 1;
+        if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;  // prompt passes: writes the SwiGLU limbs
+        if (decode_set && pdl(k_swiglu, dim3((HIDDEN + 511) / 512, n), 256, 0, s, h->part, sp.splits, sp.split_stride,
+                              h->lhq, h->lhs))
+            return 1;
         if (mb::tq::launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
         if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride,
@@ -1257,7 +1285,7 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
     for (int l = 0; l < LAYERS; l++) {
         const q8::Layer &L = h->m.layer[l];
         if (fuse(h, h->w_qkv[l], {{L.q, DIM}, {L.k, KV}, {L.v, KV}}, DIM) ||
-            fuse(h, h->w_gu[l], {{L.gate, HIDDEN}, {L.up, HIDDEN}}, DIM))
+            fuse_gate_up(h, h->w_gu[l], L.gate, L.up, DIM))
             return fail();
         h->w_o[l].q = L.o.w;
         h->w_o[l].s = L.o.s;
@@ -1310,7 +1338,7 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
         return fail();
 
     // GEMM call sites; the partial buffer is sized from the plans' split counts
-    if (plan_set(h, h->pre, max_rows) || plan_set(h, h->dec, slots)) return fail();
+    if (plan_set(h, h->pre, max_rows, true) || plan_set(h, h->dec, slots, false)) return fail();
     if (mb::tq::plan(&h->head, h->w_head.q, h->w_head.s, VOCAB, DIM, h->lhead.q, h->lhead.s, slots, h->logits, VOCAB,
                      1, h->err))
         return fail();

@@ -23,7 +23,16 @@ constexpr uint32_t kAccCols = kLimbRows;        // one group's int32 sums
 constexpr uint32_t kTmemCols = 512;             // two accumulator buffers (384 used)
 constexpr int kMaxGroups = 76;                  // groups of one split kept in shared memory (K <= 4864)
 constexpr size_t kSxBytes = (size_t)kMaxGroups * kTokens * 4;
-constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256 + kSxBytes;
+constexpr int kShLd = kTokens + 1;              // SwiGLU exchange tile [128 rows][64 tokens], padded
+constexpr size_t kShBytes = (size_t)kBM * kShLd * 4;
+constexpr size_t kSmemBase = 1024 + (size_t)kStages * kStageBytes + 256;
+constexpr size_t kSmem = kSmemBase + kSxBytes + kShBytes;  // the largest launch
+
+// Dynamic shared memory of one launch: the ring, the activation scales of one split's
+// groups and, in SwiGLU mode, the exchange tile.  Sized per launch so that small
+// launches leave room for the CTAs of the neighbouring kernels (programmatic dependent
+// launch starts them on the same SMs).
+size_t smem_bytes(const Params &p) { return kSmemBase + (size_t)2 * p.kstages * kTokens * 4 + (p.hq ? kShBytes : 0); }
 
 // Two IEEE fp32 operations in one instruction (sm_100 paired FP32 lanes):
 // (d0, d1) = (a0 * b0 + c0, a1 * b1 + c1), each rounded to nearest.
@@ -228,6 +237,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q8(const __grid_constant__
                     }
                 }
             }
+            if (p.hq) {
+                // SwiGLU: gate rows are tile rows 0..63, up rows 64..127; the 16 warps
+                // exchange the tile through shared memory (every warp meets the barrier,
+                // also after an abort), then warp e takes tokens 4e..4e+3 with lane l on
+                // features 2l, 2l + 1 (one 64-group of the next GEMM per token)
+                float *sh = sxs + 2 * p.kstages * kTokens;
+                if (ok) {
+#pragma unroll
+                    for (int t = 0; t < kEpiTokens; t++) sh[(q * 32 + lane) * kShLd + part * kEpiTokens + t] = acc[t];
+                }
+                asm volatile("bar.sync 2, %0;" ::"n"(32 * kEpiWarps) : "memory");
+                if (*abort) continue;
+                const int ew = warp - 2;
+#pragma unroll
+                for (int i = 0; i < kTokens / kEpiWarps; i++) {
+                    const int tl = (kTokens / kEpiWarps) * ew + i, tok = nt * kTokens + tl;
+                    if (tok >= p.N) break;
+                    const float g0 = sh[(2 * lane) * kShLd + tl], g1 = sh[(2 * lane + 1) * kShLd + tl];
+                    const float u0 = sh[(64 + 2 * lane) * kShLd + tl], u1 = sh[(65 + 2 * lane) * kShLd + tl];
+                    const float hv[2] = {(g0 / (1.f + expf(-g0))) * u0, (g1 / (1.f + expf(-g1))) * u1};
+                    store_limbs<2, 32>(hv, p.hq + (size_t)tok * 3 * p.hk, p.hk, mt * 64 + 2 * lane,
+                                       p.hs + (size_t)tok * (p.hk / 64) + mt, lane);
+                }
+                continue;
+            }
             if (!ok) continue;
             float *d = p.d + (long long)z * p.split_stride + m;
 #pragma unroll
@@ -315,6 +349,19 @@ int plan(Gemm *g, const int8_t *q, const float *sw, int M, int K, const int8_t *
     return 0;
 }
 
+int set_swiglu(Gemm *g, int8_t *hq, float *hs, int hk)
+{
+    if (!hq || !hs || hk <= 0 || hk % 64 || g->p.M != 2 * hk) {
+        fprintf(stderr, "mocha: int8 gemm swiglu: bad geometry (M=%d hk=%d)\n", g->p.M, hk);
+        return 1;
+    }
+    g->p.hq = hq;
+    g->p.hs = hs;
+    g->p.hk = hk;
+    g->fixed_splits = 1;
+    return 0;
+}
+
 tc::Split split_for(const Gemm &g, int n)
 {
     const int stages = g.p.K / kBK;
@@ -358,7 +405,7 @@ int launch(const Gemm &g, int n, cudaStream_t s, tc::Split *used)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = smem_bytes(p);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -36,6 +36,13 @@ struct Params {
     int M, N, K;          // M % 128 == 0, K % 128 == 0
     int kstages;          // 128-wide K stages per split
     int *err;
+    // SwiGLU mode (hq set): the weight rows are gate and up interleaved in blocks of 64
+    // (tile m holds gate rows 64m..64m+63, then up rows 64m..64m+63), K is not split,
+    // and the epilogue writes h = silu(gate) * up of features 64m..64m+63 as the limbs
+    // hq [3n][hk] and scales hs [n][hk / 64] of the next GEMM's input instead of d.
+    int8_t *hq = nullptr;
+    float *hs = nullptr;
+    int hk = 0;
 };
 
 struct Gemm {
@@ -48,6 +55,9 @@ struct Gemm {
 // sx [n_max][K/64]; output d with row stride ldd.  splits = 0: chosen per launch.
 int plan(Gemm *g, const int8_t *q, const float *sw, int M, int K, const int8_t *limbs, const float *sx, int n_max,
          float *d, long long ldd, int splits, int *err);
+// Switches a planned gate|up GEMM (M = 2 * hk rows, interleaved as in Params) to the
+// SwiGLU epilogue writing limbs hq / scales hs.
+int set_swiglu(Gemm *g, int8_t *hq, float *hs, int hk);
 tc::Split split_for(const Gemm &g, int n);
 size_t partial_floats(const Gemm &g);
 int launch(const Gemm &g, int n, cudaStream_t s, tc::Split *used = nullptr);
