@@ -229,47 +229,111 @@ __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ p
                                out.s + (size_t)t * (DIM / GROUP) + h, threadIdx.x);
 }
 
-// Attention of one row (one query position) for one KV head and the GQA query heads
-// that share it, over keys 0..pos, written as limbs for the O GEMM.  One CTA of 256
-// threads per (KV head, row):
-//   scores  one key per thread: its 64-float key row against the 7 queries in shared
-//           memory, s[h][k] in shared memory (q carries the 0.125);
+// Rows of any shape: the attention of one row (one query position) for one KV head
+// and the GQA query heads that share it, over keys 0..pos, written as limbs for the O
+// GEMM.  One CTA of 256 threads per (KV head, row):
+//   post    (kPost, rows of distinct slots such as decode steps) the head's q (7 x 64),
+//           k and v from the QKV GEMM partials exactly as k_qkv_post computes them
+//           (split sum, bias, split-half RoPE, q * 0.125); k and v go to the cache and
+//           its bf16 shadow, q and the new k / v stay in shared memory.  Without kPost
+//           k_qkv_post has run and q comes from the query buffer;
+//   scores  one key per thread: its 64-float key row against the 7 queries, s[h][k]
+//           in shared memory;
 //   softmax warp h takes head h: max, exp(s - max) in place, sum;
 //   P V     warp w takes keys w, w + 8, ...; lane l accumulates dims 2l, 2l + 1 of all
 //           7 heads (coalesced 256-byte V rows), the 8 warp partials are added in
 //           warp order;
 //   output  warp h divides by the sum and stores head h (one 64-group) as limbs.
-// Decode rows read their whole KV prefix once per KV head (no partial buffer, no
-// combine launch).
+// The cache rows of earlier positions are read through the read-only path; with kPost
+// the row written by this CTA (k == pos) is taken from shared memory.
+constexpr int ATTN_ROWS_POST = 3;  // attention kind: rows of distinct slots, QKV post fused
 constexpr int AR_THREADS = 256;
 constexpr int AR_WARPS = AR_THREADS / 32;
+static_assert(GQA * 32 + 32 == AR_THREADS, "one thread per q RoPE pair plus one warp of k pairs");
 
-__global__ void __launch_bounds__(AR_THREADS) k_attn_row(const float *__restrict__ q, Rows rows,
-                                                         const float *__restrict__ kc, const float *__restrict__ vc,
-                                                         int layer, Limbs out)
+struct QkvPost {
+    const float *part;  // QKV GEMM partials [splits][rows][QKV_ROWS]
+    int splits;
+    long long sstride;
+    const float *bias, *rope_cos, *rope_sin;
+    KvShadow sh;
+};
+
+template <bool kPost>
+__global__ void __launch_bounds__(AR_THREADS) k_attn_row(const QkvPost pp, const float *__restrict__ q, Rows rows,
+                                                         float *__restrict__ kc, float *__restrict__ vc, int layer,
+                                                         Limbs out)
 {
     pdl_enter();
     const int g = blockIdx.x, t = blockIdx.y;
     const int pos = rows.pos[t], slot = rows.slot[t];
     const int nk = min(pos, CONTEXT - 1) + 1;
     __shared__ __align__(16) float sq[GQA][HEAD_DIM];
+    __shared__ __align__(16) float snk[HEAD_DIM];
+    __shared__ float snv[HEAD_DIM];
     __shared__ float ss[GQA][CONTEXT];
     __shared__ __align__(16) float sred[AR_WARPS][GQA * HEAD_DIM];
     __shared__ float sl[GQA];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < GQA * HEAD_DIM; i += AR_THREADS)
-        sq[i / HEAD_DIM][i % HEAD_DIM] = q[(size_t)t * DIM + g * GQA * HEAD_DIM + i];
+    if (!kPost) {
+        for (int i = tid; i < GQA * HEAD_DIM; i += AR_THREADS)
+            sq[i / HEAD_DIM][i % HEAD_DIM] = q[(size_t)t * DIM + g * GQA * HEAD_DIM + i];
+    } else {
+        const float *p = pp.part + (size_t)t * QKV_ROWS;
+        auto sum2 = [&](int r0, float &d0, float &d1) {
+            d0 = p[r0];
+            d1 = p[r0 + 32];
+            for (int s = 1; s < pp.splits; s++) {
+                d0 += p[s * pp.sstride + r0];
+                d1 += p[s * pp.sstride + r0 + 32];
+            }
+            d0 += __ldg(pp.bias + r0);
+            d1 += __ldg(pp.bias + r0 + 32);
+        };
+        float d0, d1;
+        const int i = lane;
+        const int r0 = warp < GQA ? (g * GQA + warp) * HEAD_DIM + i : DIM + g * HEAD_DIM + i;
+        sum2(r0, d0, d1);
+        const float cs = __ldg(pp.rope_cos + pos * 32 + i), sn = __ldg(pp.rope_sin + pos * 32 + i);
+        const float a = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
+        const float b = __fadd_rn(__fmul_rn(d1, cs), __fmul_rn(d0, sn));
+        if (warp < GQA) {
+            sq[warp][i] = a * 0.125f;
+            sq[warp][i + 32] = b * 0.125f;
+        } else {
+            const size_t o = kv_off(slot, layer, g, pos);
+            kc[o + i] = a;
+            kc[o + i + 32] = b;
+            mb::tc::split_bf16(a, pp.sh.k_hi[o + i], pp.sh.k_lo[o + i]);
+            mb::tc::split_bf16(b, pp.sh.k_hi[o + i + 32], pp.sh.k_lo[o + i + 32]);
+            snk[i] = a;
+            snk[i + 32] = b;
+        }
+        if (warp == 0) {
+            sum2(DIM + KV + g * HEAD_DIM + i, d0, d1);
+            float *v = vc + kv_off(slot, layer, g, pos);
+            v[i] = d0;
+            v[i + 32] = d1;
+            mb::tc::split_bf16(d0, pp.sh.vt_hi[vt_off(slot, layer, g, i, pos)], pp.sh.vt_lo[vt_off(slot, layer, g, i, pos)]);
+            mb::tc::split_bf16(d1, pp.sh.vt_hi[vt_off(slot, layer, g, i + 32, pos)],
+                               pp.sh.vt_lo[vt_off(slot, layer, g, i + 32, pos)]);
+            snv[i] = d0;
+            snv[i + 32] = d1;
+        }
+    }
     __syncthreads();
     const float *kb = kc + kv_off(slot, layer, g, 0);
     const float *vb = vc + kv_off(slot, layer, g, 0);
     for (int k = tid; k < nk; k += AR_THREADS) {
-        const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)k * HEAD_DIM);
+        const bool own = kPost && k == pos;
+        const float4 *kr = own ? reinterpret_cast<const float4 *>(snk)
+                               : reinterpret_cast<const float4 *>(kb + (size_t)k * HEAD_DIM);
         float z[GQA];
 #pragma unroll
         for (int h = 0; h < GQA; h++) z[h] = 0.f;
 #pragma unroll
         for (int j = 0; j < HEAD_DIM / 4; j++) {
-            const float4 kv = __ldg(kr + j);
+            const float4 kv = own ? kr[j] : __ldg(kr + j);
 #pragma unroll
             for (int h = 0; h < GQA; h++) {
                 const float4 qv = *reinterpret_cast<const float4 *>(&sq[h][4 * j]);
@@ -302,7 +366,8 @@ __global__ void __launch_bounds__(AR_THREADS) k_attn_row(const float *__restrict
     for (int h = 0; h < GQA; h++) a[h][0] = a[h][1] = 0.f;
 #pragma unroll 4
     for (int k = warp; k < nk; k += AR_WARPS) {
-        const float2 v = __ldg(reinterpret_cast<const float2 *>(vb + (size_t)k * HEAD_DIM) + lane);
+        const float2 v = kPost && k == pos ? make_float2(snv[2 * lane], snv[2 * lane + 1])
+                                  : __ldg(reinterpret_cast<const float2 *>(vb + (size_t)k * HEAD_DIM) + lane);
 #pragma unroll
         for (int h = 0; h < GQA; h++) {
             const float p = ss[h][k];
@@ -1080,9 +1145,9 @@ size_t plan_floats(const PlanSet &ps)
     return m;
 }
 
-// Attention for rows [0, n): the query-block kernel when every 64-row block is one
-// slot at consecutive positions starting at a multiple of 64 (prompt passes whose
-// per-slot length is a multiple of 64), else the per-row chunk kernels.
+// Attention for rows [0, n) after k_qkv_post: block 2, the tensor-core kernel over
+// 128-row blocks of one slot at consecutive positions from a multiple of 128; block 1,
+// the CUDA-core kernel over such 64-row blocks; block 0, one CTA per (KV head, row).
 int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
 {
     static bool attr_done[64] = {}, tc_done[64] = {};
@@ -1104,14 +1169,24 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
         if (pdl(k_attn_block, dim3(n / QB, HEADS), 256, QB_SMEM, h->stream, h->q, rows, h->kc, h->vc, layer, h->la)) return 1;
         return 0;
     }
-    return pdl(k_attn_row, dim3(KV_HEADS, n), AR_THREADS, 0, h->stream, h->q, rows, h->kc, h->vc, layer, h->la);
+    return pdl(k_attn_row<false>, dim3(KV_HEADS, n), AR_THREADS, 0, h->stream, QkvPost{}, h->q, rows, h->kc, h->vc,
+               layer, h->la);
 }
 
 // Attention kernel for rows (host arrays): 2 when every block of 128 rows is one slot
 // at consecutive positions from a multiple of 128 (tensor cores), 1 for blocks of 64
-// (CUDA cores), 0 for per-row chunks.
+// (CUDA cores), else one CTA per (KV head, row): ATTN_ROWS_POST (QKV post-processing
+// in the same kernel) when no slot has two rows, 0 otherwise.
 int block_kind(int n, const int *pos, const int *slots)
 {
+    auto distinct = [&]() {
+        std::vector<char> seen(1024, 0);
+        for (int i = 0; i < n; i++) {
+            if (slots[i] < 0 || slots[i] >= (int)seen.size() || seen[slots[i]]) return false;
+            seen[slots[i]] = 1;
+        }
+        return true;
+    };
     auto blocks_of = [&](int b) {
         if (n % b) return false;
         for (int r = 0; r < n; r += b) {
@@ -1121,7 +1196,7 @@ int block_kind(int n, const int *pos, const int *slots)
         }
         return true;
     };
-    return blocks_of(TQ) ? 2 : (blocks_of(QB) ? 1 : 0);
+    return blocks_of(TQ) ? 2 : (blocks_of(QB) ? 1 : (distinct() ? ATTN_ROWS_POST : 0));
 }
 
 // The whole transformer for rows [0, n) plus the head for `np` projected rows
@@ -1136,9 +1211,19 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
     for (int l = 0; l < LAYERS; l++) {
         const Layer &L = h->m.layer[l];
         if (mb::tq::launch(ps.qkv[l], n, s, &sp)) return 1;
-        if (pdl(k_qkv_post, n, QKV_THREADS, 0, s, h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, rows,
-                                              h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l, h->kvs)) return 1;
-        if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
+        if (block_attention == ATTN_ROWS_POST) {
+            // rows of distinct slots: QKV post-processing fused into the row attention
+            const QkvPost pp{h->part, sp.splits, sp.split_stride, h->bqkv + (size_t)l * QKV_ROWS, h->rope_cos,
+                             h->rope_sin, h->kvs};
+            if (pdl(k_attn_row<true>, dim3(KV_HEADS, n), AR_THREADS, 0, s, pp, (const float *)nullptr, rows, h->kc,
+                    h->vc, l, h->la))
+                return 1;
+        } else {
+            if (pdl(k_qkv_post, n, QKV_THREADS, 0, s, h->part, sp.splits, sp.split_stride,
+                    h->bqkv + (size_t)l * QKV_ROWS, rows, h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l, h->kvs))
+                return 1;
+            if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
+        }
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
         if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr)) return 1;
         if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;  // prompt passes: writes the SwiGLU limbs
@@ -1207,7 +1292,7 @@ int capture_step(mocha_q8b *h, int n)
     cudaGraph_t g;
     QB_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     const Rows r{h->ntok, h->npos, h->nslot};
-    int rc = enqueue_forward(h, r, n, true, h->ident, n, 0);
+    int rc = enqueue_forward(h, r, n, true, h->ident, n, ATTN_ROWS_POST);  // one row per slot
     if (!rc) rc = enqueue_sample(h, r, n, h->ident);
     const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
     if (rc || e != cudaSuccess) {
@@ -1525,7 +1610,7 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
 extern "C" int mocha_q8b_launches_per_step(mocha_q8b *h)
 {
     if (!h) return -1;
-    return 1 + LAYERS * 9 + 1 + 2;  // embed+norm, 9 per layer, head GEMM, two sampler kernels
+    return 1 + LAYERS * 8 + 1 + 2;  // embed+norm, 8 per layer, head GEMM, two sampler kernels
 }
 
 // Sampler check: the batched sampler on caller-supplied logits (n rows of VOCAB) with
