@@ -90,6 +90,41 @@ __host__ __device__ __forceinline__ size_t vt_off(int slot, int layer, int kvh, 
 
 // ---- row kernels ----------------------------------------------------------------------
 
+// Sum over K splits of a GEMM's partials, p[0] + p[stride] + p[2 stride] + ... in split
+// order; the loads are issued several splits at a time so their latencies overlap.
+MB_DEV float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+
+template <int B>
+MB_DEV float4 sum_splits4(const float *p, int splits, long long stride)
+{
+    float4 acc = *reinterpret_cast<const float4 *>(p);
+    for (int s = 1; s < splits; s += B) {
+        float4 v[B];
+#pragma unroll
+        for (int j = 0; j < B; j++)
+            if (s + j < splits) v[j] = *reinterpret_cast<const float4 *>(p + (s + j) * stride);
+#pragma unroll
+        for (int j = 0; j < B; j++)
+            if (s + j < splits) acc = f4add(acc, v[j]);
+    }
+    return acc;
+}
+
+MB_DEV float sum_splits1(const float *p, int splits, long long stride)
+{
+    float acc = *p;
+    for (int s = 1; s < splits; s += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (s + j < splits) v[j] = p[(s + j) * stride];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (s + j < splits) acc += v[j];
+    }
+    return acc;
+}
+
 // Limbs of a DIM-wide GEMM input: int8 [rows * 3][DIM] and group scales [rows][DIM/64].
 struct Limbs {
     int8_t *q;
@@ -127,6 +162,9 @@ __global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const f
 }
 
 // x[t] += sum_s part[s][t]; then the norm of the new x into row dst_row[t] (or t).
+// B: partial loads in flight per thread (8 for the many-split decode GEMMs; 1 keeps
+// the register count, and the occupancy of the prompt passes' thousands of rows, low).
+template <int B>
 __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__restrict__ part, int splits,
                                                       long long sstride, const float *__restrict__ gain, Limbs out,
                                                       const int *__restrict__ dst_row)
@@ -134,14 +172,7 @@ __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__r
     pdl_enter();
     __shared__ float red[32];
     const int t = blockIdx.x, i0 = threadIdx.x * 4;
-    float4 acc = *reinterpret_cast<const float4 *>(part + (size_t)t * DIM + i0);
-    for (int s = 1; s < splits; s++) {
-        const float4 p = *reinterpret_cast<const float4 *>(part + s * sstride + (size_t)t * DIM + i0);
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
-    }
+    const float4 acc = sum_splits4<B>(part + (size_t)t * DIM + i0, splits, sstride);
     float4 *xp = reinterpret_cast<float4 *>(x + (size_t)t * DIM + i0);
     const float4 xv = *xp;
     const float v[4] = {xv.x + acc.x, xv.y + acc.y, xv.z + acc.z, xv.w + acc.w};
@@ -281,14 +312,8 @@ __global__ void __launch_bounds__(AR_THREADS) k_attn_row(const QkvPost pp, const
     } else {
         const float *p = pp.part + (size_t)t * QKV_ROWS;
         auto sum2 = [&](int r0, float &d0, float &d1) {
-            d0 = p[r0];
-            d1 = p[r0 + 32];
-            for (int s = 1; s < pp.splits; s++) {
-                d0 += p[s * pp.sstride + r0];
-                d1 += p[s * pp.sstride + r0 + 32];
-            }
-            d0 += __ldg(pp.bias + r0);
-            d1 += __ldg(pp.bias + r0 + 32);
+            d0 = sum_splits1(p + r0, pp.splits, pp.sstride) + __ldg(pp.bias + r0);
+            d1 = sum_splits1(p + r0 + 32, pp.splits, pp.sstride) + __ldg(pp.bias + r0 + 32);
         };
         float d0, d1;
         const int i = lane;
@@ -1225,16 +1250,19 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
             if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
         }
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
-        if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride, L.ffn_norm, h->lx, nullptr)) return 1;
+        if (pdl(sp.splits > 2 ? k_residual_norm<8> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
+                sp.split_stride, L.ffn_norm, h->lx, nullptr))
+            return 1;
         if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;  // prompt passes: writes the SwiGLU limbs
         if (decode_set && pdl(k_swiglu, dim3((HIDDEN + 511) / 512, n), 256, 0, s, h->part, sp.splits, sp.split_stride,
                               h->lhq, h->lhs))
             return 1;
         if (mb::tq::launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
-        if (pdl(k_residual_norm, n, NT, 0, s, h->x, h->part, sp.splits, sp.split_stride,
-                                          last ? h->m.final_norm : h->m.layer[l + 1].attn_norm,
-                                          last ? h->lhead : h->lx, last ? proj_dst : nullptr)) return 1;
+        if (pdl(sp.splits > 2 ? k_residual_norm<8> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
+                sp.split_stride, last ? h->m.final_norm : h->m.layer[l + 1].attn_norm, last ? h->lhead : h->lx,
+                last ? proj_dst : nullptr))
+            return 1;
     }
     if (np > 0 && mb::tq::launch(h->head, np, s)) return 1;
     QB_TRY(cudaGetLastError());
