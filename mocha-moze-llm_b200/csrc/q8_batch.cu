@@ -954,9 +954,11 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
     if (threadIdx.x < 32) {
         for (int j = threadIdx.x; j < count; j += 32) {
             const int id = hist[j];
+            // ids outside this slice (most of the window) skip the duplicate scan
+            if (id < lo || id >= lo + n || (id >= p.control_first && id != p.eos)) continue;
             bool dup = false;
             for (int u = 0; u < j; u++) dup |= hist[u] == id;
-            if (!dup && id >= lo && id < lo + n && !(id >= p.control_first && id != p.eos)) {
+            if (!dup) {
                 const float v = lg[id - lo];
                 keys[id - lo] = mb::rank_key(v < 0 ? v * p.penalty : v / p.penalty, id);
             }

@@ -1272,9 +1272,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const int count = min(max(a.seq->history_count, 0), sampling::kHistory);
                 for (int j = c.lane; j < count; j += 32) {
                     const int id = a.seq->history[j];
+                    if (id < lo || id >= lo + n) continue;  // not in this slice: no duplicate scan
                     bool dup = false;
                     for (int t = 0; t < j; t++) dup |= a.seq->history[t] == id;
-                    if (!dup && id >= lo && id < lo + n) {
+                    if (!dup) {
                         const float v = S.u.hl[id - lo];
                         S.u.hl[id - lo] = v < 0 ? v * prm.penalty : v / prm.penalty;
                     }

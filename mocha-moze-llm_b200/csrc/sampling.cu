@@ -83,9 +83,10 @@ __global__ void __launch_bounds__(kThreads)
     if (threadIdx.x < 32) {
         for (int j = threadIdx.x; j < count; j += 32) {
             const int id = hist[j];
+            if (id < lo || id >= lo + n) continue;  // not in this slice: no duplicate scan
             bool dup = false;
             for (int t = 0; t < j; t++) dup |= hist[t] == id;
-            if (!dup && id >= lo && id < lo + n) {
+            if (!dup) {
                 const float v = vals[id - lo];
                 vals[id - lo] = v < 0 ? v * penalty : v / penalty;
             }
