@@ -53,7 +53,7 @@ constexpr int NCHUNK = CONTEXT / CHUNK;
 constexpr int PART = 2 + HEAD_DIM;      // chunk max, chunk sum, 64 weighted-V sums
 constexpr int NT = DIM / 4;             // row kernels: 4 features per thread
 constexpr int QKV_THREADS = (DIM + 2 * KV) / 2;  // one thread per RoPE pair / V pair
-constexpr int SLICE = 4096;             // sampler stage 1: ids per CTA
+constexpr int SLICE = 8192;             // sampler stage 1: ids per CTA (keys in dynamic shared memory)
 constexpr int NSLICE = (VOCAB + SLICE - 1) / SLICE;
 constexpr int SAMPLE_THREADS = 1024;
 
@@ -929,7 +929,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
                                                               unsigned long long *__restrict__ out)
 {
     pdl_enter();
-    __shared__ unsigned long long keys[SLICE];
+    extern __shared__ unsigned long long keys[];  // [SLICE]
     __shared__ int hist[sampling::kHistory];
     const int r = blockIdx.y, lo = blockIdx.x * SLICE;
     const int n = min(VOCAB - lo, SLICE);
@@ -981,7 +981,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned lon
                                                               int *out_tokens, int *out_count, int out_stride)
 {
     pdl_enter();
-    constexpr int kMerge = 4096;  // >= NSLICE * kMaxK = 2432
+    constexpr int kMerge = 2048;  // >= NSLICE * kMaxK = 1216
+    static_assert(kMerge >= NSLICE * sampling::kMaxK && kMerge % SAMPLE_THREADS == 0, "merge buffer");
     __shared__ unsigned long long keys[kMerge];
     const int r = blockIdx.x;
     const sampling::Params p = *prm;
@@ -1275,8 +1276,15 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
 // projected row r (the identity map in decode steps).
 int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src)
 {
-    if (pdl(k_bs_stage1, dim3(NSLICE, np), SAMPLE_THREADS, 0, h->stream, h->logits, proj_src, rows, h->slots, h->st,
-                                                                   h->params, h->keys)) return 1;
+    static bool attr_done[64] = {};
+    if (!attr_done[h->device & 63]) {
+        QB_TRY(cudaFuncSetAttribute(k_bs_stage1, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)(SLICE * sizeof(unsigned long long))));
+        attr_done[h->device & 63] = true;
+    }
+    if (pdl(k_bs_stage1, dim3(NSLICE, np), SAMPLE_THREADS, SLICE * sizeof(unsigned long long), h->stream, h->logits,
+            proj_src, rows, h->slots, h->st, h->params, h->keys))
+        return 1;
     if (pdl(k_bs_stage2, np, SAMPLE_THREADS, 0, h->stream, h->keys, proj_src, rows, h->slots, h->st, h->params, h->ntok,
                                                       h->npos, h->nslot, h->out_tokens, h->out_count, h->out_stride)) return 1;
     QB_TRY(cudaGetLastError());
