@@ -289,7 +289,8 @@ def prefill_object(gathered, args, world):
             "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": achieved_tf / tf_peak, "peak_kind": tf_kind,
                          "algorithmic_flop_per_prompt": PREFILL_FLOP,
-                         "note": "bf16 hi/lo split: the tensor pipe issues 3x the layer-GEMM FLOPs"}}
+                         "note": "int8 tcgen05 GEMMs against three int8 limbs of each activation: the "
+                                 "tensor pipe issues 3x the algorithmic MACs (at the int8 rate, twice bf16's)"}}
 
 
 def batched_object(gathered, args, world):
@@ -311,8 +312,8 @@ def batched_object(gathered, args, world):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_kind": hbm_kind,
                          "algorithmic_bytes_per_step": step_bytes,
-                         "note": "weights counted in the reference format (int8 + fp32 scales); this path "
-                                 "streams bf16 hi/lo copies, 4 B per weight"},
+                         "note": "weights counted in the reference format (int8 + fp32 scales), read as "
+                                 "stored (q|k|v and gate|up from row-fused int8 copies)"},
             "gpu_launches_per_step": gathered[0]["launches"]}
 
 
