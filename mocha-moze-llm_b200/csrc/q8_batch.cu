@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ p
 {
     pdl_enter();
     const int h = blockIdx.x, t = blockIdx.y, d = 2 * threadIdx.x;
+    if (rows.pos[t] < per) return;  // one span: k_attn_tc wrote the row's limbs
     const int nc = rows.pos[t] / per + 1;  // partials of `per` keys each
     const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
     float m = -INFINITY;
@@ -487,7 +488,7 @@ MB_DEV void put8(uint8_t *tile, int r, int c0, const float (&v)[8], uint8_t *til
 
 __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, Rows rows,
                                                   const __grid_constant__ AttnMaps maps, int layer,
-                                                  float *__restrict__ part, int *err)
+                                                  float *__restrict__ part, Limbs out, int *err)
 {
     pdl_enter();
     const int h = blockIdx.y, g = h / GQA, t0 = blockIdx.x * TQ, z = blockIdx.z;
@@ -650,13 +651,21 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         mb::as::mbar_wait(&bar[4], 0, &never);
         for (int k = landed_n; k < issued; k++) mb::as::mbar_wait(&bar[k & 1], (k >> 1) & 1, &never);
     }
-    if (ok) {
-        float *out = part + (((size_t)(t0 + row) * HEADS + h) * NCHUNK + z) * PART;
-        // a partial is PART = 66 floats: its payload is 8-byte aligned, so float2 stores
-        out[0] = m;
-        out[1] = l;
+    if (ok && p0 + TQ <= TSPAN) {
+        // the block's keys lie in this one span: the row is finished here, as the span
+        // combine would finish it from one partial (weight exp(0) = 1), and written as
+        // limbs of the O GEMM (this thread holds the head's whole 64-group)
 #pragma unroll
-        for (int d = 0; d < HEAD_DIM; d += 2) *reinterpret_cast<float2 *>(out + 2 + d) = make_float2(o[d], o[d + 1]);
+        for (int d = 0; d < HEAD_DIM; d++) o[d] = o[d] / l;
+        mb::tq::store_limbs<HEAD_DIM, 1>(o, out.q + (size_t)(t0 + row) * 3 * DIM, DIM, h * HEAD_DIM,
+                                         out.s + (size_t)(t0 + row) * (DIM / GROUP) + h, 0);
+    } else if (ok) {
+        float *pt = part + (((size_t)(t0 + row) * HEADS + h) * NCHUNK + z) * PART;
+        // a partial is PART = 66 floats: its payload is 8-byte aligned, so float2 stores
+        pt[0] = m;
+        pt[1] = l;
+#pragma unroll
+        for (int d = 0; d < HEAD_DIM; d += 2) *reinterpret_cast<float2 *>(pt + 2 + d) = make_float2(o[d], o[d + 1]);
     }
     mb::as::tc_fence_before();
     __syncthreads();
@@ -1176,7 +1185,7 @@ size_t plan_floats(const PlanSet &ps)
 // Attention for rows [0, n) after k_qkv_post: block 2, the tensor-core kernel over
 // 128-row blocks of one slot at consecutive positions from a multiple of 128; block 1,
 // the CUDA-core kernel over such 64-row blocks; block 0, one CTA per (KV head, row).
-int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
+int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block, int max_pos)
 {
     static bool attr_done[64] = {}, tc_done[64] = {};
     if (block == 2) {
@@ -1185,8 +1194,10 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block)
             tc_done[h->device & 63] = true;
         }
         if (pdl(k_attn_tc, dim3(n / TQ, HEADS, TSPLIT), TQ, TC_SMEM, h->stream, h->q, rows, h->amaps, layer, h->apart,
-                h->err))
+                h->la, h->err))
             return 1;
+        // rows at positions < TSPAN were finished by k_attn_tc (their block needs one span)
+        if (max_pos < TSPAN) return 0;
         return pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la, TSPAN);
     }
     if (block) {
@@ -1230,7 +1241,7 @@ int block_kind(int n, const int *pos, const int *slots)
 // The whole transformer for rows [0, n) plus the head for `np` projected rows
 // (proj_dst maps row -> head row or -1; the head reads rows 0..np-1 of the head limbs).
 int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *proj_dst, int np,
-                    int block_attention)
+                    int block_attention, int max_pos)
 {
     const PlanSet &ps = decode_set ? h->dec : h->pre;
     cudaStream_t s = h->stream;
@@ -1250,7 +1261,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
             if (pdl(k_qkv_post, n, QKV_THREADS, 0, s, h->part, sp.splits, sp.split_stride,
                     h->bqkv + (size_t)l * QKV_ROWS, rows, h->rope_cos, h->rope_sin, h->q, h->kc, h->vc, l, h->kvs))
                 return 1;
-            if (enqueue_attention(h, rows, n, l, block_attention)) return 1;
+            if (enqueue_attention(h, rows, n, l, block_attention, max_pos)) return 1;
         }
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
         if (pdl(sp.splits > 2 ? k_residual_norm<8> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
@@ -1330,7 +1341,7 @@ int capture_step(mocha_q8b *h, int n)
     cudaGraph_t g;
     QB_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
     const Rows r{h->ntok, h->npos, h->nslot};
-    int rc = enqueue_forward(h, r, n, true, h->ident, n, ATTN_ROWS_POST);  // one row per slot
+    int rc = enqueue_forward(h, r, n, true, h->ident, n, ATTN_ROWS_POST, CONTEXT - 1);  // one row per slot
     if (!rc) rc = enqueue_sample(h, r, n, h->ident);
     const cudaError_t e = cudaStreamEndCapture(h->stream, &g);
     if (rc || e != cudaSuccess) {
@@ -1522,7 +1533,9 @@ extern "C" int mocha_q8b_forward(mocha_q8b *h, int n, const int *tokens, const i
     QB_TRY(cudaSetDevice(h->device));
     if (upload_rows(h, n, tokens, pos, slots) || set_projection(h, n, n_project, project_rows)) return 1;
     const Rows r{h->tok, h->pos, h->slot};
-    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project, block_kind(n, pos, slots))) return 1;
+    int max_pos = 0;
+    for (int i = 0; i < n; i++) max_pos = std::max(max_pos, pos[i]);
+    if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, n_project, block_kind(n, pos, slots), max_pos)) return 1;
     if (logits && n_project)
         QB_TRY(cudaMemcpyAsync(logits, h->logits, sizeof(float) * VOCAB * n_project, cudaMemcpyDeviceToHost,
                                h->stream));
@@ -1609,7 +1622,7 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
         QB_TRY(cudaEventRecord(h->ev[0], h->stream));
         const Rows pr{h->tok, h->pos, h->slot};
         if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b,
-                            prompt_len % TQ == 0 ? 2 : (prompt_len % QB == 0 ? 1 : 0)) ||
+                            prompt_len % TQ == 0 ? 2 : (prompt_len % QB == 0 ? 1 : 0), prompt_len - 1) ||
             enqueue_sample(h, pr, b, h->proj_src))
             return 1;
         QB_TRY(cudaEventRecord(h->ev[1], h->stream));
@@ -1716,10 +1729,10 @@ extern "C" int mocha_q8b_bench_prefill(mocha_q8b *h, int n, unsigned seed, int w
     const Rows r{h->tok, h->pos, h->slot};
     const int block = n % TQ == 0 ? 2 : (n % QB == 0 ? 1 : 0);
     for (int i = 0; i < warmup; i++)
-        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block)) return 1;
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block, n - 1)) return 1;
     QB_TRY(cudaEventRecord(h->ev[0], h->stream));
     for (int i = 0; i < steps; i++)
-        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block)) return 1;
+        if (enqueue_forward(h, r, n, n <= h->slots, h->proj_dst, 1, block, n - 1)) return 1;
     QB_TRY(cudaEventRecord(h->ev[1], h->stream));
     QB_TRY(cudaEventSynchronize(h->ev[1]));
     QB_TRY(cudaEventElapsedTime(ms, h->ev[0], h->ev[1]));

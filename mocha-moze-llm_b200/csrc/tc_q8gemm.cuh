@@ -94,6 +94,17 @@ __device__ __forceinline__ void store_limbs(const float (&v)[E], int8_t *limb0, 
             *reinterpret_cast<char4 *>(dst) = make_char4(a[l][0], a[l][1], a[l][2], a[l][3]);
         } else if constexpr (E == 2) {
             *reinterpret_cast<char2 *>(dst) = make_char2(a[l][0], a[l][1]);
+        } else if constexpr (E % 16 == 0) {  // dst 16-byte aligned
+#pragma unroll
+            for (int c = 0; c < E / 16; c++) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    w[i] = (uint32_t)(uint8_t)a[l][16 * c + 4 * i] | ((uint32_t)(uint8_t)a[l][16 * c + 4 * i + 1] << 8) |
+                           ((uint32_t)(uint8_t)a[l][16 * c + 4 * i + 2] << 16) |
+                           ((uint32_t)(uint8_t)a[l][16 * c + 4 * i + 3] << 24);
+                *reinterpret_cast<uint4 *>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
         } else {
 #pragma unroll
             for (int e = 0; e < E; e++) dst[e] = a[l][e];
