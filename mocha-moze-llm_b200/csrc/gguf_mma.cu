@@ -411,6 +411,25 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
             }
         }
     }
+    // the warp's first batch of weights, loaded before the wait: weights do not depend on
+    // the kernel ahead, so their latency overlaps the input staging below
+    const int nt = t_end - t_begin, bpt = steps / kBatch, nbatch = nt * bpt;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b0 = nbatch * warp / kWarps, b1 = nbatch * (warp + 1) / kWarps;
+    auto job = [&](int tile_local) {
+        const int tt = t_begin + tile_local;
+        const int mi = tt < g.tile_end[0] ? 0 : (tt < g.tile_end[1] ? 1 : 2);
+        Job j;
+        j.body = g.m[mi].body;
+        j.type = g.m[mi].type;
+        j.tile = tt - (mi ? g.tile_end[mi - 1] : 0);
+        j.steps = steps;
+        return j;
+    };
+    int tl = b0 / bpt, s0 = (b0 - tl * bpt) * kBatch;
+    Job jb = job(tl);
+    Batch buf[2];
+    if (b0 < b1) load_batch(jb, s0, lane, buf[0]);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     extern __shared__ __align__(16) uint8_t smem[];
     const Lay L = layout(g.cols, g.max_tiles);
@@ -421,7 +440,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     int *sa = reinterpret_cast<int *>(smem + L.sa);
     float(*gp)[kWarps + 1] = reinterpret_cast<float(*)[kWarps + 1]>(smem + L.gp);
     __shared__ float red[kWarps];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // input (and its RMSNorm: y = x * (1/sqrt(sum/cols + eps)) * gain)
     float ss = 0.f;
@@ -510,24 +528,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
 
     // batches (tile, 4 steps) of this CTA, split evenly over the warps; a warp walks its
     // range tile by tile, loading the next batch before computing the current one
-    const int nt = t_end - t_begin, bpt = steps / kBatch, nbatch = nt * bpt;
-    const int b0 = nbatch * warp / kWarps, b1 = nbatch * (warp + 1) / kWarps;
     const int g8 = lane >> 2, tg = lane & 3;
     if (b0 < b1) {
-        int tl = b0 / bpt, s0 = (b0 - tl * bpt) * kBatch;
-        auto job = [&](int tile_local) {
-            const int tt = t_begin + tile_local;
-            const int mi = tt < g.tile_end[0] ? 0 : (tt < g.tile_end[1] ? 1 : 2);
-            Job j;
-            j.body = g.m[mi].body;
-            j.type = g.m[mi].type;
-            j.tile = tt - (mi ? g.tile_end[mi - 1] : 0);
-            j.steps = steps;
-            return j;
-        };
-        Job jb = job(tl);
-        Batch buf[2];
-        load_batch(jb, s0, lane, buf[0]);
         float acc0 = 0.f, acc1 = 0.f;
         // step: compute batch bi from buf[cur] after starting batch bi + 1 into buf[cur ^ 1]
         auto step = [&](int bi, Batch &cur, Batch &nxt) {
