@@ -203,12 +203,12 @@ __global__ void k_repack_q80_mma(const uint8_t *__restrict__ raw, int tiles, int
 
 // ---- the GEMV ----------------------------------------------------------------------------
 
-// Shared memory of one CTA (cols = K): the staged input xs[K], B fragments bf[K/32][32],
+// Shared memory of one CTA (cols = K): B fragments bf[K/32][32],
 // per 32-column step the scale / 254 (sx) and the sum of x (x32), per 16-column group
 // the limb sums (sa), and the per-warp row sums gp.
 struct Lay {
     int cols, steps;
-    size_t xs, bf, sx, x32, sa, gp, bytes;
+    size_t bf, sx, x32, sa, gp, bytes;
 };
 
 __host__ __device__ inline Lay layout(int cols, int max_tiles)
@@ -216,8 +216,7 @@ __host__ __device__ inline Lay layout(int cols, int max_tiles)
     Lay L;
     L.cols = cols;
     L.steps = cols / 32;
-    L.xs = 0;
-    L.bf = L.xs + (size_t)cols * 4;
+    L.bf = 0;
     L.sx = L.bf + (size_t)L.steps * 32 * 8;
     L.x32 = L.sx + (size_t)L.steps * 4;
     L.sa = L.x32 + (size_t)L.steps * 4;
@@ -433,7 +432,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     extern __shared__ __align__(16) uint8_t smem[];
     const Lay L = layout(g.cols, g.max_tiles);
-    float *xs = reinterpret_cast<float *>(smem + L.xs);
     uint2 *bf = reinterpret_cast<uint2 *>(smem + L.bf);
     float *sx = reinterpret_cast<float *>(smem + L.sx);
     float *x32 = reinterpret_cast<float *>(smem + L.x32);
@@ -441,37 +439,46 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     float(*gp)[kWarps + 1] = reinterpret_cast<float(*)[kWarps + 1]>(smem + L.gp);
     __shared__ float red[kWarps];
 
-    // input (and its RMSNorm: y = x * (1/sqrt(sum/cols + eps)) * gain)
-    float ss = 0.f;
-    for (int i = threadIdx.x * 4; i < g.cols; i += kThreads * 4) {
-        float4 v = *reinterpret_cast<const float4 *>(g.x + i);
-        if (g.up) {  // h = silu(gate) * up, as the reference's FFN
-            const float4 u = *reinterpret_cast<const float4 *>(g.up + i);
-            v = make_float4((v.x / (1.0f + expf(-v.x))) * u.x, (v.y / (1.0f + expf(-v.y))) * u.y,
-                            (v.z / (1.0f + expf(-v.z))) * u.z, (v.w / (1.0f + expf(-v.w))) * u.w);
-        }
-        *reinterpret_cast<float4 *>(xs + i) = v;
-        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-    }
+    // input limbs: thread th = (s, t, h) owns columns 32 s + 16 h + 4 t + {0..3} = B-fragment
+    // register h of lanes 4 n + t (limb n); the 8 threads of a step are an aligned 8-lane
+    // block.  The values come straight from global memory: silu(x) * up for the FFN down
+    // GEMV, x * (1/sqrt(sum x^2 / cols + eps)) * gain for a normed input (the sum of squares
+    // by a block reduction first), else x.
+    auto col_of = [&](int th) {
+        return 32 * (th >> 3) + 16 * (th & 1) + 4 * ((th >> 1) & 3);
+    };
+    float sc = 1.f;
     if (g.gain) {
+        float ss = 0.f;
+        for (int th = threadIdx.x; th < steps * 8; th += kThreads) {
+            const float4 v = *reinterpret_cast<const float4 *>(g.x + col_of(th));
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
         ss = mb::warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
         float tot = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; w++) tot += red[w];
-        const float sc = 1.0f / sqrtf(tot / g.cols + g.eps);
-        for (int p = threadIdx.x; p < g.cols; p += kThreads) xs[p] = xs[p] * sc * __ldg(g.gain + p);
+        sc = 1.0f / sqrtf(tot / g.cols + g.eps);
     }
-    __syncthreads();
-    // limbs: thread (s, t, h) owns columns 32 s + 16 h + 4 t + {0..3} = B-fragment register
-    // h of lanes 4 n + t (limb n); the 8 threads of a step are an aligned 8-lane block
     for (int base = 0; base < steps * 8; base += kThreads) {
         const int th = base + threadIdx.x;
         const bool live = th < steps * 8;
-        const int s = live ? th >> 3 : 0, tq = (th >> 1) & 3, h = th & 1;
+        const int s = live ? th >> 3 : 0, tq = (th >> 1) & 3, h = th & 1, c0 = col_of(th);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = *reinterpret_cast<const float4 *>(xs + 32 * s + 16 * h + 4 * tq);
+        if (live) {
+            v = *reinterpret_cast<const float4 *>(g.x + c0);
+            if (g.up) {  // h = silu(gate) * up, as the reference's FFN
+                const float4 u = *reinterpret_cast<const float4 *>(g.up + c0);
+                v = make_float4((v.x / (1.0f + expf(-v.x))) * u.x, (v.y / (1.0f + expf(-v.y))) * u.y,
+                                (v.z / (1.0f + expf(-v.z))) * u.z, (v.w / (1.0f + expf(-v.w))) * u.w);
+            }
+            if (g.gain) {
+                const float4 gn = *reinterpret_cast<const float4 *>(g.gain + c0);
+                v = make_float4(v.x * sc * gn.x, v.y * sc * gn.y, v.z * sc * gn.z, v.w * sc * gn.w);
+            }
+        }
         float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         float sum = (v.x + v.y) + (v.z + v.w);
 #pragma unroll
