@@ -193,101 +193,126 @@ int pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args &&
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? 0 : 1;
 }
 
-// QKV biases, RoPE on q and k, and the KV-cache write for this position.
-__global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ v,
-                           const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
-                           RopeArgs ra, const int *__restrict__ pos_ptr, float *__restrict__ kc,
-                           float *__restrict__ vc, int layer)
-{
-    pdl_enter();
-    const int pos = *pos_ptr;
-    const int half = ra.head_dim / 2;
-    const int npairs = (ra.heads + ra.kv_heads) * half;
-    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < npairs; t += gridDim.x * blockDim.x) {
-        const bool is_q = t < ra.heads * half;
-        const int tt = is_q ? t : t - ra.heads * half;
-        const int head = tt / half, i = tt % half;
-        float *vec = is_q ? q : k;
-        const float *bias = is_q ? bq : bk;
-        // NORM: pairs (2i, 2i+1); NEOX: pairs (i, i + half)
-        const int a = head * ra.head_dim + (ra.neox ? i : 2 * i);
-        const int b = ra.neox ? a + half : a + 1;
-        float x0 = vec[a], x1 = vec[b];
-        if (bias) {
-            x0 += bias[a];
-            x1 += bias[b];
-        }
-        const float cs = ra.cos_t[pos * half + i], sn = ra.sin_t[pos * half + i];
-        const float y0 = x0 * cs - x1 * sn, y1 = x0 * sn + x1 * cs;
-        if (is_q) {
-            vec[a] = y0;
-            vec[b] = y1;
-        } else {
-            float *kd = kc + (((size_t)layer * ra.kv_heads + head) * ra.context + pos) * ra.head_dim;
-            kd[a - head * ra.head_dim] = y0;
-            kd[b - head * ra.head_dim] = y1;
-        }
-    }
-    const int kvd = ra.kv_heads * ra.head_dim;
-    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < kvd; t += gridDim.x * blockDim.x) {
-        const int head = t / ra.head_dim, d = t % ra.head_dim;
-        float *vd = vc + (((size_t)layer * ra.kv_heads + head) * ra.context + pos) * ra.head_dim;
-        vd[d] = v[t] + (bv ? bv[t] : 0.f);
-    }
-}
-
-constexpr int kAttnThreads = 256;
-constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxHeadDim = 128;
 
-// One CTA per query head; warps split the positions, online softmax per warp, then a
-// merge in shared memory.  scale = 1/sqrt(head_dim).
-__global__ void __launch_bounds__(kAttnThreads)
-    k_attention(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, RopeArgs ra,
-                const int *__restrict__ pos_ptr, int layer, float *__restrict__ out)
+// QKV post-processing and attention of one query head (one CTA of 256 threads per head):
+//   post    the head's q and its KV head's k get the biases and RoPE exactly as
+//           k_qkv_post computes them, v its bias; the first query head of each KV group
+//           writes k and v to the cache; all three stay in shared memory (the cache row
+//           at `pos` is read from there, so no CTA reads a row another is writing);
+//   scores  one position per thread: the key row against q (float4 loads), times
+//           1/sqrt(head_dim);
+//   softmax block max, exp(s - max) in place, block sum;
+//   P V     warp w takes positions w, w + 8, ...; lane l accumulates dims l + 32 j
+//           (coalesced key rows), the 8 warp partials are added in warp order.
+// One launch per layer instead of two, and no per-position warp reductions.
+constexpr int kFaThreads = 256, kFaWarps = kFaThreads / 32, kFaContext = 1024;
+
+__global__ void __launch_bounds__(kFaThreads)
+    k_attention_fused(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                      const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
+                      RopeArgs ra, const int *__restrict__ pos_ptr, float *__restrict__ kc, float *__restrict__ vc,
+                      int layer, float *__restrict__ out)
 {
     pdl_enter();
-    __shared__ float qs[kMaxHeadDim];
-    __shared__ float wm[kAttnWarps], wl[kAttnWarps];
-    __shared__ float wacc[kAttnWarps][kMaxHeadDim];
-    const int h = blockIdx.x, hd = ra.head_dim, kvh = h / (ra.heads / ra.kv_heads);
-    const int pos = *pos_ptr;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[h * hd + d];
+    __shared__ __align__(16) float qs[kMaxHeadDim], kn[kMaxHeadDim];
+    __shared__ float vn[kMaxHeadDim];
+    __shared__ float sc[kFaContext];
+    __shared__ float red[kFaWarps];
+    __shared__ float wacc[kFaWarps][kMaxHeadDim];
+    const int h = blockIdx.x, hd = ra.head_dim, half = hd / 2, gqa = ra.heads / ra.kv_heads, kvh = h / gqa;
+    const int pos = min(*pos_ptr, ra.context - 1), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool writer = h % gqa == 0;
+    const size_t row = ((size_t)layer * ra.kv_heads + kvh) * ra.context;
+    if (tid < half) {
+        // NORM: pairs (2i, 2i+1); NEOX: pairs (i, i + half)
+        const int i = tid, a = ra.neox ? i : 2 * i, b = ra.neox ? a + half : a + 1;
+        const float cs = ra.cos_t[pos * half + i], sn = ra.sin_t[pos * half + i];
+        float x0 = q[h * hd + a], x1 = q[h * hd + b];
+        if (bq) {
+            x0 += bq[h * hd + a];
+            x1 += bq[h * hd + b];
+        }
+        qs[a] = x0 * cs - x1 * sn;
+        qs[b] = x0 * sn + x1 * cs;
+        x0 = k[kvh * hd + a];
+        x1 = k[kvh * hd + b];
+        if (bk) {
+            x0 += bk[kvh * hd + a];
+            x1 += bk[kvh * hd + b];
+        }
+        const float y0 = x0 * cs - x1 * sn, y1 = x0 * sn + x1 * cs;
+        kn[a] = y0;
+        kn[b] = y1;
+        if (writer) {
+            float *kd = kc + (row + pos) * hd;
+            kd[a] = y0;
+            kd[b] = y1;
+        }
+    }
+    if (tid < hd) {
+        const float vv = v[kvh * hd + tid] + (bv ? bv[kvh * hd + tid] : 0.f);
+        vn[tid] = vv;
+        if (writer) vc[(row + pos) * hd + tid] = vv;
+    }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale = 1.0f / sqrtf((float)hd);
-    const float *kb = kc + ((size_t)layer * ra.kv_heads + kvh) * ra.context * hd;
-    const float *vb = vc + ((size_t)layer * ra.kv_heads + kvh) * ra.context * hd;
+    const float *kb = kc + row * hd, *vb = vc + row * hd;
+    float mloc = -INFINITY;
+    for (int p = tid; p <= pos; p += kFaThreads) {
+        const float4 *kr = reinterpret_cast<const float4 *>(p == pos ? kn : kb + (size_t)p * hd);
+        const float4 *qr = reinterpret_cast<const float4 *>(qs);
+        float z = 0.f;
+        for (int j = 0; j < hd / 4; j++) {
+            const float4 kv = kr[j], qv = qr[j];
+            z = fmaf(qv.x, kv.x, z);
+            z = fmaf(qv.y, kv.y, z);
+            z = fmaf(qv.z, kv.z, z);
+            z = fmaf(qv.w, kv.w, z);
+        }
+        z *= scale;
+        sc[p] = z;
+        mloc = fmaxf(mloc, z);
+    }
+    mloc = mb::warp_max(mloc);
+    if (lane == 0) red[warp] = mloc;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int w = 1; w < kFaWarps; w++) m = fmaxf(m, red[w]);
+    __syncthreads();  // red is reused for the sums
+    float lloc = 0.f;
+    for (int p = tid; p <= pos; p += kFaThreads) {
+        const float e = expf(sc[p] - m);
+        sc[p] = e;
+        lloc += e;
+    }
+    lloc = mb::warp_sum(lloc);
+    if (lane == 0) red[warp] = lloc;
+    __syncthreads();
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFaWarps; w++) l += red[w];
     const int per = hd / 32;  // dims per lane (2 or 4)
-    float m = -INFINITY, l = 0.f, acc[kMaxHeadDim / 32];
+    float acc[kMaxHeadDim / 32];
 #pragma unroll
     for (int j = 0; j < kMaxHeadDim / 32; j++) acc[j] = 0.f;
-    for (int p = warp; p <= pos; p += kAttnWarps) {
-        float z = 0.f;
-        for (int j = 0; j < per; j++) z = fmaf(qs[lane + 32 * j], kb[(size_t)p * hd + lane + 32 * j], z);
-        z = mb::warp_sum(z) * scale;
-        const float mn = fmaxf(m, z), c = expf(m - mn), e = expf(z - mn);
-        l = l * c + e;
-        for (int j = 0; j < per; j++) acc[j] = acc[j] * c + e * vb[(size_t)p * hd + lane + 32 * j];
-        m = mn;
+    for (int p = warp; p <= pos; p += kFaWarps) {
+        const float e = sc[p];
+        const float *vr = p == pos ? vn : vb + (size_t)p * hd;
+#pragma unroll
+        for (int j = 0; j < kMaxHeadDim / 32; j++)
+            if (j < per) acc[j] = fmaf(e, vr[lane + 32 * j], acc[j]);
     }
-    if (lane == 0) {
-        wm[warp] = m;
-        wl[warp] = l;
-    }
-    for (int j = 0; j < per; j++) wacc[warp][lane + 32 * j] = acc[j];
+#pragma unroll
+    for (int j = 0; j < kMaxHeadDim / 32; j++)
+        if (j < per) wacc[warp][lane + 32 * j] = acc[j];
     __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float mx = -INFINITY;
-        for (int w = 0; w < kAttnWarps; w++) mx = fmaxf(mx, wm[w]);
-        float lsum = 0.f, a = 0.f;
-        for (int w = 0; w < kAttnWarps; w++) {
-            if (wm[w] == -INFINITY) continue;
-            const float c = expf(wm[w] - mx);
-            lsum = fmaf(c, wl[w], lsum);
-            a = fmaf(c, wacc[w][d], a);
-        }
-        out[h * hd + d] = a / lsum;
+    for (int d = tid; d < hd; d += kFaThreads) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < kFaWarps; w++) a += wacc[w][d];
+        out[h * hd + d] = a / l;
     }
 }
 
@@ -409,10 +434,8 @@ int enqueue_forward(mocha_gguf *m, bool project)
         // RMSNorm folded into the fused q|k|v GEMV
         rc = (tc ? mmv({{&L.mq, m->q}, {&L.mk, m->k}, {&L.mv, m->v}}, m->x, L.attn_norm, false)
                  : multi({{&L.q, m->q}, {&L.k, m->k}, {&L.v, m->v}}, m->x, L.attn_norm, false)) ||
-             pdl(k_qkv_post, dim3(8), dim3(256), s, m->q, m->k, m->v, L.bq, L.bk, L.bv, m->rope, m->state + 1, m->kc,
-                 m->vc, l) ||
-             pdl(k_attention, dim3(in.heads), dim3(kAttnThreads), s, m->q, m->kc, m->vc, m->rope, m->state + 1, l,
-                 m->att) ||
+             pdl(k_attention_fused, dim3(in.heads), dim3(kFaThreads), s, m->q, m->k, m->v, L.bq, L.bk, L.bv,
+                 m->rope, m->state + 1, m->kc, m->vc, l, m->att) ||
              (tc ? mmv({{&L.mo, m->x}}, m->att, nullptr, true) : multi({{&L.o, m->x}}, m->att, nullptr, true)) ||
              (tc ? mmv({{&L.mgate, m->g}, {&L.mup, m->u}}, m->x, L.ffn_norm, false)
                  : multi({{&L.gate, m->g}, {&L.up, m->u}}, m->x, L.ffn_norm, false)) ||
@@ -664,7 +687,7 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
         capture(m, &m->g_decode, 3))
         return 1;
     // embedding row, per layer q|k|v, post, attention, O, gate|up, (SwiGLU,) down; head; sampler
-    m->launches_per_token = 1 + (unsigned long long)in.layers * (m->mma ? 6 : 7) + 1 + 3;
+    m->launches_per_token = 1 + (unsigned long long)in.layers * (m->mma ? 5 : 6) + 1 + 3;
     TRY(cudaStreamSynchronize(m->stream));
     return 0;
 }
