@@ -79,7 +79,7 @@ struct MmaMat {
 __host__ __device__ inline size_t mma_tile_bytes(int type, int cols)
 {
     if (cols <= 0 || cols % 256) return 0;
-    if (type == Q4_K) return (size_t)(cols / 256) * 2304;
+    if (type == Q4_K) return (size_t)(cols / 256) * 2368;  // 64 B d|dmin, 256 B unpacked scales, 2048 B nibbles
     if (type == Q6_K) return (size_t)(cols / 256) * 3360;
     if (type == Q8_0) return (size_t)(cols / 32) * 544;
     return 0;

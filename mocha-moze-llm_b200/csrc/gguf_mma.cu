@@ -48,27 +48,15 @@ constexpr size_t kPrefetchBytes = 160 * 1024;  // per CTA: 148 CTAs x 160 KB = 2
 // fp16 bits -> fp32 (exact for every fp16 value)
 MB_DEV float half_to_float(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu))); }
 
-// byte k (4..15) of a Q4_K block header held as words y (bytes 4..7), z (8..11), w (12..15)
-MB_DEV uint32_t hdr_byte(uint32_t y, uint32_t z, uint32_t w, int k)
-{
-    const uint32_t v = k < 8 ? y : k < 12 ? z : w;
-    return (v >> (8 * (k & 3))) & 0xffu;
-}
+// Repacked Q4_K record of one (16-row tile, 256-column block), kQ4Rec bytes:
+//   [0, 64)      per row r: d | dmin << 16 (the file's fp16 pair)
+//   [64, 320)    per row r: the 8 sub-block scales, then the 8 sub-block mins, one byte
+//                each, unpacked from the file's 6-bit fields (ggml's get_scale_min_k4)
+//   [320, 2368)  per 32-column step: per lane 8 bytes of nibbles in mma fragment order
+constexpr int kQ4Hdr = 64, kQ4Scales = 320, kQ4Rec = 2368;
 
-// 6-bit scale and min of Q4_K sub-block j (ggml's get_scale_min_k4)
-MB_DEV void q4k_sm(uint32_t y, uint32_t z, uint32_t w, int j, float &sc, float &mn)
-{
-    uint32_t s, m;
-    if (j < 4) {
-        s = hdr_byte(y, z, w, 4 + j) & 63u;
-        m = hdr_byte(y, z, w, 8 + j) & 63u;
-    } else {
-        s = (hdr_byte(y, z, w, 8 + j) & 15u) | ((hdr_byte(y, z, w, j) >> 6) << 4);
-        m = (hdr_byte(y, z, w, 8 + j) >> 4) | ((hdr_byte(y, z, w, 4 + j) >> 6) << 4);
-    }
-    sc = (float)s;
-    mn = (float)m;
-}
+// byte j & 3 of w as an integer (the upper bytes of the selector pick the zero word)
+MB_DEV uint32_t byte_of(uint32_t w, int j) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)(j & 3)); }
 
 MB_DEV void mma_u8s8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b)
 {
@@ -113,11 +101,26 @@ __global__ void k_repack_q4k_mma(const uint8_t *__restrict__ raw, int tiles, int
     const size_t n = (size_t)tiles * nb;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / nb), b = (int)(i % nb);
-        uint8_t *o = dst + i * 2304;
+        uint8_t *o = dst + i * kQ4Rec;
         const uint8_t *blk[16];
         for (int j = 0; j < 16; j++) blk[j] = raw + ((size_t)(16 * t + j) * nb + b) * 144;
-        for (int j = 0; j < 16; j++)
-            for (int k = 0; k < 16; k++) o[16 * j + k] = blk[j][k];
+        for (int j = 0; j < 16; j++) {
+            for (int k = 0; k < 4; k++) o[4 * j + k] = blk[j][k];
+            // 6-bit scale / min of sub-block u from the 12 scale bytes q = header bytes 4..15
+            const uint8_t *q = blk[j] + 4;
+            for (int u = 0; u < 8; u++) {
+                uint8_t sc, mn;
+                if (u < 4) {
+                    sc = q[u] & 63;
+                    mn = q[u + 4] & 63;
+                } else {
+                    sc = (uint8_t)((q[u + 4] & 15) | ((q[u - 4] >> 6) << 4));
+                    mn = (uint8_t)((q[u + 4] >> 4) | ((q[u] >> 6) << 4));
+                }
+                o[kQ4Hdr + 16 * j + u] = sc;
+                o[kQ4Hdr + 16 * j + 8 + u] = mn;
+            }
+        }
         // nibble q of column c (0..255) of a block: qs[32 (c / 64) + c % 32] >> 4 ((c / 32) & 1)
         auto q = [&](int j, int c) -> uint32_t {
             return (blk[j][16 + 32 * (c >> 6) + (c & 31)] >> (4 * ((c >> 5) & 1))) & 15u;
@@ -125,7 +128,7 @@ __global__ void k_repack_q4k_mma(const uint8_t *__restrict__ raw, int tiles, int
         for (int s = 0; s < 8; s++)
             for (int l = 0; l < 32; l++) {
                 const int g = l >> 2, tg = l & 3;
-                uint8_t *r = o + 256 + s * 256 + l * 8;
+                uint8_t *r = o + kQ4Scales + s * 256 + l * 8;
                 for (int ii = 0; ii < 4; ii++) {
                     const int c0 = 32 * s + 4 * tg + ii, c1 = c0 + 16;
                     r[ii] = (uint8_t)(q(g, c0) | (q(g, c1) << 4));
@@ -238,8 +241,9 @@ struct Job {
 // Loads of one batch (all lanes), kept in registers until the batch is computed.
 struct Batch {
     uint4 w[kBatch];     // Q4_K: nibble records (x, y); Q6_K: lo (x, y) + hi (z); Q8_0: fragments
-    uint4 h0, h1;        // Q4_K headers of rows g, g + 8; Q6_K scales of rows g, g + 8
-    uint32_t dd[kBatch]; // Q6_K: d of rows g (low 16) and g + 8 (high 16); Q8_0: per step likewise
+    uint4 h0, h1;        // Q4_K sub-block scale / min bytes of rows g, g + 8; Q6_K scales of rows g, g + 8
+    uint32_t dd[kBatch]; // Q4_K: d | dmin of rows g, g + 8; Q6_K: d of rows g (low 16) and g + 8
+                         // (high 16); Q8_0: per step likewise
 };
 
 MB_DEV void load_batch(const Job &jb, int s0, int lane, Batch &B)
@@ -247,12 +251,14 @@ MB_DEV void load_batch(const Job &jb, int s0, int lane, Batch &B)
     const int g = lane >> 2;
     if (jb.type == Q4_K) {
         const int blk = s0 >> 3, nb = jb.steps >> 3;
-        const uint8_t *rec = jb.body + ((size_t)jb.tile * nb + blk) * 2304;
-        B.h0 = __ldg(reinterpret_cast<const uint4 *>(rec + 16 * g));
-        B.h1 = __ldg(reinterpret_cast<const uint4 *>(rec + 16 * (g + 8)));
+        const uint8_t *rec = jb.body + ((size_t)jb.tile * nb + blk) * kQ4Rec;
+        B.dd[0] = __ldg(reinterpret_cast<const uint32_t *>(rec) + g);
+        B.dd[1] = __ldg(reinterpret_cast<const uint32_t *>(rec) + g + 8);
+        B.h0 = __ldg(reinterpret_cast<const uint4 *>(rec + kQ4Hdr + 16 * g));
+        B.h1 = __ldg(reinterpret_cast<const uint4 *>(rec + kQ4Hdr + 16 * (g + 8)));
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
-            const uint2 v = mb::ld_stream8(rec + 256 + ((s0 & 7) + k) * 256 + lane * 8);
+            const uint2 v = mb::ld_stream8(rec + kQ4Scales + ((s0 & 7) + k) * 256 + lane * 8);
             B.w[k] = make_uint4(v.x, v.y, 0u, 0u);
         }
     } else if (jb.type == Q6_K) {
@@ -336,18 +342,51 @@ MB_DEV void run_batch(const Job &jb, int s0, int lane, const Batch &B, const uin
         }
         return;
     }
+    if (jb.type == Q4_K) {
+        // the 4 steps are 4 sub-blocks of one 256-column block, whose activation limbs
+        // share one scale: the sub-block scales fold into int32 sums (|sum| <= 4 x 63 x
+        // 32 x 15 x 127 < 2^31), the limbs are combined once per batch, and the mins take
+        // sum_j m_j x32_j.  Lanes t = 0 hold limbs 0 and 1, lanes t = 1 limb 2; lane t = 0
+        // of each quad accumulates rows g / g + 8.
+        int T[4] = {0, 0, 0, 0};
+        float mn0 = 0.f, mn1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int s = s0 + k, j = s & 7;
+            const uint2 b = bf[s * 32 + lane];
+            int d[4] = {0, 0, 0, 0};
+            const uint32_t w0 = B.w[k].x, w1 = B.w[k].y;
+            mma_u8s8_k32(d, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, (w1 >> 4) & 0x0F0F0F0Fu, b);
+            const bool lo = j < 4;
+            const int sc0 = (int)byte_of(lo ? B.h0.x : B.h0.y, j), sc1 = (int)byte_of(lo ? B.h1.x : B.h1.y, j);
+            T[0] += sc0 * d[0];
+            T[1] += sc0 * d[1];
+            T[2] += sc1 * d[2];
+            T[3] += sc1 * d[3];
+            const float xs = x32[s];
+            mn0 = fmaf((float)byte_of(lo ? B.h0.z : B.h0.w, j), xs, mn0);
+            mn1 = fmaf((float)byte_of(lo ? B.h1.z : B.h1.w, j), xs, mn1);
+        }
+        // 254 T0 + T1 + T2 / 254 per row (T2 from lane t + 1)
+        const int e0 = __shfl_down_sync(0xffffffffu, T[0], 1), e2 = __shfl_down_sync(0xffffffffu, T[2], 1);
+        const float v0 = fmaf((float)e0, 1.f / 254.f, fmaf((float)T[0], 254.f, (float)T[1]));
+        const float v1 = fmaf((float)e2, 1.f / 254.f, fmaf((float)T[2], 254.f, (float)T[3]));
+        if (tg == 0) {
+            const float f = sx[s0];
+            const float d0 = half_to_float(B.dd[0]), dm0 = half_to_float(B.dd[0] >> 16);
+            const float d1 = half_to_float(B.dd[1]), dm1 = half_to_float(B.dd[1] >> 16);
+            acc0 += d0 * (v0 * f) - dm0 * mn0;
+            acc1 += d1 * (v1 * f) - dm1 * mn1;
+        }
+        return;
+    }
     float q0 = 0.f, q1 = 0.f;  // this lane's step: limb values of rows g / g + 8
 #pragma unroll
     for (int k = 0; k < kBatch; k++) {
         const int s = s0 + k;
         const uint2 b = bf[s * 32 + lane];
         int d[4] = {0, 0, 0, 0};
-        if (jb.type == Q4_K) {
-            const uint32_t w0 = B.w[k].x, w1 = B.w[k].y;
-            mma_u8s8_k32(d, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, (w1 >> 4) & 0x0F0F0F0Fu, b);
-        } else {
-            mma_s8s8_k32(d, B.w[k].x, B.w[k].y, B.w[k].z, B.w[k].w, b);
-        }
+        mma_s8s8_k32(d, B.w[k].x, B.w[k].y, B.w[k].z, B.w[k].w, b);
         float v0, v1;
         combine(d, v0, v1);
         v0 = __shfl_sync(0xffffffffu, v0, src);
@@ -359,16 +398,7 @@ MB_DEV void run_batch(const Job &jb, int s0, int lane, const Batch &B, const uin
     }
     const int s = s0 + tg;
     const float f = sx[s];
-    if (jb.type == Q4_K) {
-        const int j = s & 7;
-        float sc0, m0, sc1, m1;
-        q4k_sm(B.h0.y, B.h0.z, B.h0.w, j, sc0, m0);
-        q4k_sm(B.h1.y, B.h1.z, B.h1.w, j, sc1, m1);
-        const float d0 = half_to_float(B.h0.x), dm0 = half_to_float(B.h0.x >> 16);
-        const float d1 = half_to_float(B.h1.x), dm1 = half_to_float(B.h1.x >> 16);
-        acc0 += (d0 * sc0) * (q0 * f) - (dm0 * m0) * x32[s];
-        acc1 += (d1 * sc1) * (q1 * f) - (dm1 * m1) * x32[s];
-    } else {
+    {
         const uint32_t dd = tg == 0 ? B.dd[0] : tg == 1 ? B.dd[1] : tg == 2 ? B.dd[2] : B.dd[3];
         acc0 += half_to_float(dd) * (q0 * f);
         acc1 += half_to_float(dd >> 16) * (q1 * f);
@@ -439,21 +469,30 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     float(*gp)[kWarps + 1] = reinterpret_cast<float(*)[kWarps + 1]>(smem + L.gp);
     __shared__ float red[kWarps];
 
-    // input limbs: thread th = (s, t, h) owns columns 32 s + 16 h + 4 t + {0..3} = B-fragment
-    // register h of lanes 4 n + t (limb n); the 8 threads of a step are an aligned 8-lane
-    // block.  The values come straight from global memory: silu(x) * up for the FFN down
-    // GEMV, x * (1/sqrt(sum x^2 / cols + eps)) * gain for a normed input (the sum of squares
-    // by a block reduction first), else x.
-    auto col_of = [&](int th) {
-        return 32 * (th >> 3) + 16 * (th & 1) + 4 * ((th >> 1) & 3);
+    // input limbs: thread th = (s, t) owns columns 32 s + 16 h + 4 t + {0..3} for h = 0, 1,
+    // B-fragment registers h of lanes 4 n + t (limb n); a warp covers one 256-column block
+    // (8 steps), whose scale max|x| / 127 all its limbs share (one activation scale per
+    // 256 columns, like the weights' super-blocks).  The values come straight from global
+    // memory: silu(x) * up for the FFN down GEMV, x * (1/sqrt(sum x^2 / cols + eps)) * gain
+    // for a normed input (the sum of squares by a block reduction first), else x.
+    auto col_of = [&](int th, int h) { return 32 * (th >> 2) + 16 * h + 4 * (th & 3); };
+    auto load = [&](int c) {
+        float4 v = *reinterpret_cast<const float4 *>(g.x + c);
+        if (g.up) {  // h = silu(gate) * up, as the reference's FFN
+            const float4 u = *reinterpret_cast<const float4 *>(g.up + c);
+            v = make_float4((v.x / (1.0f + expf(-v.x))) * u.x, (v.y / (1.0f + expf(-v.y))) * u.y,
+                            (v.z / (1.0f + expf(-v.z))) * u.z, (v.w / (1.0f + expf(-v.w))) * u.w);
+        }
+        return v;
     };
     float sc = 1.f;
     if (g.gain) {
         float ss = 0.f;
-        for (int th = threadIdx.x; th < steps * 8; th += kThreads) {
-            const float4 v = *reinterpret_cast<const float4 *>(g.x + col_of(th));
-            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-        }
+        for (int th = threadIdx.x; th < steps * 4; th += kThreads)
+            for (int h = 0; h < 2; h++) {
+                const float4 v = *reinterpret_cast<const float4 *>(g.x + col_of(th, h));
+                ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+            }
         ss = mb::warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
@@ -462,71 +501,74 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
         for (int w = 0; w < kWarps; w++) tot += red[w];
         sc = 1.0f / sqrtf(tot / g.cols + g.eps);
     }
-    for (int base = 0; base < steps * 8; base += kThreads) {
+    for (int base = 0; base < steps * 4; base += kThreads) {
         const int th = base + threadIdx.x;
-        const bool live = th < steps * 8;
-        const int s = live ? th >> 3 : 0, tq = (th >> 1) & 3, h = th & 1, c0 = col_of(th);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) {
-            v = *reinterpret_cast<const float4 *>(g.x + c0);
-            if (g.up) {  // h = silu(gate) * up, as the reference's FFN
-                const float4 u = *reinterpret_cast<const float4 *>(g.up + c0);
-                v = make_float4((v.x / (1.0f + expf(-v.x))) * u.x, (v.y / (1.0f + expf(-v.y))) * u.y,
-                                (v.z / (1.0f + expf(-v.z))) * u.z, (v.w / (1.0f + expf(-v.w))) * u.w);
-            }
+        if (base + (threadIdx.x & ~31) >= steps * 4) break;  // whole warps: steps * 4 % 32 == 0
+        const int s = th >> 2, tq = th & 3;
+        float v[2][4];
+        float m = 0.f, sum = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int c0 = col_of(th, h);
+            float4 x = load(c0);
             if (g.gain) {
                 const float4 gn = *reinterpret_cast<const float4 *>(g.gain + c0);
-                v = make_float4(v.x * sc * gn.x, v.y * sc * gn.y, v.z * sc * gn.z, v.w * sc * gn.w);
+                x = make_float4(x.x * sc * gn.x, x.y * sc * gn.y, x.z * sc * gn.z, x.w * sc * gn.w);
             }
+            v[h][0] = x.x;
+            v[h][1] = x.y;
+            v[h][2] = x.z;
+            v[h][3] = x.w;
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            sum += (x.x + x.y) + (x.z + x.w);
         }
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        float sum = (v.x + v.y) + (v.z + v.w);
+        // block max over the warp; step sum over its 4 threads
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        }
+        for (int o = 1; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         const float inv = m > 0.f ? 127.f / m : 0.f;
-        const float q[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
-        uint32_t b[3][4];
-        int ls[3] = {0, 0, 0};
+        uint32_t *bw = reinterpret_cast<uint32_t *>(&bf[s * 32]);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const float t0 = __fadd_rn(q[j], kMagic), a0 = __fsub_rn(t0, kMagic);
-            const float r1 = __fmul_rn(__fsub_rn(q[j], a0), 254.f);
-            const float t1 = __fadd_rn(r1, kMagic), a1 = __fsub_rn(t1, kMagic);
-            const float r2 = __fmul_rn(__fsub_rn(r1, a1), 254.f);
-            const float t2 = __fadd_rn(r2, kMagic), a2 = __fsub_rn(t2, kMagic);
-            b[0][j] = __float_as_uint(t0);
-            b[1][j] = __float_as_uint(t1);
-            b[2][j] = __float_as_uint(t2);
-            ls[0] += (int)a0;
-            ls[1] += (int)a1;
-            ls[2] += (int)a2;
-        }
-        // limb sums of the 16-column group (threads of one h: t bits 1..2)
+        for (int h = 0; h < 2; h++) {
+            uint32_t b[3][4];
+            int ls[3] = {0, 0, 0};
 #pragma unroll
-        for (int n = 0; n < 3; n++) {
-            ls[n] += __shfl_xor_sync(0xffffffffu, ls[n], 2);
-            ls[n] += __shfl_xor_sync(0xffffffffu, ls[n], 4);
-        }
-        if (live) {
-            uint32_t *bw = reinterpret_cast<uint32_t *>(&bf[s * 32]);
+            for (int j = 0; j < 4; j++) {
+                const float q = v[h][j] * inv;
+                const float t0 = __fadd_rn(q, kMagic), a0 = __fsub_rn(t0, kMagic);
+                const float r1 = __fmul_rn(__fsub_rn(q, a0), 254.f);
+                const float t1 = __fadd_rn(r1, kMagic), a1 = __fsub_rn(t1, kMagic);
+                const float r2 = __fmul_rn(__fsub_rn(r1, a1), 254.f);
+                const float t2 = __fadd_rn(r2, kMagic), a2 = __fsub_rn(t2, kMagic);
+                b[0][j] = __float_as_uint(t0);
+                b[1][j] = __float_as_uint(t1);
+                b[2][j] = __float_as_uint(t2);
+                ls[0] += (int)a0;
+                ls[1] += (int)a1;
+                ls[2] += (int)a2;
+            }
+            // limb sums of the 16-column group (s, h): the step's 4 threads
+#pragma unroll
+            for (int n = 0; n < 3; n++) {
+                ls[n] += __shfl_xor_sync(0xffffffffu, ls[n], 1);
+                ls[n] += __shfl_xor_sync(0xffffffffu, ls[n], 2);
+            }
 #pragma unroll
             for (int n = 0; n < 3; n++)
                 bw[2 * (4 * n + tq) + h] =
                     __byte_perm(__byte_perm(b[n][0], b[n][1], 0x0040), __byte_perm(b[n][2], b[n][3], 0x0040), 0x5410);
-            if ((th & 7) == 0) {
-                sx[s] = m / (127.f * 254.f);
-                x32[s] = sum;
-            }
-            if ((th & 6) == 0) {  // t == 0: the group's sums
+            if (tq == 0) {
                 const int grp = 2 * s + h;
                 sa[4 * grp + 0] = ls[0];
                 sa[4 * grp + 1] = ls[1];
                 sa[4 * grp + 2] = ls[2];
                 sa[4 * grp + 3] = 0;
             }
+        }
+        if (tq == 0) {
+            sx[s] = m / (127.f * 254.f);
+            x32[s] = sum;
         }
     }
     // B-fragment columns 3..7 (lanes 12..31) are zero
