@@ -390,13 +390,25 @@ __global__ void __launch_bounds__(AR_THREADS) k_attn_row(const QkvPost pp, const
     float a[GQA][2];
 #pragma unroll
     for (int h = 0; h < GQA; h++) a[h][0] = a[h][1] = 0.f;
-#pragma unroll 4
-    for (int k = warp; k < nk; k += AR_WARPS) {
-        const float2 v = kPost && k == pos ? make_float2(snv[2 * lane], snv[2 * lane + 1])
-                                  : __ldg(reinterpret_cast<const float2 *>(vb + (size_t)k * HEAD_DIM) + lane);
+    // cache rows first (16 iterations unrolled: their loads are in flight together), then
+    // with kPost the row of `pos` (the last key, so the order per warp is unchanged) from
+    // shared memory
+    const int nglob = kPost ? nk - 1 : nk;
+#pragma unroll 16
+    for (int k = warp; k < nglob; k += AR_WARPS) {
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(vb + (size_t)k * HEAD_DIM) + lane);
 #pragma unroll
         for (int h = 0; h < GQA; h++) {
             const float p = ss[h][k];
+            a[h][0] = fmaf(p, v.x, a[h][0]);
+            a[h][1] = fmaf(p, v.y, a[h][1]);
+        }
+    }
+    if (kPost && warp == (nk - 1) % AR_WARPS) {
+        const float2 v = make_float2(snv[2 * lane], snv[2 * lane + 1]);
+#pragma unroll
+        for (int h = 0; h < GQA; h++) {
+            const float p = ss[h][nk - 1];
             a[h][0] = fmaf(p, v.x, a[h][0]);
             a[h][1] = fmaf(p, v.y, a[h][1]);
         }
