@@ -587,7 +587,10 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
     in.eps = (float)num("attention.layer_norm_rms_epsilon", 1e-5);
     in.rope_base = (float)num("rope.freq_base", 10000.0);
     in.context = (int)num("context_length", 1024);
-    if (in.context > 1024 || in.context < 1) in.context = 1024;  // the reference engines run a 1024 context
+    // the reference engines run a 1024 context; k_attention_fused keeps one score per
+    // position of it in shared memory
+    static_assert(kFaContext >= 1024, "attention score buffer shorter than the context");
+    if (in.context > 1024 || in.context < 1) in.context = 1024;
     const auto te = g.tensors.find("token_embd.weight");
     if (te == g.tensors.end() || in.layers < 1 || in.dim < 256 || in.heads < 1 || in.kv_heads < 1 ||
         in.heads % in.kv_heads || in.dim % in.heads) {
