@@ -75,6 +75,12 @@ class Group:
             self.dist.destroy_process_group()
 
 
+def partition(n, world, rank):
+    """Sequences of an n-sequence job that rank `rank` of `world` serves: i mod world ==
+    rank.  Every sequence is served by exactly one rank; there is no data-path exchange."""
+    return [i for i in range(n) if i % world == rank]
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -217,7 +223,7 @@ def bench_batched(group, data, args, parts):
         return {"prefill_ms": pre_ms, "decode_s": 0.0, "prefill_s": 0.0, "generated": 0, "nseq": 0, "wall": 0.0,
                 "launches": 0}
     # batched serving: sequences i with i % world == rank
-    mine = [i for i in range(args.serve_seqs) if i % world == rank]
+    mine = partition(args.serve_seqs, world, rank)
     prompts = np.random.default_rng(2024).integers(0, 151936, (args.serve_seqs, SERVE_PROMPT))[mine]
     h.generate(prompts[:SERVE_BATCH], 8, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12, seed_base=7)
     group.barrier()

@@ -78,14 +78,18 @@ int mocha_q8_launches_per_step(mocha_q8 *h);
 int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps);
 
 /* Penalty + control mask + top-k candidates (the selection gpu_collect performs)
- * for callers that cannot allocate device memory at call time -- a host that has
- * reserved the whole GPU memory budget in its own pool, or code running during a
- * stream capture.  No counterpart in the reference.  logits[0..rows) and
- * history[0..count) are host arrays; the k best (value, id) pairs, penalised values
- * and ties to the lower id first, go to host values[k] / ids[k].  stream may be NULL.
- * All device buffers live in one fixed ~672 KiB __device__ array, so rows <= 151936;
- * larger requests fail.  The first call on a device looks the array up (make it
- * before any stream capture); calls that overlap on the GPU share the array and race. */
+ * for callers that cannot allocate device memory at call time: a host that has
+ * reserved the whole GPU memory budget in its own pool, or a latency-critical loop
+ * that must not take cudaMalloc's implicit device synchronisation.  No counterpart
+ * in the reference.  logits[0..rows) and history[0..count) are host arrays; the k
+ * best (value, id) pairs, penalised values and ties to the lower id first, go to
+ * host values[k] / ids[k]; the call waits for `stream` (may be NULL) before it
+ * returns.  The control mask is Qwen2.5's: ids >= 151643 other than EOS 151645 are
+ * set to -1e30 (it only touches rows past 151643).  All device buffers live in one
+ * fixed ~672 KiB __device__ array, so 1 <= k <= min(64, rows) and rows <= 151936;
+ * other requests fail with a message.  The first call on a device looks the array's
+ * address up (make it before any stream capture on that device); calls that overlap
+ * on the GPU share the array and race. */
 int mocha_topk_static(const float *logits, int rows, const int *history, int count, float penalty, int k,
                       float *values, int *ids, void *stream);
 
@@ -125,7 +129,8 @@ int mocha_gguf_launches_per_step(mocha_gguf *m);
 /* ---- batched engine: prefill and multi-sequence decode on tensor cores ------------
  * The batched extension of the reference ABI (gpu_forward_batch / gpu_sample_batch /
  * gpu_prefill with an explicit device index; no reference counterpart).  A handle owns
- * the model, bf16 hi/lo copies of every weight for the tcgen05 GEMMs, activation
+ * the model file as stored (int8 weights + fp32 scales), row-fused int8 copies of
+ * q|k|v and gate|up for the tcgen05 GEMMs (248 MB), activation
  * buffers for `max_rows` rows and the fp32 KV cache of `slots` sequences
  * ([slot][layer][kv head][pos][64]). */
 typedef struct mocha_q8b mocha_q8b;

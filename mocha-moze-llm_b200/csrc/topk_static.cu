@@ -2,23 +2,25 @@
 //
 // Some callers cannot call cudaMalloc at the moment they want candidates: a serving
 // host that has reserved the whole GPU memory budget in its own pool (an extra
-// allocation fails or fragments it), code running while a stream is being
-// captured (allocation is not allowed there), or a latency-critical loop where
-// cudaMalloc's implicit device synchronisation would stall other streams.  This
+// allocation fails or fragments it), or a latency-critical loop where cudaMalloc's
+// implicit device synchronisation would stall the other streams.  This
 // entry point runs the same penalty / control-mask / top-k kernels as gpu_collect
 // (sampling.cu), but every device-side buffer it needs -- the staged logits and
 // history, the parameters, the per-CTA partial keys and the merged keys -- lives in
 // one file-scope __device__ array of fixed size.  The caller passes host inputs and
-// host outputs.
+// host outputs; the call waits for its stream before it returns.
 //
 // Limits and sharing rules:
-//   * rows <= kMaxRows (151,936, one Qwen2.5 vocabulary); larger requests fail with
-//     a message.  The array occupies ~672 KiB on every GPU that loads the library,
+//   * 1 <= k <= min(64, rows) and rows <= kMaxRows (151,936, one Qwen2.5
+//     vocabulary); other requests fail with a message.  The array occupies ~672 KiB on every GPU that loads the library,
 //     until the process exits.
 //   * Every call reuses the same array, which keeps the previous call's contents;
 //     everything a call reads is written by that call first.  Calls that overlap on
 //     the GPU (from several host threads or streams) race on the array and must not
 //     be issued concurrently.
+//   * The control mask is Qwen2.5's (src/minimind.cu:143-144): ids >= 151643 other
+//     than EOS 151645 are set to -1e30 before selection, so it only touches callers
+//     whose rows extend past 151643.
 //   * The first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (and sets the merge kernel's shared-memory limit); make
 //     that first call before starting any stream capture on that device.
@@ -87,6 +89,10 @@ extern "C" int mocha_topk_static(const float *logits, int rows, const int *histo
     }
     if (k < 1 || k > sampling::kMaxK || count < 0 || count > sampling::kHistory) {
         fprintf(stderr, "mocha_topk_static: k must be 1..64 and count 0..64\n");
+        return 1;
+    }
+    if (k > rows) {  // fewer candidates than asked for: the merge would return empty keys
+        fprintf(stderr, "mocha_topk_static: k=%d exceeds rows=%d\n", k, rows);
         return 1;
     }
     unsigned char *base = scratch_for_current_device();

@@ -68,35 +68,42 @@ def quantize_groups(w: np.ndarray):
     return q, scale
 
 
-def write_random_model(path: str, seed: int = 1) -> str:
-    """Write a random-init Qwen2.5-0.5B-shaped grouped-Q8 file; returns ``path``."""
-    rng = np.random.default_rng(seed)
+def write_model(path: str, tensors) -> str:
+    """Write a grouped-Q8 file from fp32 tensors given in file order; returns ``path``.
+
+    ``tensors`` yields ``(values, quantised)`` per tensor slot: ``values`` an fp32 array
+    of shape (rows, cols) or (n,) -- or, for large matrices, an iterable of row blocks
+    that are quantised and written one after the other -- and ``quantised`` whether it is
+    stored as int8 + per-64 scales.  The record is (data, scales, rows, cols) with
+    rows = shape[0] and cols = shape[-1] (n and n for vectors), like
+    ``tools/convert-qwen.py:45``; the header's shape fields are the Qwen2.5-0.5B ones.
+    """
     records = []
     tmp = path + ".tmp"
     with open(tmp, "wb") as f:
         f.write(bytes(HEADER_BYTES))
-        for rows, cols, quant, kind in tensor_shapes():
+        count = 0
+        for values, quant in tensors:
+            blocks = [values] if isinstance(values, np.ndarray) else values
+            rows, cols = 0, 0
             offset = f.tell()
-            if quant:
-                scale_parts = []
-                # bound temporaries for the 136M-entry embedding
-                step = max(1, (1 << 24) // cols)
-                for r0 in range(0, rows, step):
-                    n = min(step, rows - r0)
-                    w = rng.standard_normal((n, cols), dtype=np.float32) * np.float32(0.02)
-                    q, s = quantize_groups(w)
+            scale_parts = []
+            for b in blocks:
+                rows += b.shape[0]
+                cols = b.shape[-1]
+                if quant:
+                    q, sc = quantize_groups(b)
                     f.write(q.tobytes())
-                    scale_parts.append(s)
-                scale_offset = f.tell()
-                for s in scale_parts:
-                    f.write(s.astype("<f4").tobytes())
-            else:
-                n = rows
-                v = rng.standard_normal(n, dtype=np.float32)
-                v = (np.float32(1) + np.float32(0.01) * v) if kind == "norm" else np.float32(0.02) * v
-                f.write(v.astype("<f4").tobytes())
-                scale_offset = 0
+                    scale_parts.append(sc)
+                else:
+                    f.write(np.ascontiguousarray(b, dtype="<f4").tobytes())
+            scale_offset = f.tell() if quant else 0
+            for sc in scale_parts:
+                f.write(sc.astype("<f4").tobytes())
             records.append((offset, scale_offset, rows, cols))
+            count += 1
+        if count != TENSORS:
+            raise ValueError(f"{count} tensors, the format has {TENSORS}")
         size = f.tell()
         f.seek(0)
         f.write(struct.pack("<8I", MAGIC, VERSION, size, DIM, HIDDEN, LAYERS, VOCAB, GROUP))
@@ -104,6 +111,31 @@ def write_random_model(path: str, seed: int = 1) -> str:
             f.write(struct.pack("<4I", *rec))
     os.replace(tmp, path)
     return path
+
+
+def random_tensors(seed: int = 1):
+    """Seeded random-init fp32 tensors of the Qwen2.5-0.5B shapes in file order:
+    weights N(0, 0.02) (the embedding in row blocks, to bound temporaries), norm gains
+    1 + N(0, 0.01), biases N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+
+    def blocks(rows, cols):  # drawn lazily, in file order
+        step = max(1, (1 << 24) // cols)
+        for r0 in range(0, rows, step):
+            yield rng.standard_normal((min(step, rows - r0), cols), dtype=np.float32) * np.float32(0.02)
+
+    for rows, cols, quant, kind in tensor_shapes():
+        if quant:
+            yield blocks(rows, cols), True
+        else:
+            v = rng.standard_normal(rows, dtype=np.float32)
+            v = (np.float32(1) + np.float32(0.01) * v) if kind == "norm" else np.float32(0.02) * v
+            yield v, False
+
+
+def write_random_model(path: str, seed: int = 1) -> str:
+    """Write a random-init Qwen2.5-0.5B-shaped grouped-Q8 file; returns ``path``."""
+    return write_model(path, random_tensors(seed))
 
 
 def model_path(seed: int = 1, cache_dir: str | None = None) -> str:

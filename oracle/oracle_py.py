@@ -17,10 +17,17 @@ VOCAB = 151936
 DIM = 896
 
 
+def reference_dir() -> str:
+    """The reference source directory the oracle recipe builds from (MOCHA_REFERENCE_DIR,
+    else the recipe's default); it need not exist."""
+    p = subprocess.run(["make", "-s", "-C", HERE, "refdir"], check=True, capture_output=True, text=True)
+    return p.stdout.strip()
+
+
 def build(ref: bool = True) -> None:
     """Build liboracle.so and, when the reference sources exist, oracle/_ref."""
     subprocess.run(["make", "-C", HERE, "all"], check=True, capture_output=True)
-    if ref and os.path.isdir("/root/reference/src"):
+    if ref and os.path.isdir(os.path.join(reference_dir(), "src")):
         subprocess.run(["make", "-C", HERE, "ref"], check=True, capture_output=True)
 
 
