@@ -31,7 +31,8 @@ PUBLISHED_TOKS = 7.75          # reference CUDA decode on GK20A (docs/performanc
 PROMPT_LEN, NEW_TOKENS, PROMPT_SEED, MODEL_SEED = 34, 256, 7, 1
 WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per token
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
-REF_SAMPLE_TOKENS = 32
+ONE_THREAD_TOKENS = 16         # bounded 1-thread sample of the reference engine
+SERVE_REF_SEQS = 2             # sequences of the batched job timed on the reference engine
 TRAFFIC_PER_TOKEN = 554_759_680  # DRAM read + write per k_step launch (551.35 + 3.41 MB), ncu, position 40
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
@@ -148,18 +149,23 @@ def model_bytes(group):
     return path, np.fromfile(path, dtype=np.uint8)
 
 
-def run_reference_engine(model_path, prompt, n, threads):
+def run_reference_engine(model_path, prompt, n, threads, sampling=("0", "42", "1.0", "1", "1.0"), metrics=False):
+    """One run of the reference CPU engine (src/minimind.cpp built from the reference
+    sources); sampling = (temperature, seed, repeat penalty, top-k, top-p)."""
     binary = os.path.join(ORACLE, "_ref", "minimind_cpu")
+    temp, seed, pen, k, top_p = sampling
     with tempfile.NamedTemporaryFile("w", suffix=".txt", delete=False) as f:
         f.write(" ".join(map(str, prompt)))
     try:
-        p = subprocess.run([binary, model_path, f.name, str(n), "cpu", "0", "42", "0", "1.0", "1", "1.0"],
+        p = subprocess.run([binary, model_path, f.name, str(n), "cpu", temp, seed, "0", pen, k, top_p],
                            capture_output=True, text=True, env=dict(os.environ, OMP_NUM_THREADS=str(threads)))
     finally:
         os.unlink(f.name)
     if p.returncode != 0:
         raise RuntimeError(p.stderr)
     m = dict(re.findall(r"(\w+)=([^\s]+)", p.stderr))
+    if metrics:
+        return m
     gen = int(m["GENERATED"])
     tps = float(m["DECODE_TPS"])
     return gen, tps, (gen - 1) / tps if tps > 0 else 0.0
@@ -178,22 +184,24 @@ def reference_arm(args):
     prompt = mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED)
     cores = os.cpu_count()
     for _ in range(args.warmup):
-        run_reference_engine(path, prompt, REF_SAMPLE_TOKENS, cores)
+        run_reference_engine(path, prompt, NEW_TOKENS, cores)
     toks, secs = 0, 0.0
     for _ in range(args.steps):
-        gen, tps, s = run_reference_engine(path, prompt, REF_SAMPLE_TOKENS, cores)
+        gen, tps, s = run_reference_engine(path, prompt, NEW_TOKENS, cores)
         toks += gen - 1
         secs += s
     value = toks / secs
-    sample = (f"reference CPU engine, {PROMPT_LEN}-token prompt + {REF_SAMPLE_TOKENS} greedy tokens per step, "
-              f"DECODE_TPS definition (tokens after the first / decode wall time)")
+    sample = (f"reference CPU engine (src/minimind.cpp -O3 -fopenmp, {cores} threads), the full workload per "
+              f"step: {PROMPT_LEN}-token prompt + {NEW_TOKENS} greedy tokens, DECODE_TPS definition (tokens "
+              f"after the first / decode wall time)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": value / PUBLISHED_TOKS, "dtype": "f32",
         "data": "synthetic: random-init weights (seed 1), 34 random prompt ids",
-        "config": {"workload": "Qwen2.5-0.5B grouped-Q8 b=1 greedy decode (sample of the 256-token run)",
-                   "parallelism": "cpu"},
+        "config": {"workload": "Qwen2.5-0.5B grouped-Q8 b=1 greedy decode: 34-token prompt, 256 generated "
+                               "(positions 33..288), one step = one 256-token decode",
+                   "global_batch": 1, "seq_len": PROMPT_LEN + NEW_TOKENS, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -286,17 +294,25 @@ def gguf_objects(gathered, args, world):
     return res
 
 
+INT8_TOPS_DATASHEET = 4500.0   # B200 dense int8 tensor peak (datasheet; no measured int8 figure exists here)
+PREFILL_GEMM_FLOP = 2 * 357_826_560 * 1024 + 2 * 136_134_656   # the GEMM part of PREFILL_FLOP
+
+
 def prefill_object(gathered, args, world):
     tf_peak, tf_kind = peak_tflops()
     pre_ms = max(g["prefill_ms"] for g in gathered) / args.steps
     achieved_tf = PREFILL_FLOP / (pre_ms / 1e3) / 1e12
+    issued_tops = (3 * PREFILL_GEMM_FLOP + (PREFILL_FLOP - PREFILL_GEMM_FLOP)) / (pre_ms / 1e3) / 1e12
     return {"value": PREFILL_LEN * world / (pre_ms / 1e3), "unit": "tok/s", "ms_per_prompt": pre_ms,
             "config": {"workload": "one 1024-token prompt of uniform random ids per GPU, head on the last position"},
-            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s",
-                         "frac": achieved_tf / tf_peak, "peak_kind": tf_kind,
+            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": INT8_TOPS_DATASHEET, "unit": "TFLOP/s",
+                         "frac": achieved_tf / INT8_TOPS_DATASHEET, "peak_kind": "datasheet dense int8",
                          "algorithmic_flop_per_prompt": PREFILL_FLOP,
-                         "note": "int8 tcgen05 GEMMs against three int8 limbs of each activation: the "
-                                 "tensor pipe issues 3x the algorithmic MACs (at the int8 rate, twice bf16's)"}}
+                         "issued_tops": issued_tops, "issued_frac": issued_tops / INT8_TOPS_DATASHEET,
+                         "bf16_peak": tf_peak, "bf16_peak_kind": tf_kind, "bf16_frac": achieved_tf / tf_peak,
+                         "note": "the GEMMs issue tcgen05.mma kind::i8 against three int8 limbs of each "
+                                 "activation (3x the algorithmic MACs: issued_tops); the attention runs bf16 "
+                                 "pairs. achieved counts the reference's int8 x fp32 MACs once"}}
 
 
 def batched_object(gathered, args, world):
@@ -324,13 +340,18 @@ def batched_object(gathered, args, world):
 
 
 def cpu_baseline(model_path, prompt):
+    """The reference CPU engine on this host: the b=1 workload at all threads (its own
+    DECODE_TPS) plus a bounded one-thread sample."""
     binary = os.path.join(ORACLE, "_ref", "minimind_cpu")
     cores = os.cpu_count()
     if os.path.exists(binary):
-        gen, tps, _ = run_reference_engine(model_path, prompt, 64, cores)
+        gen, tps, _ = run_reference_engine(model_path, prompt, NEW_TOKENS, cores)
+        _, tps1, _ = run_reference_engine(model_path, prompt, ONE_THREAD_TOKENS, 1)
         return {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
                 "sample": f"reference CPU engine (src/minimind.cpp, -O3 -fopenmp), {PROMPT_LEN}-token prompt + "
-                          f"64 greedy tokens, DECODE_TPS"}
+                          f"{NEW_TOKENS} greedy tokens, DECODE_TPS",
+                "one_thread": {"value": tps1, "unit": "tok/s", "cores": 1,
+                               "sample": f"{PROMPT_LEN}-token prompt + {ONE_THREAD_TOKENS} greedy tokens, DECODE_TPS"}}
     sys.path.insert(0, ORACLE)
     import numpy as np
     import oracle_py
@@ -340,6 +361,44 @@ def cpu_baseline(model_path, prompt):
     dt = time.perf_counter() - t0
     return {"value": 8 / dt, "unit": "tok/s", "cores": cores, "kind": "port",
             "sample": "oracle restatement, 34-token prompt + 8 tokens, prompt included"}
+
+
+def prefill_cpu_baseline(model_path):
+    """The reference engine's own prefill of the longest prompt it accepts next to one
+    generated token (prompt + n <= 1024, src/minimind.cpp:98): 1023 tokens, PREFILL_S."""
+    binary = os.path.join(ORACLE, "_ref", "minimind_cpu")
+    if not os.path.exists(binary):
+        return None
+    import mocha_q8
+    prompt = mocha_q8.random_prompt(PREFILL_LEN - 1, 1234)
+    cores = os.cpu_count()
+    m = run_reference_engine(model_path, prompt, 1, cores, metrics=True)
+    secs = float(m["PREFILL_S"])
+    return {"value": (PREFILL_LEN - 1) / secs, "unit": "tok/s", "cores": cores, "kind": "reference",
+            "prefill_s": secs,
+            "sample": f"reference CPU engine, one {PREFILL_LEN - 1}-token prompt with 1 generated token (its cap), "
+                      "prompt tokens / PREFILL_S"}
+
+
+def batched_cpu_baseline(model_path):
+    """The batched job on the reference engine: sequences run one after the other at all
+    threads, tok/s = generated tokens / wall time (WALL_S), over a bounded sample."""
+    binary = os.path.join(ORACLE, "_ref", "minimind_cpu")
+    if not os.path.exists(binary):
+        return None
+    import numpy as np
+    prompts = np.random.default_rng(2024).integers(0, 151936, (SERVE_SEQS, SERVE_PROMPT))
+    cores = os.cpu_count()
+    gen, wall = 0, 0.0
+    for i in range(SERVE_REF_SEQS):
+        m = run_reference_engine(model_path, prompts[i].tolist(), SERVE_NEW, cores,
+                                 sampling=("0.7", str(7 + i), "1.12", "40", "0.9"), metrics=True)
+        gen += int(m["GENERATED"])
+        wall += float(m["WALL_S"])
+    return {"value": gen / wall, "unit": "tok/s", "cores": cores, "kind": "reference",
+            "sample": f"reference CPU engine, sequences 0..{SERVE_REF_SEQS - 1} of the job run one after the "
+                      f"other ({SERVE_PROMPT}-token prompt + {SERVE_NEW} tokens, T 0.7, top-k 40, top-p 0.9, "
+                      "penalty 1.12), generated tokens / WALL_S"}
 
 
 def main():
@@ -439,6 +498,10 @@ def main():
         out["gguf"] = gguf_objects(gathered, args, world)
     if not args.no_cpu_baseline and "decode" in parts:
         out["cpu_baseline"] = cpu_baseline(path, mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED))
+    if not args.no_cpu_baseline and "prefill" in out:
+        out["prefill"]["cpu_baseline"] = prefill_cpu_baseline(path)
+    if not args.no_cpu_baseline and "batched" in out:
+        out["batched"]["cpu_baseline"] = batched_cpu_baseline(path)
     print(json.dumps(out))
     group.close()
     return 0

@@ -69,11 +69,15 @@ int mocha_q8_bench_decode(mocha_q8 *h, int token, int pos0, int pos_end, int war
 int mocha_q8_launches_per_step(mocha_q8 *h);
 
 /* Diagnostic: one persistent step (forward + projection) for `token` at `pos` that
- * records %globaltimer stamps of every CTA into stamps[148][320] (0 = not reached):
- * [0] start; per layer l at 2 + 12 l: +0 x_in gathered, +1 QKV done, +2 attention
- * done, +3 attention combined, +4 O done, +5 x_mid gathered, +9 gate/up chunks
- * resident, +10 gate/up input quantized, +7 SwiGLU done, +6 down partials stored,
- * +8 own rows reduced; [300] head start, [301] head done, [302] token drawn.
+ * records %globaltimer stamps of every CTA into stamps[148][640] (0 = not reached):
+ * [0] start; per layer l at 2 + 24 l: +0 x_in gathered, +11 QKV chunk taken, +12 its
+ * input normalised and quantized, +13 QKV products done, +1 QKV done, +14 query and
+ * K/V words arrived (attention CTAs), +15 past K/V resident, +16 split softmax and
+ * P.V done, +2 attention done, +17 partials gathered, +3 attention combined, +4 O
+ * done, +5 x_mid gathered, +9 gate/up chunks resident, +10 gate/up input quantized,
+ * +18 gate/up products done, +7 SwiGLU done, +19 SwiGLU slice quantized, +20 down
+ * chunk taken, +21 down products done, +6 down partials stored, +22 own rows polled,
+ * +8 own rows reduced; [578] head start, [579] head done, [580] token drawn.
  * Fails on the per-phase graph path. */
 int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *stamps);
 

@@ -854,19 +854,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         }
         // ---- QKV + bias + RoPE + KV write
         if (l > 0 && !gather<1>(c, xin_r, DIM, make_tag(epoch, l - 1, PH_X), S.xs)) return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * 12 + 0);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
             const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 11);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
             norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), 0);
             const int npair = hd.count;
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 12);
             const uint8_t *frag = w + sizeof(ChunkHdr);
             const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
             const float *bias = sc + 8 * kGroups;
             gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
             cbar();
             if (c.ct < npair) {
+                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 13);
                 const int pair = hd.first + c.ct;
                 const uint32_t tag = make_tag(epoch, l, PH_QKV);
                 int kind, t;
@@ -902,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             give_back(c, cur);
             remaining--;
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 1);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 1);
 
         // ---- attention: one split of one query head per CTA
         if (unit.head >= 0) {
@@ -930,6 +933,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     }
                 }
                 S.u.att.q[c.ct] = __uint_as_float((uint32_t)w);
+                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 14);
                 if (has_cur) {
                     S.u.att.k[np - 1][c.ct] = __uint_as_float((uint32_t)wk);
                     S.u.att.v[np - 1][c.ct] = __uint_as_float((uint32_t)wv);
@@ -937,6 +941,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             cp_async_wait_all();
             if (!cbar_and(ok)) return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 15);
             // Online softmax per warp: warp cw owns positions 8 cw .. 8 cw + 7 (lane & 7
             // picks the position, lane >> 3 the quarter of the 64 dims of its score); it
             // keeps its own max, sum of weights and 64 accumulators, and 64 threads merge
@@ -984,6 +989,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 }
             }
             cbar();
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 16);
             if (c.ct < HEAD_DIM) {
                 float mx = -INFINITY;
                 for (int w = 0; w < nw; w++) mx = fmaxf(mx, S.u.att.wp[w][0]);
@@ -1003,14 +1009,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             cbar();
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 2);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 2);
 
         // ---- O projection + residual: combine every head's splits, then the rows
         if (!gather_if<(kPartWords / 4 + kNT - 1) / kNT>(c, part_r, kPartWords, make_tag(epoch, l, PH_ATTN), S.u.part,
                                                        UsedSplit{splits}))
             return drain(c, cur);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 17);
         combine_quantize(&S, c.ct, splits);
-        stamp(a, cta, c.ct, 2 + l * 12 + 3);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 3);
         {
             const uint8_t *w = take(c, cur, OPROJ);
             if (!w) return drain(c, cur);
@@ -1027,16 +1034,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             give_back(c, cur);
             remaining--;
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 4);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
 
         // ---- RMSNorm -> gate/up -> SwiGLU
         if (!gather<1>(c, xmid_r, DIM, make_tag(epoch, l, PH_O), S.xs)) return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * 12 + 5);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
         {
             // this layer's gate/up chunks (2 or 3, all resident in the ring together):
             // slots cur.k .. cur.k + ngu - 1
+            // (a CTA without a spare piece has two: waiting for a third slot would wait
+            // for the down chunk behind them)
             int ngu = 0, T = 0;
-            while (ngu < 3 && ngu < remaining) {
+            const int want = has_spare(cta) ? 3 : 2;
+            while (ngu < want && ngu < remaining) {
                 if (!peek(c, cur, ngu)) return drain(c, cur);
                 const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + ngu) % kSlots]);
                 if (h->kind != GATEUP || h->layer != (uint32_t)l) break;
@@ -1052,9 +1062,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 return drain(c, cur);
             }
             const uint32_t s0 = cur.k % kSlots, s1 = (cur.k + 1) % kSlots, s2 = (cur.k + (ngu > 2 ? 2 : 0)) % kSlots;
-            stamp(a, cta, c.ct, 2 + l * 12 + 9);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 9);
             norm_quantize(&S, c.ct, reinterpret_cast<const float *>(S.ring[s0] + kGainOff), 0);
-            stamp(a, cta, c.ct, 2 + l * 12 + 10);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
             Tiles tl{{S.ring[s0] + sizeof(ChunkHdr), S.ring[s1] + sizeof(ChunkHdr), S.ring[s2] + sizeof(ChunkHdr)},
                      {nullptr, nullptr, nullptr},
                      T,
@@ -1065,6 +1075,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             tl.sc[2] = reinterpret_cast<const float *>(tl.frag[2] + (size_t)max(1, min(2, T - 4)) * kTileBytes);
             gemv_mma(&S, c.cw, c.lane, tl);
             cbar();
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 18);
             // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and
             // its up row 8 below; it lands at its column of down step 0 (own block) or 1
             if (c.ct < 8 * T) {
@@ -1080,17 +1091,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             cur.k += ngu;
             remaining -= ngu;
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 7);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 7);
         quantize_slice(c, nks);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 19);
         {
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
             for (;;) {
                 const uint8_t *w = take(c, cur, DOWN);
                 if (!w) return drain(c, cur);
+                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 20);
                 const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
                 const uint8_t *frag = w + sizeof(ChunkHdr);
                 const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
                 down_step(c, frag, sw, (int)hd.first, pacc);
+                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
                 const bool last = hd.first + 1 == hd.count;
                 if (last) {
                     // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
@@ -1113,7 +1127,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 if (last) break;
             }
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 6);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
         // reduce: warp r sums row xlo + r over the 148 CTAs (lane: CTAs 4 lane .. +3 and
         // 128 + 4 lane .. +3), then the butterfly; plus the residual x_mid
         {
@@ -1149,18 +1163,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     }
                 }
                 float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 22);
                 sum = mb::warp_sum(sum);
                 if (c.lane == 0) dw_store_rep(scr.xin + row, kStrideDim, S.xs[row] + sum, make_tag(epoch, l, PH_X));
             }
             if (!cbar_and(ok)) return drain(c, cur);
         }
-        stamp(a, cta, c.ct, 2 + l * 12 + 8);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
     }
 
     if (project) {
         // ---- final norm + tied head, logits kept in shared memory for selection
         if (!gather<1>(c, xin_r, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
-        stamp(a, cta, c.ct, 300);
+        stamp(a, cta, c.ct, kTraceHead);
         const int lo = a.P->head_lo[cta], n = a.P->head_lo[cta + 1] - lo;
         // the rest of this CTA's stream is its head chunks: 32 vocabulary rows (two
         // tiles) each, the last one shorter
@@ -1308,7 +1323,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     }
 
     // ---- end of step: the last CTA finishes the token
-    stamp(a, cta, c.ct, 301);
+    stamp(a, cta, c.ct, kTraceHead + 1);
     cbar();
     if (c.ct == 0) {
         __threadfence();
@@ -1355,7 +1370,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             a.b.st->token = a.prompt[pos + 1];
         }
     }
-    stamp(a, cta, c.ct, 302);
+    stamp(a, cta, c.ct, kTraceHead + 2);
     if (c.ct == 0) {
         a.b.st->steps++;
         a.sy->done = 0;

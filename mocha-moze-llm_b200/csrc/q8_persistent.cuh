@@ -85,7 +85,11 @@ int enqueue_step(const q8::Model *dm, const Plan *dplan, const q8::Buffers &b, S
                  int mode, const sampling::Params *prm, sampling::SeqState *seq, int *out_ring, int *out_count,
                  const int *prompt, unsigned *host_error, cudaStream_t s, unsigned long long *trace = nullptr);
 
-constexpr int kTraceStamps = 320;  // per CTA; see the stamp() points in the kernel
+// Trace stamps per CTA: [0] start, layer l's points at 2 + kTraceLayer * l + k (k < 23,
+// see the stamp() calls in the kernel), the head at kTraceHead + {0, 1, 2}.
+constexpr int kTraceLayer = 24;
+constexpr int kTraceHead = 2 + kTraceLayer * q8::LAYERS;  // 578
+constexpr int kTraceStamps = 640;
 
 int init_device();
 

@@ -7,6 +7,14 @@
 * ``qwen15b``: Qwen2.5-1.5B shapes (28 layers, 1536 hidden, 12/2 heads of 128, FFN 8960,
   vocab 151936, tied embeddings, QKV biases, RoPE base 1e6, RMSNorm eps 1e-6).
 
+Each file also carries a small byte-level BPE tokenizer in the ``tokenizer.ggml.*``
+metadata (``synthetic_tokenizer``): the 256 byte tokens, merges that spell a list of
+common English words, and the architecture's special tokens at their usual ids (Llama 3:
+``<|begin_of_text|>`` 128000 ... ``<|eot_id|>`` 128009, pre-tokenizer ``llama-bpe``, BOS
+added; Qwen2: ``<|endoftext|>`` 151643, ``<|im_start|>`` 151644, ``<|im_end|>`` 151645,
+pre-tokenizer ``qwen2``), so text prompts reach these random models the way they reach
+real ones.
+
 Tensor types follow the Q4_K_M mix of the benchmark configuration: Q4_K everywhere,
 Q6_K for ``token_embd`` and for ``attn_v`` / ``ffn_down`` of even layers, and (Qwen)
 Q8_0 for the bias-carrying ``attn_k``.  Norm gains are 1 + N(0, 0.01) and biases
@@ -130,6 +138,58 @@ def tensor_types(arch: Arch, layer: int) -> dict:
     }
 
 
+WORDS = ("the of and to in a is that for it as was with be by on not he this are or his from at which but "
+         "have an they you were her she there had been one all we can has their will would who more if no when "
+         "out so what up said about into than them only other time new some could these two may first then do "
+         "any like my now over such our man me even most made after also did many before must through back "
+         "years where much your way well down should because each just those people how too little state good "
+         "very make world still own see men work long get here between both life being under never day same "
+         "another know while last might us great old year off come since against go came right used take three "
+         "please introduce yourself briefly hello assistant user system model language answer question").split()
+
+LLAMA3_SPECIAL = {128000: "<|begin_of_text|>", 128001: "<|end_of_text|>", 128004: "<|finetune_right_pad_id|>",
+                  128006: "<|start_header_id|>", 128007: "<|end_header_id|>", 128008: "<|eom_id|>",
+                  128009: "<|eot_id|>", 128010: "<|python_tag|>"}
+QWEN2_SPECIAL = {151643: "<|endoftext|>", 151644: "<|im_start|>", 151645: "<|im_end|>"}
+
+
+def synthetic_tokenizer(arch: Arch):
+    """(tokens, token types, merges, {pre, bos, eos, add_bos}) of the models' tokenizer:
+    byte tokens 0..255 in GPT-2's byte alphabet, then one token per merge (the words of
+    WORDS and their space-prefixed forms, spelled left to right), unused fillers, and
+    the architecture's special tokens (type 3) at their usual ids."""
+    from gguf_tokenizer import byte_alphabet
+    alpha = byte_alphabet()
+    tokens = [alpha[b] for b in range(256)]
+    seen = set(tokens)
+    merges = []
+    for w in WORDS:
+        for form in (w, " " + w):
+            chars = "".join(alpha[b] for b in form.encode("utf-8"))
+            for k in range(1, len(chars)):
+                left, right = chars[:k], chars[k]
+                if chars[:k + 1] in seen:
+                    continue
+                merges.append(f"{left} {right}")
+                tokens.append(chars[:k + 1])
+                seen.add(chars[:k + 1])
+    types = [1] * len(tokens)
+    special = LLAMA3_SPECIAL if arch.gguf_arch == "llama" else QWEN2_SPECIAL
+    first = min(special)
+    tokens += [f"<|unused_{i}|>" for i in range(len(tokens), arch.vocab)]
+    types += [5] * (arch.vocab - len(types))
+    for i in range(first, arch.vocab):
+        if arch.gguf_arch == "llama" and i not in special:
+            tokens[i], types[i] = f"<|reserved_special_token_{i - first}|>", 3
+    for i, t in special.items():
+        tokens[i], types[i] = t, 3
+    if arch.gguf_arch == "llama":
+        meta = {"pre": "llama-bpe", "bos": 128000, "eos": 128009, "add_bos": True}
+    else:
+        meta = {"pre": "qwen2", "bos": 151643, "eos": 151645, "add_bos": False}
+    return tokens, types, merges, meta
+
+
 def write_model(path: str, arch_name: str, seed: int = 1) -> str:
     from gguf import GGMLQuantizationType, GGUFWriter
 
@@ -148,6 +208,15 @@ def write_model(path: str, arch_name: str, seed: int = 1) -> str:
     w.add_rope_dimension_count(arch.head_dim)
     w.add_vocab_size(arch.vocab)
     w.add_file_type(15)  # MOSTLY_Q4_K_M
+    tokens, types, merges, meta = synthetic_tokenizer(arch)
+    w.add_tokenizer_model("gpt2")
+    w.add_tokenizer_pre(meta["pre"])
+    w.add_token_list(tokens)
+    w.add_token_types(types)
+    w.add_token_merges(merges)
+    w.add_bos_token_id(meta["bos"])
+    w.add_eos_token_id(meta["eos"])
+    w.add_add_bos_token(meta["add_bos"])
 
     def add_q(name, qtype, rows, cols):
         w.add_tensor(name, random_matrix(rng, qtype, rows, cols), raw_dtype=GGMLQuantizationType(qtype))
@@ -187,7 +256,7 @@ def write_model(path: str, arch_name: str, seed: int = 1) -> str:
 def model_path(arch_name: str, seed: int = 1, cache_dir: str | None = None) -> str:
     cache_dir = cache_dir or os.environ.get("MOCHA_MODEL_CACHE") or "/tmp/mocha-b200-models"
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"{arch_name}-q4km-seed{seed}.gguf")
+    path = os.path.join(cache_dir, f"{arch_name}-q4km-seed{seed}-tok.gguf")
     if not os.path.exists(path):
         write_model(path, arch_name, seed)
     return path

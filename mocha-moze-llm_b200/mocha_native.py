@@ -185,9 +185,9 @@ class Q8Handle:
         return ms.value
 
     def trace_step(self, token: int, pos: int):
-        """%globaltimer stamps [148 CTAs][320] of one persistent step (see mocha_q8_trace_step)."""
+        """%globaltimer stamps [148 CTAs][640] of one persistent step (see mocha_q8_trace_step)."""
         import numpy as np
-        st = np.zeros((148, 320), dtype=np.uint64)
+        st = np.zeros((148, 640), dtype=np.uint64)
         if self.lib.mocha_q8_trace_step(self.h, token, pos, st.ctypes.data) != 0:
             raise RuntimeError("mocha_q8_trace_step failed")
         return st
