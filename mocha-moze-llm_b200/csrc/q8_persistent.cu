@@ -30,7 +30,10 @@
 // positions of each query head (K/V of past positions are prefetched with cp.async
 // before the query exists) -> O + residual -> RMSNorm -> gate/up + SwiGLU on this
 // CTA's own slice of the hidden units -> the down projection of that slice for all
-// 896 rows (split-K) -> each CTA sums the 148 partials of its own rows + residual.
+// 896 rows (split-K), added into one accumulator per row as 64-bit fixed point
+// (value * 2^32, red.add: integer sums do not depend on the order of arrival, so
+// the result is deterministic) -> an arrival counter -> every CTA reads the 896 sums
+// and adds them to its own copy of x_mid: the next layer's input, with no gather.
 // The vocabulary head is fused with the repetition penalty, the control mask and a
 // per-CTA top-k; the last CTA to finish (one atomic ticket) merges the candidates,
 // draws the token and advances the epoch.
@@ -76,7 +79,9 @@ constexpr int kStrideDim = replica_stride(DIM);
 constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
 static_assert(DIM % 64 == 0 && kCTAs % 4 == 0, "layout");
 
-enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_D = 3, PH_X = 4 };
+enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2 };
+constexpr float kFixScale = 4294967296.0f;     // 2^32: down partials as 64-bit fixed point
+constexpr float kFixInv = 1.0f / 4294967296.0f;
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
@@ -121,6 +126,11 @@ __host__ __device__ inline bool has_spare(int c) { return c >= kSpareFirst; }
 __host__ __device__ inline int spare_lo(int c) { return 32 * kCTAs + 8 * (c - kSpareFirst); }
 
 // ---- low-level primitives --------------------------------------------------
+
+// Error paths (a wait that has spun for a long time, a failed check) are kept out of
+// line: they never run on the hot path, and inlined copies of them would crowd the
+// per-layer loop out of the instruction caches.
+#define Q8P_COLD __device__ __noinline__
 
 MB_DEV uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -167,7 +177,7 @@ MB_DEV bool mbar_test(unsigned long long *bar, uint32_t parity)
 
 MB_DEV unsigned ld_volatile(const unsigned *p) { return *(const volatile unsigned *)p; }
 
-MB_DEV void fail(Sync *sy, unsigned *host_error, unsigned code)
+Q8P_COLD void fail(Sync *sy, unsigned *host_error, unsigned code)
 {
     atomicCAS(&sy->error, 0u, code);
     *(volatile unsigned *)host_error = code;
@@ -177,14 +187,19 @@ MB_DEV void fail(Sync *sy, unsigned *host_error, unsigned code)
 // A wait that has spun for `spun` cycles gives up when another CTA has recorded an
 // error -- read only once the wait is long, since the flag costs an L2 round trip --
 // or when the bound expires (recorded here with `code`).
-MB_DEV bool give_up(Sync *sy, unsigned *host_error, long long spun, unsigned code)
+Q8P_COLD bool give_up_slow(Sync *sy, unsigned *host_error, long long spun, unsigned code)
 {
-    if (spun < kErrorPollCycles) return false;
     if (spun > kTimeoutCycles) {
         fail(sy, host_error, code);
         return true;
     }
     return ld_volatile(&sy->error) != 0;
+}
+
+MB_DEV bool give_up(Sync *sy, unsigned *host_error, long long spun, unsigned code)
+{
+    if (spun < kErrorPollCycles) return false;
+    return give_up_slow(sy, host_error, spun, code);
 }
 
 MB_DEV bool mbar_wait(unsigned long long *bar, uint32_t parity, Sync *sy, unsigned *host_error)
@@ -238,6 +253,20 @@ MB_DEV unsigned long long dw_load(const unsigned long long *p)
     unsigned long long w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
+}
+
+// 64-bit fixed-point add (the result is not returned: a reduction in L2)
+MB_DEV void fix_add(unsigned long long *p, float v)
+{
+    const long long q = __float2ll_rn(v * kFixScale);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
+}
+
+MB_DEV unsigned long long ld_acquire_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 
 MB_DEV uint32_t make_tag(uint32_t epoch, int layer, int phase) { return (epoch << 8) | (layer << 3) | phase; }
@@ -801,12 +830,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const Model *M = a.M;
     const Scratch &scr = a.scr;
     // the copies of the broadcast arrays this CTA reads
-    const unsigned long long *xin_r = scr.xin + c.rep * kStrideDim;
     const unsigned long long *xmid_r = scr.xmid + c.rep * kStrideDim;
     const unsigned long long *part_r = scr.part + c.rep * kStridePart;
     const unsigned long long *kv_r = scr.kv + c.rep * kStrideKv;
     const int nks = has_spare(cta) ? 2 : 1;  // down-projection steps of this CTA
-    const int xlo = (int)((long long)DIM * cta / kCTAs), xn = (int)((long long)DIM * (cta + 1) / kCTAs) - xlo;
+    // the down-projection accumulators of this step (set epoch & 1); this CTA clears its
+    // share of the other set, which the next step uses (the last step that used it has
+    // finished: it was the previous launch on this stream)
+    const int set = (int)(epoch & 1u);
+    unsigned long long *dacc = scr.dacc + (size_t)set * LAYERS * DIM;
+    unsigned long long *dcnt = scr.dcnt + (size_t)set * LAYERS;
+    {
+        unsigned long long *other = scr.dacc + (size_t)(set ^ 1) * LAYERS * DIM;
+        const int lo = LAYERS * DIM * cta / kCTAs, hi = LAYERS * DIM * (cta + 1) / kCTAs;
+        for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) other[i] = 0ull;
+        if (cta == 0 && threadIdx.x < LAYERS) scr.dcnt[(size_t)(set ^ 1) * LAYERS + threadIdx.x] = 0ull;
+    }
     // B-fragment columns 3..7 stay zero; columns 0..2 are rewritten by every quantize
     for (int i = c.ct; i < kSteps * 32; i += kNT) S.bf[i >> 5][i & 31] = make_uint2(0u, 0u);
     for (int i = c.ct; i < 2 * 32; i += kNT) {
@@ -853,7 +892,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             asm volatile("cp.async.commit_group;" ::: "memory");
         }
         // ---- QKV + bias + RoPE + KV write
-        if (l > 0 && !gather<1>(c, xin_r, DIM, make_tag(epoch, l - 1, PH_X), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
             const uint8_t *w = take(c, cur, QKV);
@@ -1112,13 +1150,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     const int n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
                     const int g = c.lane >> 2;
                     const float f = S.sh;
-                    const uint32_t tag = make_tag(epoch, l, PH_D);
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         if (i < n && (c.lane & 3) == 0) {
                             const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
-                            dw_store(scr.pd + (size_t)r0 * kCTAs + cta, pacc[i][0] * f, tag);
-                            dw_store(scr.pd + (size_t)r1 * kCTAs + cta, pacc[i][1] * f, tag);
+                            fix_add(dacc + (size_t)l * DIM + r0, pacc[i][0] * f);
+                            fix_add(dacc + (size_t)l * DIM + r1, pacc[i][1] * f);
                         }
                     }
                 }
@@ -1128,53 +1165,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
-        // reduce: warp r sums row xlo + r over the 148 CTAs (lane: CTAs 4 lane .. +3 and
-        // 128 + 4 lane .. +3), then the butterfly; plus the residual x_mid
+        // all-reduce: this CTA's additions are complete before its arrival counts (the
+        // barrier in give_back orders every warp's before thread 0's fence); once all
+        // 148 have arrived every CTA reads the sums and adds them to its x_mid
         {
             int ok = 1;
-            if (c.cw < xn) {
-                const int row = xlo + c.cw;
-                const unsigned long long *src = scr.pd + (size_t)row * kCTAs;
-                const uint32_t tag = make_tag(epoch, l, PH_D);
-                const bool two = 128 + 4 * c.lane < kCTAs;
-                unsigned need = two ? 0xFFu : 0xFu;
-                float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                long long t0 = 0;
-                for (;;) {
-#pragma unroll
-                    for (int k = 0; k < 2; k++) {
-                        if (!(need >> (4 * k) & 0xFu)) continue;
-                        unsigned long long w4[4];
-                        dw_load4(src + 128 * k + 4 * c.lane, w4);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            if ((need >> (4 * k + j) & 1u) && (uint32_t)(w4[j] >> 32) == tag) {
-                                v[4 * k + j] = __uint_as_float((uint32_t)w4[j]);
-                                need &= ~(1u << (4 * k + j));
-                            }
+            if (c.ct == 0) {
+                unsigned long long *cnt = dcnt + l;
+                __threadfence();
+                atomicAdd(cnt, 1ull);
+                if (ld_acquire_u64(cnt) < (unsigned long long)kCTAs) {
+                    const long long t0 = clock64();
+                    while (ld_acquire_u64(cnt) < (unsigned long long)kCTAs) {
+                        if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
+                            ok = 0;
+                            break;
                         }
                     }
-                    if (!need) break;
-                    if (t0 == 0) {
-                        t0 = clock64();
-                    } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
-                        ok = 0;
-                        break;
-                    }
                 }
-                float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 22);
-                sum = mb::warp_sum(sum);
-                if (c.lane == 0) dw_store_rep(scr.xin + row, kStrideDim, S.xs[row] + sum, make_tag(epoch, l, PH_X));
             }
             if (!cbar_and(ok)) return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 22);
+            if (c.ct < DIM / 4) {
+                unsigned long long v[4];
+                dw_load4(dacc + (size_t)l * DIM + 4 * c.ct, v);
+                float4 x = *reinterpret_cast<const float4 *>(S.xs + 4 * c.ct);
+                x.x += __ll2float_rn((long long)v[0]) * kFixInv;
+                x.y += __ll2float_rn((long long)v[1]) * kFixInv;
+                x.z += __ll2float_rn((long long)v[2]) * kFixInv;
+                x.w += __ll2float_rn((long long)v[3]) * kFixInv;
+                *reinterpret_cast<float4 *>(S.xs + 4 * c.ct) = x;
+            }
+            cbar();
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
     }
 
     if (project) {
         // ---- final norm + tied head, logits kept in shared memory for selection
-        if (!gather<1>(c, xin_r, DIM, make_tag(epoch, LAYERS - 1, PH_X), S.xs)) return drain(c, cur);
         stamp(a, cta, c.ct, kTraceHead);
         const int lo = a.P->head_lo[cta], n = a.P->head_lo[cta + 1] - lo;
         // the rest of this CTA's stream is its head chunks: 32 vocabulary rows (two
@@ -1374,7 +1402,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     if (c.ct == 0) {
         a.b.st->steps++;
         a.sy->done = 0;
-        const unsigned next = epoch + 1 >= (1u << 24) ? 1u : epoch + 1;
+        // wraps to 2: the accumulator set (epoch & 1) keeps alternating
+        const unsigned next = epoch + 1 >= (1u << 24) ? 2u : epoch + 1;
         __threadfence();
         atomicExch(&a.sy->epoch, next);
     }
@@ -1393,7 +1422,8 @@ size_t smem_bytes() { return sizeof(Smem); }
 
 size_t scratch_words()
 {
-    return (size_t)DIM + (size_t)kReplicas * (kStrideKv + kStridePart + 2 * kStrideDim) + (size_t)DIM * kCTAs;
+    return (size_t)DIM + (size_t)kReplicas * (kStrideKv + kStridePart + kStrideDim) + 2 * (size_t)LAYERS * DIM +
+           2 * (size_t)LAYERS;
 }
 
 void carve_scratch(unsigned long long *base, Scratch *scr)
@@ -1402,8 +1432,8 @@ void carve_scratch(unsigned long long *base, Scratch *scr)
     scr->kv = scr->q + DIM;
     scr->part = scr->kv + kReplicas * kStrideKv;
     scr->xmid = scr->part + kReplicas * kStridePart;
-    scr->xin = scr->xmid + kReplicas * kStrideDim;
-    scr->pd = scr->xin + kReplicas * kStrideDim;
+    scr->dacc = scr->xmid + kReplicas * kStrideDim;
+    scr->dcnt = scr->dacc + 2 * (size_t)LAYERS * DIM;
 }
 
 int init_device()

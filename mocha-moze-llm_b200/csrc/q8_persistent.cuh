@@ -65,8 +65,9 @@ struct Scratch {
     unsigned long long *kv;       // [kReplicas][KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
     unsigned long long *part;     // [kReplicas][HEADS][kMaxSplit][ATTN_PARTIAL] attention partials
     unsigned long long *xmid;     // [kReplicas][DIM] residual after attention
-    unsigned long long *xin;      // [kReplicas][DIM] residual after the FFN (input of the next layer)
-    unsigned long long *pd;       // [DIM][kCTAs] down-projection partial sums: row r, CTA c
+    unsigned long long *dacc;     // [2][LAYERS][DIM] down-projection sums, 64-bit fixed point (value * 2^32),
+                                  // two sets used by alternating steps (epoch & 1)
+    unsigned long long *dcnt;     // [2][LAYERS] CTAs whose down additions are complete
     unsigned long long *cand;     // [kCTAs][64] per-CTA candidate keys (plain)
 };
 
