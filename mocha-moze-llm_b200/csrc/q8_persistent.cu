@@ -28,12 +28,16 @@
 // phases; each reader waits exactly for the words it needs.
 // Per layer: QKV (+bias, split-half RoPE, KV write) -> attention split over the
 // positions of each query head (K/V of past positions are prefetched with cp.async
-// before the query exists) -> O + residual -> RMSNorm -> gate/up + SwiGLU on this
+// before the query exists); each split projects its unnormalised output through the
+// head's 64 columns of O, the splits of a head exchange their (max, sum of weights)
+// and scale their projection to the head's softmax, and the 896 rows are all-reduced
+// like the down projection below -> x_mid in every CTA -> RMSNorm -> gate/up + SwiGLU on this
 // CTA's own slice of the hidden units -> the down projection of that slice for all
 // 896 rows (split-K), added into one accumulator per row as 64-bit fixed point
 // (value * 2^32, red.add: integer sums do not depend on the order of arrival, so
-// the result is deterministic) -> an arrival counter -> every CTA reads the 896 sums
-// and adds them to its own copy of x_mid: the next layer's input, with no gather.
+// the result is deterministic) whose low byte counts the additions -> every CTA polls
+// the 896 accumulators until each holds all 148 additions and adds the sums to its
+// own copy of x_mid: the next layer's input, with no gather.
 // The vocabulary head is fused with the repetition penalty, the control mask and a
 // per-CTA top-k; the last CTA to finish (one atomic ticket) merges the candidates,
 // draws the token and advances the epoch.
@@ -70,25 +74,28 @@ constexpr int kGateupPerChunk = 16;            // hidden units per gate/up chunk
 constexpr int kHeadPerChunk = 32;              // vocabulary rows per head chunk (two tiles)
 constexpr int kHeadSlice = 1040;               // >= ceil(VOCAB / kCTAs)
 constexpr int kDownTiles = DIM / 16;           // 56 row tiles of the down projection
-constexpr int kPartWords = HEADS * kMaxSplit * ATTN_PARTIAL;
+constexpr int kPartWords = HEADS * kMaxSplit * 2;   // (max, sum of weights) of every attention split
+constexpr int kOStepBytes = kDownTiles * 512;        // one 32-column step of a head's O columns, all 896 rows
+constexpr int kOHeadBytes = 2 * kOStepBytes;
 constexpr int kGpStride = kConsumerWarps + 1;  // padded: conflict-free row sums
 constexpr int kKStride = HEAD_DIM + 4;         // cached key row in shared memory: conflict-free float4 reads
 constexpr int kStrideKv = replica_stride(2 * KV);
-constexpr int kStridePart = replica_stride(kPartWords);
-constexpr int kStrideDim = replica_stride(DIM);
 constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
 static_assert(DIM % 64 == 0 && kCTAs % 4 == 0, "layout");
 
-enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2 };
-constexpr float kFixScale = 4294967296.0f;     // 2^32: down partials as 64-bit fixed point
+enum Phase { PH_QKV = 0, PH_ATTN = 1 };
+constexpr float kFixScale = 4294967296.0f;     // 2^32: partial sums as fixed point ...
 constexpr float kFixInv = 1.0f / 4294967296.0f;
+// ... in bits 8..63 of an accumulator word; bits 0..7 count the additions (< 256), so a
+// reader sees from the word alone when every contributor's addition has landed.  Each
+// addition is (q << 8) + 1, q = rint(v * 2^32): the low byte only ever gains the +1s,
+// and the sum is the word shifted right arithmetically by 8 (|sum| < 2^23 fits).
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
     __align__(16) float xs[DIM];  // residual (x_in, then x_mid) of the current layer
     __align__(16) float ns[DIM];  // normalised input / attention output
     union __align__(16) {
-        float part[kPartWords];    // gathered attention partials
         struct {
             float k[kAttnLenMax][kKStride];
             float v[kAttnLenMax][HEAD_DIM];
@@ -99,6 +106,10 @@ struct Smem {
     } u;
     __align__(16) uint2 bf[kSteps][32];  // B fragments of the current 896-wide input (lanes 12..31 zero)
     __align__(16) uint2 bfh[2][32];      // B fragments of the SwiGLU slice (lanes 12..31 zero)
+    __align__(16) uint2 bfo[2][32];      // B fragments of this split's attention output (64 dims)
+    __align__(16) float ost[2][32];      // that output, unnormalised, before quantization
+    float so;                            // its scale / 254
+    float att_m, att_l, att_w;           // this split's max and sum of weights; its weight in the head
     float gp[5 * 16][kGpStride];   // per-warp partial row sums of the current job (<= 5 tiles)
     float sxs[kGroups];            // input scale / 254 per group
     __align__(16) float hst[2][32];  // this CTA's SwiGLU outputs at their column in each down step
@@ -255,18 +266,11 @@ MB_DEV unsigned long long dw_load(const unsigned long long *p)
     return w;
 }
 
-// 64-bit fixed-point add (the result is not returned: a reduction in L2)
+// one counted fixed-point addition (the result is not returned: a reduction in L2)
 MB_DEV void fix_add(unsigned long long *p, float v)
 {
-    const long long q = __float2ll_rn(v * kFixScale);
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
-}
-
-MB_DEV unsigned long long ld_acquire_u64(const unsigned long long *p)
-{
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
+    const unsigned long long q = (unsigned long long)__float2ll_rn(v * kFixScale);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((q << 8) + 1ull) : "memory");
 }
 
 MB_DEV uint32_t make_tag(uint32_t epoch, int layer, int phase) { return (epoch << 8) | (layer << 3) | phase; }
@@ -291,65 +295,6 @@ MB_DEV void dw_load4(const unsigned long long *p, unsigned long long (&v)[4])
                  : "=l"(v[0]), "=l"(v[1]), "=l"(v[2]), "=l"(v[3])
                  : "l"(p)
                  : "memory");
-}
-
-// Poll the data words src[0..n) (n a multiple of 4, src 32-byte aligned) that `want`
-// selects until each carries `tag`, storing their floats to dst.  Thread ct owns the
-// 4-word groups ct, ct+kNT, ...; each request covers a whole group and only groups
-// with missing words are polled again, back to back: the exchange is bound by how
-// soon a reader sees the last word, not by the polling traffic (the words have four
-// replicas).  Every consumer thread returns the same verdict.
-template <int E, typename Want>
-MB_DEV bool gather_if(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst, Want want)
-{
-    const int ng = n >> 2;
-    unsigned need[E];
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        const int g = c.ct + e * kNT;
-        need[e] = 0;
-        if (g < ng)
-#pragma unroll
-            for (int j = 0; j < 4; j++) need[e] |= want(4 * g + j) ? (1u << j) : 0u;
-    }
-    int ok = 1;
-    long long t0 = 0;
-    for (;;) {
-        unsigned missing = 0;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            if (!need[e]) continue;
-            const int g = c.ct + e * kNT;
-            unsigned long long v[4];
-            dw_load4(src + 4 * g, v);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if ((need[e] >> j & 1u) && (uint32_t)(v[j] >> 32) == tag) {
-                    dst[4 * g + j] = __uint_as_float((uint32_t)v[j]);
-                    need[e] &= ~(1u << j);
-                }
-            }
-            missing |= need[e];
-        }
-        if (!missing) break;
-        if (t0 == 0) {
-            t0 = clock64();
-        } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
-            ok = 0;
-            break;
-        }
-    }
-    return cbar_and(ok) != 0;
-}
-
-struct All {
-    MB_DEV bool operator()(int) const { return true; }
-};
-
-template <int E>
-MB_DEV bool gather(Ctx &c, const unsigned long long *src, int n, uint32_t tag, float *dst)
-{
-    return gather_if<E>(c, src, n, tag, dst, All{});
 }
 
 // ---- int8 tensor-core matrix-vector products ------------------------------------
@@ -451,40 +396,15 @@ MB_DEV void norm_quantize(Smem *Sp, int ct, const float *gain, int keep)
     cbar();
 }
 
-// Combine of the attention splits gathered in S.u.part (per head: running max, sum of
-// weights, 64 accumulators per split), quantized straight into S.bf / S.sxs.  Thread
-// t < 224 owns four consecutive output columns, all of one head.
-MB_DEV void combine_quantize(Smem *Sp, int ct, int splits)
-{
-    Smem &S = *Sp;
-    if (ct < 256) {
-        const int t = min(ct, 223), col = quant_col(t), hd = col / HEAD_DIM, d = col % HEAD_DIM;
-        const float *p = S.u.part + (size_t)hd * kMaxSplit * ATTN_PARTIAL;
-        float mx = -INFINITY;
-        for (int s = 0; s < splits; s++) mx = fmaxf(mx, p[s * ATTN_PARTIAL]);
-        float lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int s = 0; s < splits; s++) {
-            const float wgt = expf(p[s * ATTN_PARTIAL] - mx);
-            lsum = fmaf(wgt, p[s * ATTN_PARTIAL + 1], lsum);
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[j] = fmaf(wgt, p[s * ATTN_PARTIAL + 2 + d + j], acc[j]);
-        }
-        const float n[4] = {acc[0] / lsum, acc[1] / lsum, acc[2] / lsum, acc[3] / lsum};
-        float m = fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3])));
-        m = group_max16(m);
-        if (ct < 224) put_limbs(S, t, n, m);
-    }
-    cbar();
-}
-
-// S.hst[ks][0..32) for ks < nks (one scale for all) -> S.bfh and S.sh; warp 0.
-MB_DEV void quantize_slice(Ctx &c, int nks)
+// src[ks][0..32) for ks < nks (one scale for all) -> B fragments bf[ks] and the scale
+// / 254; warp 0.
+MB_DEV void quantize_slice(Ctx &c, const float (*src)[32], int nks, uint2 (*bf)[32], float *scale)
 {
     if (c.cw == 0) {
         const int t = c.lane & 15, ks = t >> 3, tig = (t >> 1) & 3, h = t & 1;
         const bool live = c.lane < 16 && ks < nks;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = *reinterpret_cast<const float4 *>(&c.S.hst[ks][16 * h + 4 * tig]);
+        if (live) v = *reinterpret_cast<const float4 *>(&src[ks][16 * h + 4 * tig]);
         float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         m = mb::warp_max(m);
         const float inv = m > 0.f ? 127.f / m : 0.f;
@@ -492,12 +412,12 @@ MB_DEV void quantize_slice(Ctx &c, int nks)
         uint32_t p0, p1, p2;
         limbs4(q, p0, p1, p2);
         if (live) {
-            uint32_t *b = reinterpret_cast<uint32_t *>(&c.S.bfh[ks][0]);
+            uint32_t *b = reinterpret_cast<uint32_t *>(&bf[ks][0]);
             b[2 * tig + h] = p0;
             b[2 * (4 + tig) + h] = p1;
             b[2 * (8 + tig) + h] = p2;
         }
-        if (c.lane == 0) c.S.sh = m / (127.f * 254.f);
+        if (c.lane == 0) *scale = m / (127.f * 254.f);
     }
     cbar();
 }
@@ -603,10 +523,10 @@ MB_DEV float row_sum(const Ctx &c, int T, int row)
 // Down projection, one 32-column step of this CTA's hidden units for all 896 rows
 // ([kDownTiles][32 lanes][16 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
 // partials (v * weight scale) are added to acc[tile][row g | row g + 8].
-MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, int ks, float (&acc)[4][2])
+MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float (&acc)[4][2])
 {
     const int t0 = kDownTiles * c.cw / kConsumerWarps, n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
-    const uint2 b = c.S.bfh[ks][c.lane];
+    const uint2 b = bfs[c.lane];
     const int g = c.lane >> 2;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -625,6 +545,36 @@ MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, int ks, floa
 MB_DEV size_t kv_index(int layer, int kvh, int pos)
 {
     return (((size_t)layer * KV_HEADS + kvh) * CONTEXT + pos) * HEAD_DIM;
+}
+
+// S.xs += the 896 counted fixed-point sums at acc once each holds `count` additions:
+// thread t < 224 polls its four words (one 32-byte request per round).  Every consumer
+// thread returns the same verdict (ends with a barrier).
+MB_DEV bool add_sums(Ctx &c, const unsigned long long *acc, unsigned count)
+{
+    int ok = 1;
+    if (c.ct < DIM / 4) {
+        unsigned long long v[4];
+        dw_load4(acc + 4 * c.ct, v);
+        long long t0 = 0;
+        while ((unsigned)(v[0] & 0xFFu) != count || (unsigned)(v[1] & 0xFFu) != count ||
+               (unsigned)(v[2] & 0xFFu) != count || (unsigned)(v[3] & 0xFFu) != count) {
+            if (t0 == 0) {
+                t0 = clock64();
+            } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
+                ok = 0;
+                break;
+            }
+            dw_load4(acc + 4 * c.ct, v);
+        }
+        float4 x = *reinterpret_cast<const float4 *>(c.S.xs + 4 * c.ct);
+        x.x += __ll2float_rn((long long)v[0] >> 8) * kFixInv;
+        x.y += __ll2float_rn((long long)v[1] >> 8) * kFixInv;
+        x.z += __ll2float_rn((long long)v[2] >> 8) * kFixInv;
+        x.w += __ll2float_rn((long long)v[3] >> 8) * kFixInv;
+        *reinterpret_cast<float4 *>(c.S.xs + 4 * c.ct) = x;
+    }
+    return cbar_and(ok) != 0;
 }
 
 // ---- the kernel ---------------------------------------------------------------
@@ -667,7 +617,6 @@ MB_DEV const uint8_t *take(Ctx &c, Cursor &cur, uint32_t kind)
     const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(w);
     bool ok = h->kind == kind && h->count >= 1;
     if (kind == QKV) ok = ok && h->count <= 4;
-    if (kind == OPROJ) ok = ok && h->count <= 8;
     if (kind == GATEUP) ok = ok && (h->count == 8 || h->count == (uint32_t)kGateupPerChunk);
     if (kind == HEAD) ok = ok && h->count <= (uint32_t)kHeadPerChunk;
     if (kind == DOWN) ok = ok && h->count <= 2 && h->first < h->count;
@@ -770,11 +719,6 @@ struct AttnUnit {
     int head, split, p0, np;
 };
 
-struct UsedSplit {
-    int splits;
-    MB_DEV bool operator()(int i) const { return (i / ATTN_PARTIAL) % kMaxSplit < splits; }
-};
-
 __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -830,8 +774,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const Model *M = a.M;
     const Scratch &scr = a.scr;
     // the copies of the broadcast arrays this CTA reads
-    const unsigned long long *xmid_r = scr.xmid + c.rep * kStrideDim;
-    const unsigned long long *part_r = scr.part + c.rep * kStridePart;
     const unsigned long long *kv_r = scr.kv + c.rep * kStrideKv;
     const int nks = has_spare(cta) ? 2 : 1;  // down-projection steps of this CTA
     // the down-projection accumulators of this step (set epoch & 1); this CTA clears its
@@ -839,12 +781,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     // finished: it was the previous launch on this stream)
     const int set = (int)(epoch & 1u);
     unsigned long long *dacc = scr.dacc + (size_t)set * LAYERS * DIM;
-    unsigned long long *dcnt = scr.dcnt + (size_t)set * LAYERS;
+    unsigned long long *xacc = scr.xacc + (size_t)set * LAYERS * DIM;
     {
-        unsigned long long *other = scr.dacc + (size_t)(set ^ 1) * LAYERS * DIM;
+        unsigned long long *od = scr.dacc + (size_t)(set ^ 1) * LAYERS * DIM;
+        unsigned long long *ox = scr.xacc + (size_t)(set ^ 1) * LAYERS * DIM;
         const int lo = LAYERS * DIM * cta / kCTAs, hi = LAYERS * DIM * (cta + 1) / kCTAs;
-        for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) other[i] = 0ull;
-        if (cta == 0 && threadIdx.x < LAYERS) scr.dcnt[(size_t)(set ^ 1) * LAYERS + threadIdx.x] = 0ull;
+        for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) {
+            od[i] = 0ull;
+            ox[i] = 0ull;
+        }
     }
     // B-fragment columns 3..7 stay zero; columns 0..2 are rewritten by every quantize
     for (int i = c.ct; i < kSteps * 32; i += kNT) S.bf[i >> 5][i & 31] = make_uint2(0u, 0u);
@@ -890,6 +835,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 cp_async16(&S.u.att.v[p][q4 * 4], vb + p * HEAD_DIM + q4 * 4);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
+            // this head's O columns and scales, wanted after the attention: into L2 now
+            if (c.ct == 0) {
+                const uint8_t *of = a.P->ofrag + (size_t)(l * HEADS + unit.head) * kOHeadBytes;
+                const float *os = a.P->oscale + (size_t)(l * HEADS + unit.head) * DIM;
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(of), "r"(kOHeadBytes) : "memory");
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(os), "r"(DIM * 4) : "memory");
+            }
         }
         // ---- QKV + bias + RoPE + KV write
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
@@ -951,6 +903,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             const int h = unit.head, kvh = h / GQA, np = unit.np;
             const bool has_cur = unit.p0 + np == pos + 1;
             const unsigned long long ready = (unsigned long long)tag << 32;
+            // this warp's tiles of the head's O columns (both 32-column steps) and their
+            // rows' scales, loaded now so the projection after the softmax waits for nothing
+            const int ot0 = kDownTiles * c.cw / kConsumerWarps, otn = kDownTiles * (c.cw + 1) / kConsumerWarps - ot0;
+            uint4 ofr[2][4];
+            float osc[4][2];
+            {
+                const uint8_t *of = a.P->ofrag + (size_t)(l * HEADS + h) * kOHeadBytes;
+                const float *os = a.P->oscale + (size_t)(l * HEADS + h) * DIM;
+                const int g = c.lane >> 2;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int ti = min(ot0 + i, kDownTiles - 1);
+#pragma unroll
+                    for (int ks = 0; ks < 2; ks++)
+                        ofr[ks][i] = __ldcg(reinterpret_cast<const uint4 *>(of + ks * kOStepBytes +
+                                                                            ((size_t)ti * 32 + c.lane) * 16));
+                    osc[i][0] = __ldcg(os + 16 * ti + g);
+                    osc[i][1] = __ldcg(os + 16 * ti + g + 8);
+                }
+            }
             // the query of this head, and this position's K/V when the split holds it
             int ok = 1;
             if (c.ct < HEAD_DIM) {
@@ -1037,46 +1009,94 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     lsum = fmaf(f, S.u.att.wp[w][1], lsum);
                     acc = fmaf(f, S.u.att.wp[w][2 + c.ct], acc);
                 }
-                const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
-                unsigned long long *out = scr.part + ((size_t)h * kMaxSplit + unit.split) * ATTN_PARTIAL;
-                dw_store_rep(out + 2 + c.ct, kStridePart, acc, ptag);
+                S.ost[c.ct >> 5][c.ct & 31] = acc;
                 if (c.ct == 0) {
-                    dw_store_rep(out, kStridePart, mx, ptag);
-                    dw_store_rep(out + 1, kStridePart, lsum, ptag);
+                    S.att_m = mx;
+                    S.att_l = lsum;
+                    if (splits > 1) {  // for the other splits of this head
+                        const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
+                        unsigned long long *ml = scr.part + 2 * ((size_t)h * kMaxSplit + unit.split);
+                        dw_store(ml, mx, ptag);
+                        dw_store(ml + 1, lsum, ptag);
+                    }
+                }
+            }
+            cbar();
+            quantize_slice(c, S.ost, 2, S.bfo, &S.so);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 3);
+            // warp 0 starts reading the splits' (max, sum) before the products
+            const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
+            const unsigned long long *ml = scr.part + 2 * ((size_t)h * kMaxSplit + min(c.lane, splits - 1));
+            unsigned long long w0 = 0, w1 = 0;
+            if (c.cw == 0 && splits > 1) {
+                w0 = dw_load(ml);
+                w1 = dw_load(ml + 1);
+            }
+            // the unnormalised output through O's 64 columns of this head: P = O_h acc
+            float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (i < otn) {
+#pragma unroll
+                    for (int ks = 0; ks < 2; ks++) {
+                        int d[4] = {0, 0, 0, 0};
+                        mma_s8(d, ofr[ks][i], S.bfo[ks][c.lane]);
+                        float v0, v1;
+                        combine(d, v0, v1);
+                        pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
+                        pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
+                    }
+                }
+            }
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
+            // this split's weight in the head's softmax: exp(m - M) / L over the splits
+            if (c.cw == 0) {
+                float wgt = 0.f;
+                if (splits == 1) {
+                    wgt = 1.0f / S.att_l;
+                } else {
+                    if (c.lane < splits && ((uint32_t)(w0 >> 32) != ptag || (uint32_t)(w1 >> 32) != ptag)) {
+                        const long long t0 = clock64();
+                        while ((uint32_t)(w0 >> 32) != ptag || (uint32_t)(w1 >> 32) != ptag) {
+                            if ((uint32_t)(w0 >> 32) != ptag) w0 = dw_load(ml);
+                            if ((uint32_t)(w1 >> 32) != ptag) w1 = dw_load(ml + 1);
+                            if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
+                                ok = 0;
+                                break;
+                            }
+                        }
+                    }
+                    const float m = c.lane < splits ? __uint_as_float((uint32_t)w0) : -INFINITY;
+                    const float lv = c.lane < splits ? __uint_as_float((uint32_t)w1) : 0.f;
+                    const float M = mb::warp_max(m);
+                    const float L = mb::warp_sum(c.lane < splits ? expf(m - M) * lv : 0.f);
+                    wgt = expf(S.att_m - M) / L;
+                }
+                if (c.lane == 0) S.att_w = wgt;
+            }
+            if (!cbar_and(ok)) return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 23);
+            {
+                const float f = S.so * S.att_w;
+                const int g = c.lane >> 2;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    if (i < otn && (c.lane & 3) == 0) {
+                        const int r0 = 16 * (ot0 + i) + g, r1 = r0 + 8;
+                        fix_add(xacc + (size_t)l * DIM + r0, pacc[i][0] * f);
+                        fix_add(xacc + (size_t)l * DIM + r1, pacc[i][1] * f);
+                    }
                 }
             }
             cbar();
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 2);
 
-        // ---- O projection + residual: combine every head's splits, then the rows
-        if (!gather_if<(kPartWords / 4 + kNT - 1) / kNT>(c, part_r, kPartWords, make_tag(epoch, l, PH_ATTN), S.u.part,
-                                                       UsedSplit{splits}))
-            return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 17);
-        combine_quantize(&S, c.ct, splits);
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 3);
-        {
-            const uint8_t *w = take(c, cur, OPROJ);
-            if (!w) return drain(c, cur);
-            const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            const int R = hd.count;
-            const uint8_t *frag = w + sizeof(ChunkHdr);
-            const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
-            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
-            cbar();
-            if (c.ct < R) {
-                const int row = hd.first + c.ct;
-                dw_store_rep(scr.xmid + row, kStrideDim, S.xs[row] + row_sum(c, 1, c.ct), make_tag(epoch, l, PH_O));
-            }
-            give_back(c, cur);
-            remaining--;
-        }
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
+        // ---- x_mid = x_in + the attention block, all-reduced over the attention CTAs
+        if (!add_sums(c, xacc + (size_t)l * DIM, (unsigned)(HEADS * splits))) return drain(c, cur);
+        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
 
         // ---- RMSNorm -> gate/up -> SwiGLU
-        if (!gather<1>(c, xmid_r, DIM, make_tag(epoch, l, PH_O), S.xs)) return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
         {
             // this layer's gate/up chunks (2 or 3, all resident in the ring together):
             // slots cur.k .. cur.k + ngu - 1
@@ -1130,7 +1150,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             remaining -= ngu;
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 7);
-        quantize_slice(c, nks);
+        quantize_slice(c, S.hst, nks, S.bfh, &S.sh);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 19);
         {
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
@@ -1141,7 +1161,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
                 const uint8_t *frag = w + sizeof(ChunkHdr);
                 const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
-                down_step(c, frag, sw, (int)hd.first, pacc);
+                down_step(c, frag, sw, S.bfh[hd.first], pacc);
                 stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
                 const bool last = hd.first + 1 == hd.count;
                 if (last) {
@@ -1165,39 +1185,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
-        // all-reduce: this CTA's additions are complete before its arrival counts (the
-        // barrier in give_back orders every warp's before thread 0's fence); once all
-        // 148 have arrived every CTA reads the sums and adds them to its x_mid
-        {
-            int ok = 1;
-            if (c.ct == 0) {
-                unsigned long long *cnt = dcnt + l;
-                __threadfence();
-                atomicAdd(cnt, 1ull);
-                if (ld_acquire_u64(cnt) < (unsigned long long)kCTAs) {
-                    const long long t0 = clock64();
-                    while (ld_acquire_u64(cnt) < (unsigned long long)kCTAs) {
-                        if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
-                            ok = 0;
-                            break;
-                        }
-                    }
-                }
-            }
-            if (!cbar_and(ok)) return drain(c, cur);
-            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 22);
-            if (c.ct < DIM / 4) {
-                unsigned long long v[4];
-                dw_load4(dacc + (size_t)l * DIM + 4 * c.ct, v);
-                float4 x = *reinterpret_cast<const float4 *>(S.xs + 4 * c.ct);
-                x.x += __ll2float_rn((long long)v[0]) * kFixInv;
-                x.y += __ll2float_rn((long long)v[1]) * kFixInv;
-                x.z += __ll2float_rn((long long)v[2]) * kFixInv;
-                x.w += __ll2float_rn((long long)v[3]) * kFixInv;
-                *reinterpret_cast<float4 *>(S.xs + 4 * c.ct) = x;
-            }
-            cbar();
-        }
+        // all-reduce: once all 148 CTAs' additions are complete every CTA adds the sums
+        // to its x_mid -- the next layer's input
+        if (!add_sums(c, dacc + (size_t)l * DIM, kCTAs)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
     }
 
@@ -1422,8 +1412,7 @@ size_t smem_bytes() { return sizeof(Smem); }
 
 size_t scratch_words()
 {
-    return (size_t)DIM + (size_t)kReplicas * (kStrideKv + kStridePart + kStrideDim) + 2 * (size_t)LAYERS * DIM +
-           2 * (size_t)LAYERS;
+    return (size_t)DIM + (size_t)kReplicas * kStrideKv + kPartWords + 4 * (size_t)LAYERS * DIM;
 }
 
 void carve_scratch(unsigned long long *base, Scratch *scr)
@@ -1431,9 +1420,9 @@ void carve_scratch(unsigned long long *base, Scratch *scr)
     scr->q = base;
     scr->kv = scr->q + DIM;
     scr->part = scr->kv + kReplicas * kStrideKv;
-    scr->xmid = scr->part + kReplicas * kStridePart;
-    scr->dacc = scr->xmid + kReplicas * kStrideDim;
-    scr->dcnt = scr->dacc + 2 * (size_t)LAYERS * DIM;
+    scr->dacc = scr->part + kPartWords;
+    scr->xacc = scr->dacc + 2 * (size_t)LAYERS * DIM;
+
 }
 
 int init_device()
@@ -1560,12 +1549,6 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
                 bias[2 * j + 1] = bv[r0 + 32];
             }
             if (!emit896(QKV, l, lo, hi - lo, rows, bias, lt[ATTN_NORM].data)) return 1;
-            // O: this CTA's residual rows
-            rows.assign(8, none);
-            split(DIM, kCTAs, c, lo, hi);
-            if (hi - lo > 8) return 1;
-            for (int r = lo; r < hi; r++) rows[r - lo] = {&lt[WO], r};
-            if (!emit896(OPROJ, l, lo, hi - lo, rows, {}, 0)) return 1;
             // gate/up: tiles of 8 gate rows then the 8 up rows of the same hidden units;
             // the CTA's block in two chunks, then its spare piece (one tile)
             std::vector<std::pair<int, int>> pieces = {{32 * c, 16}, {32 * c + 16, 16}};
@@ -1611,6 +1594,31 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
             if (!emit896(HEAD, LAYERS, r0, n, rows, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
         }
     }
+    // O by head, read by the attention CTAs (not streamed per CTA): for layer l and head
+    // h, the two 32-column steps of columns [64 h, 64 h + 64) over all 896 rows in the
+    // down projection's tile order, then the rows' scales of that 64-column group
+    stream.resize((stream.size() + 255) & ~(size_t)255, 0);
+    const size_t o_frag_off = stream.size();
+    for (int l = 0; l < LAYERS; l++) {
+        const FileTensor *wo = &t[1 + l * STRIDE + WO];
+        const int8_t *ow = reinterpret_cast<const int8_t *>(hfile + wo->data);
+        for (int h = 0; h < HEADS; h++)
+            for (int ks = 0; ks < 2; ks++)
+                for (int ti = 0; ti < kDownTiles; ti++) {
+                    const int8_t *rr[16];
+                    for (int j = 0; j < 16; j++) rr[j] = ow + (size_t)(16 * ti + j) * DIM;
+                    put_step(stream, rr, HEAD_DIM * h + 32 * ks, false);
+                }
+    }
+    const size_t o_scale_off = stream.size();
+    for (int l = 0; l < LAYERS; l++) {
+        const FileTensor *wo = &t[1 + l * STRIDE + WO];
+        std::vector<float> osc;
+        for (int h = 0; h < HEADS; h++)
+            for (int r = 0; r < DIM; r++) osc.push_back(scale({wo, r}, h));
+        put_floats(osc);
+    }
+    if (o_scale_off - o_frag_off != (size_t)LAYERS * HEADS * kOHeadBytes) return 1;
     hplan->chunk_begin[kCTAs] = (uint32_t)chunks.size();
     hplan->head_lo[kCTAs] = VOCAB;
     for (int c = 0; c < kCTAs; c++)
@@ -1625,6 +1633,8 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
         return 1;
     }
     hplan->stream = *dstream;
+    hplan->ofrag = *dstream + o_frag_off;
+    hplan->oscale = reinterpret_cast<const float *>(*dstream + o_scale_off);
     hplan->chunks = *dchunks;
     hplan->blob = dfile;
     *stream_bytes = stream.size();

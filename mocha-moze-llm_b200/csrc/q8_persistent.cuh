@@ -39,6 +39,8 @@ struct Plan {
     const uint8_t *stream;                 // all CTAs' streams back to back
     const Chunk *chunks;                   // all chunks, CTA-major
     const uint8_t *blob;                   // the uploaded model file (gains)
+    const uint8_t *ofrag;                  // O by head: [layer][head][2 steps][56 tiles][32 lanes][16 B]
+    const float *oscale;                   // [layer][head][896] O scales of the head's 64-column group
     uint32_t chunk_begin[kCTAs + 1];
     uint32_t head_begin[kCTAs];            // first head chunk of each CTA (head chunks are last)
     uint32_t head_lo[kCTAs + 1];           // contiguous vocabulary rows per CTA
@@ -63,11 +65,11 @@ constexpr int replica_stride(int words) { return (words + 63) / 64 * 64 + 32; }
 struct Scratch {
     unsigned long long *q;        // [DIM] rotated queries
     unsigned long long *kv;       // [kReplicas][KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
-    unsigned long long *part;     // [kReplicas][HEADS][kMaxSplit][ATTN_PARTIAL] attention partials
-    unsigned long long *xmid;     // [kReplicas][DIM] residual after attention
-    unsigned long long *dacc;     // [2][LAYERS][DIM] down-projection sums, 64-bit fixed point (value * 2^32),
-                                  // two sets used by alternating steps (epoch & 1)
-    unsigned long long *dcnt;     // [2][LAYERS] CTAs whose down additions are complete
+    unsigned long long *part;     // [HEADS][kMaxSplit][2] (max, sum of weights) of every attention split
+    unsigned long long *dacc;     // [2][LAYERS][DIM] down-projection sums: fixed point (value * 2^32) in bits
+                                  // 8..63, additions counted in bits 0..7; two sets used by alternating
+                                  // steps (epoch & 1)
+    unsigned long long *xacc;     // [2][LAYERS][DIM] attention block (O of every head) sums, the same form
     unsigned long long *cand;     // [kCTAs][64] per-CTA candidate keys (plain)
 };
 
