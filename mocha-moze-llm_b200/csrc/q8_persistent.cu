@@ -363,19 +363,26 @@ MB_DEV float group_max16(float m)
     return m;
 }
 
-// RMSNorm of S.xs with `gain`, in the reference's rounding ((x * s) * g, s =
-// 1/sqrt(sum x^2 / DIM + eps)), quantized straight into S.bf / S.sxs; with keep the
-// normalised vector also goes to S.ns.  Consumer threads ct < 256 (warps 0..7) work;
-// every consumer thread calls it (two consumer barriers).
-MB_DEV void norm_quantize(Smem *Sp, int ct, const float *gain, int keep)
+// The four gain values of thread ct's columns (see norm_quantize), loaded ahead of use.
+MB_DEV float4 load_gain(int ct, const float *gain)
+{
+    return ct < 256 ? __ldg(reinterpret_cast<const float4 *>(gain + quant_col(min(ct, 223))))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// RMSNorm of S.xs with the gain g (this thread's four columns, from load_gain), in the
+// reference's rounding ((x * s) * g, s = 1/sqrt(sum x^2 / DIM + eps)), quantized
+// straight into S.bf / S.sxs; with keep the normalised vector also goes to S.ns.
+// Consumer threads ct < 256 (warps 0..7) work; every consumer thread calls it (two
+// consumer barriers).
+MB_DEV void norm_quantize(Smem *Sp, int ct, float4 g, int keep)
 {
     Smem &S = *Sp;
     const int t = min(ct, 223), col = quant_col(t), lane = ct & 31;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), g = x;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     float pm = 0.f;
     if (ct < 256) {
         x = *reinterpret_cast<const float4 *>(S.xs + col);
-        g = *reinterpret_cast<const float4 *>(gain + col);
         float ss = 0.f;
         if (ct < 224) ss = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
         pm = fmaxf(fmaxf(fabsf(x.x * g.x), fabsf(x.y * g.y)), fmaxf(fabsf(x.z * g.z), fabsf(x.w * g.w)));
@@ -821,6 +828,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     }
     cbar();
 
+    // the RMSNorm gains are loaded a layer ahead and carried in registers (a load placed
+    // next to its use would put two dependent L2 round trips on the critical path)
+    float4 g_attn = load_gain(c.ct, M->layer[0].attn_norm), g_ffn = load_gain(c.ct, M->layer[0].ffn_norm);
     for (int l = 0; l < LAYERS; l++) {
         // K/V of past positions for this CTA's attention split: no dependency on this
         // step, copied asynchronously while the QKV phase runs
@@ -846,13 +856,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         // ---- QKV + bias + RoPE + KV write
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
+            norm_quantize(&S, c.ct, g_attn, 0);
+            g_attn = load_gain(c.ct, M->layer[min(l + 1, LAYERS - 1)].attn_norm);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 12);
             const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 11);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
-            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(w + kGainOff), 0);
             const int npair = hd.count;
-            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 12);
             const uint8_t *frag = w + sizeof(ChunkHdr);
             const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
             const float *bias = sc + 8 * kGroups;
@@ -1098,6 +1109,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 
         // ---- RMSNorm -> gate/up -> SwiGLU
         {
+            norm_quantize(&S, c.ct, g_ffn, 0);
+            g_ffn = load_gain(c.ct, M->layer[min(l + 1, LAYERS - 1)].ffn_norm);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
             // this layer's gate/up chunks (2 or 3, all resident in the ring together):
             // slots cur.k .. cur.k + ngu - 1
             // (a CTA without a spare piece has two: waiting for a third slot would wait
@@ -1121,8 +1135,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             const uint32_t s0 = cur.k % kSlots, s1 = (cur.k + 1) % kSlots, s2 = (cur.k + (ngu > 2 ? 2 : 0)) % kSlots;
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 9);
-            norm_quantize(&S, c.ct, reinterpret_cast<const float *>(S.ring[s0] + kGainOff), 0);
-            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
             Tiles tl{{S.ring[s0] + sizeof(ChunkHdr), S.ring[s1] + sizeof(ChunkHdr), S.ring[s2] + sizeof(ChunkHdr)},
                      {nullptr, nullptr, nullptr},
                      T,
@@ -1204,7 +1216,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         }
         if (c.ct == 0)
             for (int i = 0; i < kSlots; i++) S.slot_fill[(cur.k + i) % kSlots] = (int)(cur.k + i);
-        norm_quantize(&S, c.ct, reinterpret_cast<const float *>(S.ring[cur.k % kSlots] + kGainOff), cta == 0);
+        norm_quantize(&S, c.ct, load_gain(c.ct, M->final_norm), cta == 0);
         if (cta == 0)
             for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
         // Warp w takes tiles w, w + 16, ... in order (tile t = tile t & 1 of chunk t >> 1),
