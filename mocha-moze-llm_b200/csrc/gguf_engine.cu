@@ -734,7 +734,7 @@ extern "C" int mocha_gguf_forward(mocha_gguf *m, int token, int pos, int project
     if (project && logits)
         TRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->info.vocab, cudaMemcpyDeviceToHost, m->stream));
     TRY(cudaStreamSynchronize(m->stream));
-    return 0;
+    return gguf::gemv_take_timeout();
 }
 
 namespace {
@@ -789,6 +789,7 @@ extern "C" int mocha_gguf_generate(mocha_gguf *m, const int *prompt, int n_promp
     for (int i = 1; i < n_new; i++) TRY(cudaGraphLaunch(m->g_decode, m->stream));
     TRY(cudaEventRecord(m->ev[3], m->stream));
     TRY(cudaStreamSynchronize(m->stream));
+    if (gguf::gemv_take_timeout()) return 1;
     int n = 0;
     for (int i = 0; i < n_new; i++) out_tokens[i] = m->h_out[i];
     while (n < n_new && out_tokens[n] != m->info.eos) n++;
@@ -830,7 +831,7 @@ extern "C" int mocha_gguf_bench_decode(mocha_gguf *m, int token, int pos0, int p
     TRY(cudaEventRecord(m->ev[1], m->stream));
     TRY(cudaStreamSynchronize(m->stream));
     TRY(cudaEventElapsedTime(ms, m->ev[0], m->ev[1]));
-    return 0;
+    return gguf::gemv_take_timeout();
 }
 
 extern "C" int mocha_gguf_launches_per_step(mocha_gguf *m) { return m ? (int)m->launches_per_token : 0; }

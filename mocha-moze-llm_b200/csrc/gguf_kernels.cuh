@@ -99,5 +99,8 @@ struct MultiGemvMma {
     float eps;
 };
 int enqueue_gemv_mma(const MultiGemvMma &g, cudaStream_t s);
+// 1 (with a message) when a staged GEMV's bounded wait for its weights expired since the
+// last call; clears the flag.
+int gemv_take_timeout();
 
 }  // namespace gguf

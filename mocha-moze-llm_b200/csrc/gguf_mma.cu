@@ -26,8 +26,18 @@
 // the block's scales applied in fp32: Q4_K d*sc*(...) - dmin*m*sum(x) over the 32
 // columns, Q6_K d*scale*(... - 32*sum of the limbs), Q8_0 d*(...).  Rows are tiles
 // of 16; a CTA takes a contiguous range of tiles and its 16 warps split the CTA's
-// (tile, 4-step batch) work evenly, keeping the next batch's weight loads in flight;
-// per-warp row sums are added in warp order.
+// (tile, 4-step batch) work evenly; per-warp row sums are added in warp order.
+//
+// Weight staging.  When a CTA's whole range fits in shared memory next to the input
+// fragments (every per-layer GEMV of the two GGUF models: at most ~130 KB per CTA), its
+// first thread copies the range into shared memory with bulk asynchronous copies
+// (cp.async.bulk, completing on an mbarrier) before it waits for the kernel ahead --
+// weights do not depend on it -- so the HBM stream of every CTA starts at once and runs
+// while the input is being quantized; the warps then read their batches from shared
+// memory.  Otherwise (the vocabulary head) each warp loads its batches from global
+// memory into registers, keeping the next batch's loads in flight.
+#include <algorithm>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -44,6 +54,7 @@ constexpr int kThreads = 512, kWarps = kThreads / 32;
 constexpr int kGrid = mb::kSMs;  // one CTA per SM (512 threads x ~100 registers)
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
 constexpr size_t kPrefetchBytes = 160 * 1024;  // per CTA: 148 CTAs x 160 KB = 24 MB of the 126 MB L2
+constexpr size_t kSmemLimit = 220 * 1024;      // dynamic shared memory per CTA
 
 // fp16 bits -> fp32 (exact for every fp16 value)
 MB_DEV float half_to_float(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu))); }
@@ -246,19 +257,51 @@ struct Batch {
                          // (high 16); Q8_0: per step likewise
 };
 
+// plain loads from the staged shared-memory copy, or read-only / streaming global loads
+template <bool S, typename T>
+MB_DEV T ld_w(const void *p)
+{
+    return *reinterpret_cast<const T *>(p);
+}
+template <>
+MB_DEV uint32_t ld_w<false, uint32_t>(const void *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+template <>
+MB_DEV uint4 ld_w<false, uint4>(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+template <>
+MB_DEV uint16_t ld_w<false, uint16_t>(const void *p) { return __ldg(reinterpret_cast<const uint16_t *>(p)); }
+template <bool S>
+MB_DEV uint2 ld_s8(const void *p)
+{
+    if constexpr (S) return *reinterpret_cast<const uint2 *>(p);
+    else return mb::ld_stream8(p);
+}
+template <bool S>
+MB_DEV uint32_t ld_s4(const void *p)
+{
+    if constexpr (S) return *reinterpret_cast<const uint32_t *>(p);
+    else return mb::ld_stream4(p);
+}
+template <bool S>
+MB_DEV uint4 ld_s16(const void *p)
+{
+    if constexpr (S) return *reinterpret_cast<const uint4 *>(p);
+    else return mb::ld_stream16u(p);
+}
+
+template <bool S>
 MB_DEV void load_batch(const Job &jb, int s0, int lane, Batch &B)
 {
     const int g = lane >> 2;
     if (jb.type == Q4_K) {
         const int blk = s0 >> 3, nb = jb.steps >> 3;
         const uint8_t *rec = jb.body + ((size_t)jb.tile * nb + blk) * kQ4Rec;
-        B.dd[0] = __ldg(reinterpret_cast<const uint32_t *>(rec) + g);
-        B.dd[1] = __ldg(reinterpret_cast<const uint32_t *>(rec) + g + 8);
-        B.h0 = __ldg(reinterpret_cast<const uint4 *>(rec + kQ4Hdr + 16 * g));
-        B.h1 = __ldg(reinterpret_cast<const uint4 *>(rec + kQ4Hdr + 16 * (g + 8)));
+        B.dd[0] = ld_w<S, uint32_t>(rec + 4 * g);
+        B.dd[1] = ld_w<S, uint32_t>(rec + 4 * (g + 8));
+        B.h0 = ld_w<S, uint4>(rec + kQ4Hdr + 16 * g);
+        B.h1 = ld_w<S, uint4>(rec + kQ4Hdr + 16 * (g + 8));
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
-            const uint2 v = mb::ld_stream8(rec + kQ4Scales + ((s0 & 7) + k) * 256 + lane * 8);
+            const uint2 v = ld_s8<S>(rec + kQ4Scales + ((s0 & 7) + k) * 256 + lane * 8);
             B.w[k] = make_uint4(v.x, v.y, 0u, 0u);
         }
     } else if (jb.type == Q6_K) {
@@ -267,21 +310,22 @@ MB_DEV void load_batch(const Job &jb, int s0, int lane, Batch &B)
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
             const int p = (s0 & 7) + k;
-            const uint2 v = mb::ld_stream8(rec + p * 256 + lane * 8);
-            const uint32_t hw = mb::ld_stream4(rec + 2048 + p * 128 + lane * 4);
+            const uint2 v = ld_s8<S>(rec + p * 256 + lane * 8);
+            const uint32_t hw = ld_s4<S>(rec + 2048 + p * 128 + lane * 4);
             B.w[k] = make_uint4(v.x, v.y, hw, 0u);
         }
-        B.h0 = __ldg(reinterpret_cast<const uint4 *>(rec + 3072 + 16 * g));
-        B.h1 = __ldg(reinterpret_cast<const uint4 *>(rec + 3072 + 16 * (g + 8)));
-        const uint16_t *dp = reinterpret_cast<const uint16_t *>(rec + 3328);
-        B.dd[0] = (uint32_t)__ldg(dp + g) | ((uint32_t)__ldg(dp + g + 8) << 16);
+        B.h0 = ld_w<S, uint4>(rec + 3072 + 16 * g);
+        B.h1 = ld_w<S, uint4>(rec + 3072 + 16 * (g + 8));
+        const uint8_t *dp = rec + 3328;
+        B.dd[0] = (uint32_t)ld_w<S, uint16_t>(dp + 2 * g) | ((uint32_t)ld_w<S, uint16_t>(dp + 2 * (g + 8)) << 16);
     } else {
         const uint8_t *tile = jb.body + (size_t)jb.tile * jb.steps * 544;
-        const uint16_t *dp = reinterpret_cast<const uint16_t *>(tile + (size_t)jb.steps * 512);
+        const uint8_t *dp = tile + (size_t)jb.steps * 512;
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
-            B.w[k] = mb::ld_stream16u(tile + (size_t)(s0 + k) * 512 + lane * 16);
-            B.dd[k] = (uint32_t)__ldg(dp + (s0 + k) * 16 + g) | ((uint32_t)__ldg(dp + (s0 + k) * 16 + g + 8) << 16);
+            B.w[k] = ld_s16<S>(tile + (size_t)(s0 + k) * 512 + lane * 16);
+            B.dd[k] = (uint32_t)ld_w<S, uint16_t>(dp + 2 * ((s0 + k) * 16 + g)) |
+                      ((uint32_t)ld_w<S, uint16_t>(dp + 2 * ((s0 + k) * 16 + g + 8)) << 16);
         }
     }
 }
@@ -413,17 +457,76 @@ struct Gemv {
     const float *x, *gain, *up;  // up: the input is silu(x) * up (the SwiGLU of the FFN)
     float eps;
     int max_tiles;    // tiles per CTA at most (shared-memory row sums)
+    size_t ring;      // staged: offset of the weight copy in dynamic shared memory
 };
 
+// Set when a staged GEMV's copy did not complete within its bound (read by the engine).
+__device__ unsigned g_gemv_timeout;
+constexpr long long kStageTimeoutCycles = 4000000000LL;
+
+MB_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+template <bool Staged>
 __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
 {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long stage_bar;
     const int total = g.tile_end[g.n - 1];
     const int t_begin = (int)((long long)total * blockIdx.x / gridDim.x);
     const int t_end = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     const int steps = g.cols / 32;
-    // this CTA's weight bytes into L2 while the kernel ahead finishes
-    if (threadIdx.x < g.n) {
+    // this CTA's tiles of each matrix, [ra[i], rb[i]) in matrix i's own numbering, and
+    // where their copy starts in the staged range
+    int ra[3], rb[3];
+    size_t roff[3];
+    {
+        size_t off = 0;
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            const int start = i ? g.tile_end[i - 1] : 0, end = i < g.n ? g.tile_end[i] : start;
+            ra[i] = max(t_begin, start) - start;
+            rb[i] = max(min(t_end, end) - start, ra[i]);
+            roff[i] = off;
+            if (i < g.n) off += (size_t)(rb[i] - ra[i]) * mma_tile_bytes(g.m[i].type, g.cols);
+        }
+    }
+    if (Staged) {
+        // the whole range into shared memory: bulk copies of at most 32 KB, all completing
+        // on one mbarrier, started before the wait (nothing here depends on the kernel ahead)
+        if (threadIdx.x == 0) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&stage_bar)) : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            size_t bytes = 0;
+#pragma unroll
+            for (int i = 0; i < 3; i++)
+                if (i < g.n) bytes += (size_t)(rb[i] - ra[i]) * mma_tile_bytes(g.m[i].type, g.cols);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&stage_bar)),
+                         "r"((uint32_t)bytes)
+                         : "memory");
+            const uint64_t policy = mb::evict_first_policy();
+#pragma unroll
+            for (int i = 0; i < 3; i++) {
+                if (i >= g.n) break;
+                const size_t tb = mma_tile_bytes(g.m[i].type, g.cols);
+                const uint8_t *src = g.m[i].body + (size_t)ra[i] * tb;
+                uint8_t *dst = smem + g.ring + roff[i];
+                for (size_t left = (size_t)(rb[i] - ra[i]) * tb; left > 0;) {
+                    const uint32_t n = (uint32_t)(left < 32768 ? left : 32768);
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+                        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+                        "l"(src), "r"(n), "r"(smem_u32(&stage_bar)), "l"(policy)
+                        : "memory");
+                    src += n;
+                    dst += n;
+                    left -= n;
+                }
+            }
+        }
+    } else if (threadIdx.x < g.n) {
+        // this CTA's weight bytes into L2 while the kernel ahead finishes
         const int i = threadIdx.x, start = i ? g.tile_end[i - 1] : 0;
         const int a = max(t_begin, start), b = min(t_end, g.tile_end[i]);
         if (a < b) {
@@ -449,18 +552,22 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
         const int tt = t_begin + tile_local;
         const int mi = tt < g.tile_end[0] ? 0 : (tt < g.tile_end[1] ? 1 : 2);
         Job j;
-        j.body = g.m[mi].body;
         j.type = g.m[mi].type;
         j.tile = tt - (mi ? g.tile_end[mi - 1] : 0);
         j.steps = steps;
+        if (Staged) {  // the staged copy of matrix mi's range starts at its tile ra[mi]
+            j.body = smem + g.ring + (mi == 0 ? roff[0] : mi == 1 ? roff[1] : roff[2]);
+            j.tile -= mi == 0 ? ra[0] : mi == 1 ? ra[1] : ra[2];
+        } else {
+            j.body = g.m[mi].body;
+        }
         return j;
     };
     int tl = b0 / bpt, s0 = (b0 - tl * bpt) * kBatch;
     Job jb = job(tl);
     Batch buf[2];
-    if (b0 < b1) load_batch(jb, s0, lane, buf[0]);
+    if (!Staged && b0 < b1) load_batch<false>(jb, s0, lane, buf[0]);
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    extern __shared__ __align__(16) uint8_t smem[];
     const Lay L = layout(g.cols, g.max_tiles);
     uint2 *bf = reinterpret_cast<uint2 *>(smem + L.bf);
     float *sx = reinterpret_cast<float *>(smem + L.sx);
@@ -574,6 +681,24 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     // B-fragment columns 3..7 (lanes 12..31) are zero
     for (int i = threadIdx.x; i < steps * 20; i += kThreads) bf[(i / 20) * 32 + 12 + i % 20] = make_uint2(0u, 0u);
     __syncthreads();
+    if (Staged) {  // the weights have landed (bounded wait; the phase flips once)
+        uint32_t done = 0;
+        const long long t0 = clock64();
+        while (!done) {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done)
+                : "r"(smem_u32(&stage_bar))
+                : "memory");
+            if (!done && clock64() - t0 > kStageTimeoutCycles) break;
+        }
+        if (__syncthreads_or(!done)) {
+            if (threadIdx.x == 0) atomicOr(&g_gemv_timeout, 1u);
+            return;
+        }
+        if (b0 < b1) load_batch<true>(jb, s0, lane, buf[0]);
+    }
 
     // batches (tile, 4 steps) of this CTA, split evenly over the warps; a warp walks its
     // range tile by tile, loading the next batch before computing the current one
@@ -590,7 +715,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
             Job jn = jb;
             if (bi + 1 < b1) {
                 if (tln != tl) jn = job(tln);
-                load_batch(jn, s0n, lane, nxt);
+                load_batch<Staged>(jn, s0n, lane, nxt);
             }
             run_batch(jb, s0, lane, cur, bf, sx, x32, sa, acc0, acc1);
             if (bi + 1 == b1 || tln != tl) {
@@ -673,31 +798,60 @@ int enqueue_gemv_mma(const MultiGemvMma &in, cudaStream_t s)
     const int grid = tiles < kGrid ? tiles : kGrid;
     g.max_tiles = (tiles + grid - 1) / grid;
     const Lay L = layout(in.cols, g.max_tiles);
-    if (L.bytes > 220 * 1024) return 1;
+    if (L.bytes > kSmemLimit) return 1;
+    // the largest CTA range (each CTA takes tiles [total c / grid, total (c+1) / grid))
+    size_t range = 0;
+    for (int c = 0; c < grid; c++) {
+        const int tb = (int)((long long)tiles * c / grid), te = (int)((long long)tiles * (c + 1) / grid);
+        size_t bytes = 0;
+        for (int i = 0; i < in.n; i++) {
+            const int start = i ? g.tile_end[i - 1] : 0;
+            const int a = std::max(tb, start), b = std::min(te, g.tile_end[i]);
+            if (a < b) bytes += (size_t)(b - a) * mma_tile_bytes(in.m[i].type, in.cols);
+        }
+        range = std::max(range, bytes);
+    }
+    g.ring = (L.bytes + 127) & ~(size_t)127;
+    const bool staged = g.ring + range <= kSmemLimit;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(k_gemv_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemv_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) !=
+                cudaSuccess)
             return 1;
         configured[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = L.bytes;
+    cfg.dynamicSmemBytes = staged ? g.ring + range : L.bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_mma, g);
+    const cudaError_t e =
+        staged ? cudaLaunchKernelEx(&cfg, k_gemv_mma<true>, g) : cudaLaunchKernelEx(&cfg, k_gemv_mma<false>, g);
     if (e != cudaSuccess) {
         fprintf(stderr, "CUDA gguf mma gemv: %d %s\n", (int)e, cudaGetErrorString(e));
         return 1;
     }
     return 0;
+}
+
+int gemv_take_timeout()
+{
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_timeout, sizeof v) != cudaSuccess) return 1;
+    if (!v) return 0;
+    fprintf(stderr, "MOCHA_B200: a staged GGUF GEMV's weight copy did not complete (bounded wait expired)\n");
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(g_gemv_timeout, &zero, sizeof zero);
+    return 1;
 }
 
 }  // namespace gguf
