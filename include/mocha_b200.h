@@ -156,10 +156,19 @@ int mocha_q8b_prefill(mocha_q8b *h, int slot, const int *tokens, int n, float *l
 /* The reference token loop for nseq sequences of prompt_len tokens each: n_new tokens
  * per sequence (fewer if EOS comes first; EOS not reported), sampling as in
  * mocha_sampling with seed seed_base + sequence index.  out_tokens[nseq][n_new],
- * out_counts[nseq]. */
+ * out_counts[nseq].  Continuous batching: min(slots, max_rows / prompt_len) sequences
+ * decode together, one row per slot; a slot whose sequence finishes is refilled with
+ * the next waiting sequence (its prompt pass, then it joins the decode steps). */
 int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, int n_new,
                        const mocha_sampling *sampling, unsigned seed_base, int *out_tokens, int *out_counts,
                        mocha_timing *timing);
+
+/* mocha_q8b_generate with a token budget per sequence, n_new[i] <= out_stride:
+ * out_tokens[nseq][out_stride].  Sequences with smaller budgets leave their slots
+ * early, and waiting sequences take them mid-stream. */
+int mocha_q8b_generate_each(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, const int *n_new,
+                            const mocha_sampling *sampling, unsigned seed_base, int *out_tokens, int out_stride,
+                            int *out_counts, mocha_timing *timing);
 
 /* Device-timed prefill of an n-token seeded random prompt in slot 0 (head on the
  * last position): warmup passes, then *ms = CUDA-event time of `steps` passes. */

@@ -994,12 +994,14 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage1(const float *__res
 }
 
 // Stage 2: merge the slices, draw the token, record it for the slot and set up the
-// slot's next decode row (next_* arrays, indexed by projected row).
+// slot's next decode row (next_* arrays, at next_index[r] for projected row r, or at r
+// when next_index is null).
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned long long *__restrict__ in,
                                                               const int *proj_src, Rows rows, int nslots,
                                                               sampling::SeqState *st, const sampling::Params *prm,
                                                               int *next_tok, int *next_pos, int *next_slot,
-                                                              int *out_tokens, int *out_count, int out_stride)
+                                                              const int *next_index, int *out_tokens,
+                                                              int *out_count, int out_stride)
 {
     pdl_enter();
     constexpr int kMerge = 2048;  // >= NSLICE * kMaxK = 1216
@@ -1033,9 +1035,10 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_bs_stage2(const unsigned lon
             out_count[slot] = n + 1;
             sampling::record_token(token, p, s, nullptr, nullptr);
         }
-        next_tok[r] = s->finished ? p.eos : token;
-        next_pos[r] = min(pos + 1, CONTEXT - 1);
-        next_slot[r] = slot;
+        const int ni = next_index ? next_index[r] : r;
+        next_tok[ni] = s->finished ? p.eos : token;
+        next_pos[ni] = min(pos + 1, CONTEXT - 1);
+        next_slot[ni] = slot;
     }
 }
 
@@ -1072,6 +1075,7 @@ struct mocha_q8b {
     int *tok = nullptr, *pos = nullptr, *slot = nullptr;            // prompt rows [max_rows]
     int *ntok = nullptr, *npos = nullptr, *nslot = nullptr;         // decode rows [slots]
     int *proj_src = nullptr, *proj_dst = nullptr, *ident = nullptr;  // [slots], [max_rows], [slots]
+    int *next_index = nullptr;                                       // [slots]: decode row of a refilled slot
     int *err = nullptr;
     unsigned long long *keys = nullptr;
     sampling::SeqState *st = nullptr;
@@ -1297,7 +1301,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
 
 // Sampling for projected rows 0..np-1; proj_src[r] is the activation row of
 // projected row r (the identity map in decode steps).
-int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src)
+int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src, const int *next_index = nullptr)
 {
     static bool attr_done[64] = {};
     if (!attr_done[h->device & 63]) {
@@ -1309,7 +1313,8 @@ int enqueue_sample(mocha_q8b *h, Rows rows, int np, const int *proj_src)
             proj_src, rows, h->slots, h->st, h->params, h->keys))
         return 1;
     if (pdl(k_bs_stage2, np, SAMPLE_THREADS, 0, h->stream, h->keys, proj_src, rows, h->slots, h->st, h->params, h->ntok,
-                                                      h->npos, h->nslot, h->out_tokens, h->out_count, h->out_stride)) return 1;
+            h->npos, h->nslot, next_index, h->out_tokens, h->out_count, h->out_stride))
+        return 1;
     QB_TRY(cudaGetLastError());
     return 0;
 }
@@ -1450,7 +1455,7 @@ extern "C" int mocha_q8b_open(int device, const void *file, unsigned long long b
         dalloc(&h->lhead.s, (size_t)slots * (DIM / GROUP)) ||
         dalloc(&h->logits, (size_t)slots * VOCAB) || dalloc(&h->tok, R) || dalloc(&h->pos, R) ||
         dalloc(&h->slot, R) || dalloc(&h->ntok, slots) || dalloc(&h->npos, slots) || dalloc(&h->nslot, slots) ||
-        dalloc(&h->proj_src, slots) || dalloc(&h->proj_dst, R) || dalloc(&h->ident, slots) || dalloc(&h->err, 1) ||
+        dalloc(&h->proj_src, slots) || dalloc(&h->proj_dst, R) || dalloc(&h->ident, slots) || dalloc(&h->next_index, slots) || dalloc(&h->err, 1) ||
         dalloc(&h->keys, (size_t)slots * NSLICE * sampling::kMaxK) || dalloc(&h->st, slots) ||
         dalloc(&h->params, 1) || dalloc(&h->out_count, slots))
         return fail();
@@ -1513,8 +1518,8 @@ extern "C" int mocha_q8b_close(mocha_q8b *h)
     void *ptrs[] = {h->d_file, h->bqkv, h->x, h->q, h->part, h->apart, h->logits, h->lx.q, h->lx.s, h->la.q,
                     h->la.s, h->lhq, h->lhs, h->lhead.q, h->lhead.s, h->kc, h->vc, h->kvs.k_hi, h->kvs.k_lo,
                     h->kvs.vt_hi, h->kvs.vt_lo, h->rope_cos, h->rope_sin, h->tok,
-                    h->pos, h->slot, h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->err,
-                    h->keys, h->st, h->params, h->out_tokens, h->out_count};
+                    h->pos, h->slot, h->ntok, h->npos, h->nslot, h->proj_src, h->proj_dst, h->ident, h->next_index,
+                    h->err, h->keys, h->st, h->params, h->out_tokens, h->out_count};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     for (int l = 0; l < LAYERS; l++)
@@ -1571,24 +1576,32 @@ extern "C" int mocha_q8b_prefill(mocha_q8b *h, int slot, const int *tokens, int 
 // time; each wave prefills its prompts in one pass (rows of all its slots), samples
 // the first token from the last prompt position, then runs n_new - 1 decode steps as
 // one CUDA graph per step with tokens and positions kept on the device.
-extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, int n_new,
-                                  const mocha_sampling *sp, unsigned seed_base, int *out_tokens, int *out_counts,
-                                  mocha_timing *timing)
+namespace qb {
+namespace {
+
+// Continuous batching: the first min(slots, max_rows / prompt_len) sequences take a slot
+// each and are prefilled together; every decode step then advances all of those slots
+// (one row per slot, a captured graph).  The host looks at the slots between runs of
+// steps -- a run lasts until the first active sequence can have reached its token
+// budget, at most kCheckEvery steps, so an EOS is noticed soon -- harvests every slot
+// whose sequence has finished (EOS or n_new[i] tokens) and refills it at once with the
+// next waiting sequence: that sequence's prompt rows run in one prompt pass (several
+// refills share it), its first token goes to the slot's decode row (next_index), and
+// the next step decodes it alongside the others.  Sampler state per slot: the last 64
+// prompt tokens, seed seed_base + sequence index (src/minimind.cpp:160-179).
+constexpr int kCheckEvery = 32;
+
+int generate_impl(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, const int *n_new, int max_new,
+                  const mocha_sampling *sp, unsigned seed_base, int *out_tokens, int *out_counts, mocha_timing *timing)
 {
-    if (!h || nseq < 1 || !prompts || prompt_len < 1 || n_new < 1 || prompt_len + n_new > CONTEXT || !sp ||
-        !out_tokens || !out_counts || sp->top_k < 1 || sp->top_k > sampling::kMaxK || !(sp->top_p > 0.f) ||
-        sp->top_p > 1.f || sp->temperature < 0.f || sp->repeat_penalty < 1.f) {
-        fprintf(stderr, "mocha_q8b_generate: bad arguments\n");
-        return 1;
-    }
     QB_TRY(cudaSetDevice(h->device));
     const int wave = std::min(h->slots, std::max(1, h->max_rows / prompt_len));
     if (wave < 1) return 1;
-    if (h->out_stride < n_new) {
+    if (h->out_stride < max_new) {
         if (h->out_tokens) cudaFree(h->out_tokens);
         h->out_tokens = nullptr;
-        if (dalloc(&h->out_tokens, (size_t)h->slots * n_new)) return 1;
-        h->out_stride = n_new;
+        if (dalloc(&h->out_tokens, (size_t)h->slots * max_new)) return 1;
+        h->out_stride = max_new;
     }
     for (int i = 0; i < nseq; i++)
         for (int j = 0; j < prompt_len; j++)
@@ -1598,69 +1611,95 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
             }
     sampling::Params prm{sp->repeat_penalty, sp->temperature, sp->top_k, sp->top_p, EOS, CONTROL_FIRST, VOCAB};
     QB_TRY(cudaMemcpyAsync(h->params, &prm, sizeof(prm), cudaMemcpyHostToDevice, h->stream));
+    const int b = std::min(wave, nseq);        // slots stepped together
+    std::vector<int> seq_of(b, -1);             // sequence in each slot, -1 free
+    std::vector<sampling::SeqState> st(b);
+    std::vector<int> counts(b), row;
+    int next = 0;                               // next waiting sequence
     double prefill_s = 0, decode_s = 0;
     int generated = 0;
-    std::vector<int> tok, pos, sl, src, counts(h->slots);
-    std::vector<sampling::SeqState> st(h->slots);
-    for (int s0 = 0; s0 < nseq; s0 += wave) {
-        const int b = std::min(wave, nseq - s0);
-        // sampler state: the last 64 prompt tokens, seed base + sequence index
-        for (int i = 0; i < b; i++) {
-            sampling::SeqState &x = st[i];
+    float ms = 0;
+    // fill the free slots with waiting sequences: one prompt pass over all their rows
+    auto admit = [&]() -> int {
+        std::vector<int> tok, pos, sl, src, idx;
+        for (int i = 0; i < b && next < nseq; i++) {
+            if (seq_of[i] >= 0) continue;
+            const int q = next++;
+            seq_of[i] = q;
+            sampling::SeqState x;
             memset(&x, 0, sizeof x);
-            const int *p = prompts + (size_t)(s0 + i) * prompt_len;
+            const int *p = prompts + (size_t)q * prompt_len;
             const int from = std::max(0, prompt_len - sampling::kHistory);
             for (int j = from; j < prompt_len; j++) x.history[x.history_count++] = p[j];
             x.history_head = x.history_count % sampling::kHistory;
-            x.seed = seed_base + (unsigned)(s0 + i);
+            x.seed = seed_base + (unsigned)q;
             x.last_token = p[prompt_len - 1];
-        }
-        QB_TRY(cudaMemcpyAsync(h->st, st.data(), sizeof(sampling::SeqState) * b, cudaMemcpyHostToDevice, h->stream));
-        QB_TRY(cudaMemsetAsync(h->out_count, 0, sizeof(int) * h->slots, h->stream));
-        tok.resize((size_t)b * prompt_len);
-        pos.resize(tok.size());
-        sl.resize(tok.size());
-        src.resize(b);
-        for (int i = 0; i < b; i++) {
+            QB_TRY(cudaMemcpyAsync(h->st + i, &x, sizeof x, cudaMemcpyHostToDevice, h->stream));
+            QB_TRY(cudaMemsetAsync(h->out_count + i, 0, sizeof(int), h->stream));
             for (int j = 0; j < prompt_len; j++) {
-                tok[(size_t)i * prompt_len + j] = prompts[(size_t)(s0 + i) * prompt_len + j];
-                pos[(size_t)i * prompt_len + j] = j;
-                sl[(size_t)i * prompt_len + j] = i;
+                tok.push_back(p[j]);
+                pos.push_back(j);
+                sl.push_back(i);
             }
-            src[i] = i * prompt_len + prompt_len - 1;
+            src.push_back((int)tok.size() - 1);
+            idx.push_back(i);
         }
-        const int n = b * prompt_len;
-        if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, b, src.data())) return 1;
+        if (src.empty()) return 0;
+        const int n = (int)tok.size(), np = (int)src.size();
+        if (upload_rows(h, n, tok.data(), pos.data(), sl.data()) || set_projection(h, n, np, src.data())) return 1;
+        QB_TRY(cudaMemcpyAsync(h->next_index, idx.data(), sizeof(int) * np, cudaMemcpyHostToDevice, h->stream));
         QB_TRY(cudaEventRecord(h->ev[0], h->stream));
         const Rows pr{h->tok, h->pos, h->slot};
-        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, b,
+        if (enqueue_forward(h, pr, n, n <= h->slots, h->proj_dst, np,
                             prompt_len % TQ == 0 ? 2 : (prompt_len % QB == 0 ? 1 : 0), prompt_len - 1) ||
-            enqueue_sample(h, pr, b, h->proj_src))
+            enqueue_sample(h, pr, np, h->proj_src, h->next_index))
             return 1;
         QB_TRY(cudaEventRecord(h->ev[1], h->stream));
-        if (n_new > 1 && capture_step(h, b)) return 1;
-        for (int step = 1; step < n_new; step++) QB_TRY(cudaGraphLaunch(h->g_step, h->stream));
-        QB_TRY(cudaEventRecord(h->ev[2], h->stream));
-        QB_TRY(cudaEventSynchronize(h->ev[2]));
-        if (check_err(h)) return 1;
-        float a = 0, c = 0;
-        QB_TRY(cudaEventElapsedTime(&a, h->ev[0], h->ev[1]));
-        QB_TRY(cudaEventElapsedTime(&c, h->ev[1], h->ev[2]));
-        prefill_s += a * 1e-3;
-        decode_s += c * 1e-3;
+        QB_TRY(cudaEventSynchronize(h->ev[1]));  // idx and the row vectors are host temporaries
+        QB_TRY(cudaEventElapsedTime(&ms, h->ev[0], h->ev[1]));
+        prefill_s += ms * 1e-3;
+        return 0;
+    };
+    if (admit()) return 1;
+    if (capture_step(h, b)) return 1;
+    for (;;) {
         QB_TRY(cudaMemcpy(counts.data(), h->out_count, sizeof(int) * b, cudaMemcpyDeviceToHost));
+        QB_TRY(cudaMemcpy(st.data(), h->st, sizeof(sampling::SeqState) * b, cudaMemcpyDeviceToHost));
+        if (check_err(h)) return 1;
+        int run = kCheckEvery, active = 0;
         for (int i = 0; i < b; i++) {
-            // tokens before EOS; EOS itself is not reported
-            int cnt = std::min(counts[i], n_new);
-            std::vector<int> row(n_new);
-            QB_TRY(cudaMemcpy(row.data(), h->out_tokens + (size_t)i * h->out_stride, sizeof(int) * n_new,
-                              cudaMemcpyDeviceToHost));
-            int kept = 0;
-            while (kept < cnt && row[kept] != EOS) kept++;
-            memcpy(out_tokens + (size_t)(s0 + i) * n_new, row.data(), sizeof(int) * kept);
-            out_counts[s0 + i] = kept;
-            generated += kept;
+            const int q = seq_of[i];
+            if (q < 0) continue;
+            if (st[i].finished || counts[i] >= n_new[q]) {  // harvest: tokens before EOS, at most n_new
+                const int cnt = std::min(counts[i], n_new[q]);
+                row.resize((size_t)std::max(cnt, 1));
+                if (cnt > 0)
+                    QB_TRY(cudaMemcpy(row.data(), h->out_tokens + (size_t)i * h->out_stride, sizeof(int) * cnt,
+                                      cudaMemcpyDeviceToHost));
+                int kept = 0;
+                while (kept < cnt && row[kept] != EOS) kept++;
+                memcpy(out_tokens + (size_t)q * max_new, row.data(), sizeof(int) * kept);
+                out_counts[q] = kept;
+                generated += kept;
+                seq_of[i] = -1;
+            } else {
+                active++;
+                run = std::min(run, n_new[q] - counts[i]);
+            }
         }
+        if (next < nseq) {
+            const int before = next;
+            if (admit()) return 1;
+            active += next - before;
+            if (next > before) run = 1;  // look again once the new sequences have a token
+        }
+        if (!active) break;
+        QB_TRY(cudaEventRecord(h->ev[2], h->stream));
+        for (int k = 0; k < std::max(run, 1); k++) QB_TRY(cudaGraphLaunch(h->g_step, h->stream));
+        QB_TRY(cudaEventRecord(h->ev[3], h->stream));
+        QB_TRY(cudaEventSynchronize(h->ev[3]));
+        QB_TRY(cudaEventElapsedTime(&ms, h->ev[2], h->ev[3]));
+        decode_s += ms * 1e-3;
     }
     if (timing) {
         timing->prefill_s = prefill_s;
@@ -1668,6 +1707,45 @@ extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, in
         timing->generated = generated;
     }
     return 0;
+}
+
+bool generate_args_ok(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, const mocha_sampling *sp,
+                      const int *out_tokens, const int *out_counts)
+{
+    return h && nseq >= 1 && prompts && prompt_len >= 1 && sp && out_tokens && out_counts && sp->top_k >= 1 &&
+           sp->top_k <= sampling::kMaxK && sp->top_p > 0.f && sp->top_p <= 1.f && sp->temperature >= 0.f &&
+           sp->repeat_penalty >= 1.f;
+}
+
+}  // namespace
+}  // namespace qb
+
+extern "C" int mocha_q8b_generate(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, int n_new,
+                                  const mocha_sampling *sp, unsigned seed_base, int *out_tokens, int *out_counts,
+                                  mocha_timing *timing)
+{
+    if (!generate_args_ok(h, nseq, prompts, prompt_len, sp, out_tokens, out_counts) || n_new < 1 ||
+        prompt_len + n_new > CONTEXT) {
+        fprintf(stderr, "mocha_q8b_generate: bad arguments\n");
+        return 1;
+    }
+    std::vector<int> each((size_t)nseq, n_new);
+    return generate_impl(h, nseq, prompts, prompt_len, each.data(), n_new, sp, seed_base, out_tokens, out_counts,
+                         timing);
+}
+
+extern "C" int mocha_q8b_generate_each(mocha_q8b *h, int nseq, const int *prompts, int prompt_len, const int *n_new,
+                                       const mocha_sampling *sp, unsigned seed_base, int *out_tokens, int out_stride,
+                                       int *out_counts, mocha_timing *timing)
+{
+    bool ok = generate_args_ok(h, nseq, prompts, prompt_len, sp, out_tokens, out_counts) && n_new && out_stride >= 1;
+    for (int i = 0; ok && i < nseq; i++) ok = n_new[i] >= 1 && n_new[i] <= out_stride && prompt_len + n_new[i] <= CONTEXT;
+    if (!ok) {
+        fprintf(stderr, "mocha_q8b_generate_each: bad arguments\n");
+        return 1;
+    }
+    return generate_impl(h, nseq, prompts, prompt_len, n_new, out_stride, sp, seed_base, out_tokens, out_counts,
+                         timing);
 }
 
 extern "C" int mocha_q8b_launches_per_step(mocha_q8b *h)

@@ -79,6 +79,9 @@ _SIGS = {
     "mocha_q8b_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
     "mocha_q8b_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(MochaSampling),
                                      C.c_uint, C.c_void_p, C.c_void_p, C.POINTER(MochaTiming)]),
+    "mocha_q8b_generate_each": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                          C.POINTER(MochaSampling), C.c_uint, C.c_void_p, C.c_int, C.c_void_p,
+                                          C.POINTER(MochaTiming)]),
     "mocha_q8b_launches_per_step": (C.c_int, [C.c_void_p]),
     "mocha_q8b_bench_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_uint, C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "mocha_q8b_sample_check": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -311,6 +314,22 @@ class Q8BatchHandle:
         if self.lib.mocha_q8b_generate(self.h, nseq, pr.ctypes.data, plen, n_new, C.byref(s), seed_base,
                                        out.ctypes.data, counts.ctypes.data, C.byref(t)):
             raise RuntimeError("mocha_q8b_generate failed")
+        return [out[i, :counts[i]].tolist() for i in range(nseq)], t
+
+    def generate_each(self, prompts, n_new, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0, seed_base=42):
+        """Per-sequence token budgets n_new[i] (continuous batching refills freed slots)."""
+        import numpy as np
+        pr = np.ascontiguousarray(prompts, dtype=np.int32)
+        nseq, plen = pr.shape
+        nn = np.ascontiguousarray(n_new, dtype=np.int32)
+        stride = int(nn.max())
+        out = np.zeros((nseq, stride), np.int32)
+        counts = np.zeros(nseq, np.int32)
+        s = MochaSampling(temperature, top_k, top_p, penalty, 0)
+        t = MochaTiming()
+        if self.lib.mocha_q8b_generate_each(self.h, nseq, pr.ctypes.data, plen, nn.ctypes.data, C.byref(s), seed_base,
+                                            out.ctypes.data, stride, counts.ctypes.data, C.byref(t)):
+            raise RuntimeError("mocha_q8b_generate_each failed")
         return [out[i, :counts[i]].tolist() for i in range(nseq)], t
 
     def bench_prefill(self, n, seed, warmup, steps) -> float:

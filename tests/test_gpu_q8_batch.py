@@ -113,3 +113,22 @@ def test_sampler_bit_exact(batch, oracle_lib, temperature, top_k, top_p, penalty
     for i in range(n):
         ref, _, _ = oracle_lib.sample(logits[i], hists[i][-64:], temperature, top_k, top_p, penalty, int(seeds[i]))
         assert got[i] == ref, (i, got[i], ref)
+
+
+def test_continuous_batching_refills_slots(native, q8_model_bytes, oracle):
+    """Seven sequences with different token budgets through three slots: a slot freed by
+    a finished sequence is refilled mid-stream, and every stream still equals the
+    oracle's (sampled, per-sequence seeds)."""
+    h = native.Q8BatchHandle(0, q8_model_bytes, max_rows=48, slots=3)
+    try:
+        prompts = np.random.default_rng(18).integers(0, VOCAB, (7, 16))
+        budgets = [5, 9, 3, 12, 4, 7, 6]
+        toks, timing = h.generate_each(prompts, budgets, temperature=0.7, top_k=40, top_p=0.9, penalty=1.12,
+                                       seed_base=100)
+    finally:
+        h.close()
+    for i in range(7):
+        ref, _ = oracle.generate(prompts[i].tolist(), budgets[i], temperature=0.7, top_k=40, top_p=0.9,
+                                 penalty=1.12, seed=100 + i)
+        assert toks[i] == ref, (i, toks[i], ref)
+    assert timing.generated == sum(len(t) for t in toks)
