@@ -33,7 +33,7 @@ WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per toke
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 ONE_THREAD_TOKENS = 16         # bounded 1-thread sample of the reference engine
 SERVE_REF_SEQS = 2             # sequences of the batched job timed on the reference engine
-TRAFFIC_PER_TOKEN = 554_759_680  # DRAM read + write per k_step launch (551.35 + 3.41 MB), ncu, position 40
+TRAFFIC_PER_TOKEN = 545_005_568  # DRAM read + write per k_step launch (544.58 + 0.43 MB), ncu, positions 40-42
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
@@ -252,6 +252,10 @@ def bench_gguf(group, args):
     import mocha_native
     out = {}
     for arch, plen, nnew, wbytes, kvpos in GGUF_WORKLOADS:
+        if args.gguf_arch and arch != args.gguf_arch:
+            continue
+        if args.gguf_tokens:
+            plen, nnew = (int(v) for v in args.gguf_tokens.split(","))
         if group.rank == 0:
             mocha_gguf_model.model_path(arch)
         group.barrier()
@@ -276,6 +280,10 @@ def gguf_objects(gathered, args, world):
     hbm_peak, hbm_kind = peaks()
     res = {}
     for arch, plen, nnew, wbytes, kvpos in GGUF_WORKLOADS:
+        if arch not in gathered[0]["gguf"]:
+            continue
+        if args.gguf_tokens:
+            plen, nnew = (int(v) for v in args.gguf_tokens.split(","))
         ms = max(g["gguf"][arch]["ms"] for g in gathered)
         per_tok = ms / 1e3 / (args.steps * nnew)
         mean_pos1 = (plen + plen - 1 + nnew) / 2
@@ -401,6 +409,46 @@ def batched_cpu_baseline(model_path):
                       "penalty 1.12), generated tokens / WALL_S"}
 
 
+# phase boundaries of the persistent step's trace stamps (offset within a layer, name),
+# in the order a CTA reaches them; see mocha_q8_trace_step in include/mocha_b200.h
+TRACE_PHASES = [(0, "x_in"), (12, "qkv norm+limbs"), (11, "qkv chunk"), (13, "qkv products"), (1, "qkv stored"),
+                (14, "att q/k/v in"), (15, "att past K/V"), (16, "att softmax+PV"), (2, "attention + O added"),
+                (5, "x_mid"), (10, "ffn norm+limbs"), (9, "gate/up chunks"), (18, "gate/up products"),
+                (7, "swiglu"), (19, "h limbs"), (20, "down chunk"), (21, "down products"), (6, "down added"),
+                (8, "x_out")]
+
+
+def trace_step(pos):
+    """Phase timeline (%globaltimer stamps of every CTA) of one persistent b=1 decode step
+    at position `pos` after a 34-token prompt: median and last CTA per phase boundary, in
+    microseconds after the layer's input is complete, for layers 0, 12 and 23."""
+    import numpy as np
+
+    import mocha_native
+    import mocha_q8
+    data = np.fromfile(mocha_q8.model_path(MODEL_SEED), dtype=np.uint8)
+    h = mocha_native.Q8Handle(0, data)
+    toks, _ = h.generate(mocha_q8.random_prompt(PROMPT_LEN, PROMPT_SEED), 4)
+    st = h.trace_step(toks[0], pos).astype(np.int64)
+    rel = (st - st[:, 0].min()) / 1000.0
+    rel[st == 0] = np.nan
+    per = 24
+    for layer in (0, 12, 23):
+        base = np.nanmedian(rel[:, 2 + per * layer])
+        print(f"layer {layer} (us after x_in; median / last CTA)")
+        for k, name in TRACE_PHASES:
+            col = rel[:, 2 + per * layer + k]
+            if not np.all(np.isnan(col)):
+                print(f"  {name:22s} {np.nanmedian(col) - base:6.2f} / {np.nanmax(col) - base:6.2f}  "
+                      f"({int(np.sum(~np.isnan(col)))} CTAs)")
+    head = 2 + per * 24
+    xin = [np.nanmedian(rel[:, 2 + per * layer]) for layer in range(24)]
+    print(f"layer average {(xin[23] - xin[1]) / 22:.2f} us; head {np.nanmedian(rel[:, head]):.1f} -> "
+          f"{np.nanmax(rel[:, head + 1]):.1f} us; step {np.nanmax(rel[:, head + 2]):.1f} us")
+    h.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,11 +459,17 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the prefill and batched-serving objects")
     ap.add_argument("--serve-seqs", type=int, default=SERVE_SEQS, help="batched job size (smaller for profiling)")
     ap.add_argument("--serve-new", type=int, default=SERVE_NEW, help="tokens per sequence of the batched job")
+    ap.add_argument("--gguf-arch", default="", help="run one GGUF model (llama1b or qwen15b) in the gguf part")
+    ap.add_argument("--gguf-tokens", default="", help="PROMPT,NEW tokens of the gguf part (shorter for profiling)")
+    ap.add_argument("--trace-step", type=int, default=0,
+                    help="print the phase timeline of one persistent decode step at this position and exit")
     ap.add_argument("--parts", default="decode,prefill,batched,gguf",
                     help="comma list of workloads to run (profiling runs select one); the default runs all four")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.trace_step:
+        return trace_step(args.trace_step)
     if args.warmup < 3:
         args.warmup = 3
 
