@@ -55,6 +55,7 @@ constexpr int kGrid = mb::kSMs;  // one CTA per SM (512 threads x ~100 registers
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
 constexpr size_t kPrefetchBytes = 160 * 1024;  // per CTA: 148 CTAs x 160 KB = 24 MB of the 126 MB L2
 constexpr size_t kSmemLimit = 220 * 1024;      // dynamic shared memory per CTA
+constexpr int kMaxUnits = 3;                   // input units per thread: K <= 3 * 512 * 8 = 12,288
 
 // fp16 bits -> fp32 (exact for every fp16 value)
 MB_DEV float half_to_float(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu))); }
@@ -567,6 +568,14 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     Job jb = job(tl);
     Batch buf[2];
     if (!Staged && b0 < b1) load_batch<false>(jb, s0, lane, buf[0]);
+    // the RMSNorm gain of this thread's columns does not depend on the kernel ahead
+    // either (a normed input has at most 512 units: its K is the model width)
+    float4 gv[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (g.gain && (int)threadIdx.x < steps * 4) {
+        const int th = threadIdx.x;
+        gv[0] = __ldg(reinterpret_cast<const float4 *>(g.gain + 32 * (th >> 2) + 4 * (th & 3)));
+        gv[1] = __ldg(reinterpret_cast<const float4 *>(g.gain + 32 * (th >> 2) + 16 + 4 * (th & 3)));
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const Lay L = layout(g.cols, g.max_tiles);
     uint2 *bf = reinterpret_cast<uint2 *>(smem + L.bf);
@@ -583,21 +592,30 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
     // memory: silu(x) * up for the FFN down GEMV, x * (1/sqrt(sum x^2 / cols + eps)) * gain
     // for a normed input (the sum of squares by a block reduction first), else x.
     auto col_of = [&](int th, int h) { return 32 * (th >> 2) + 16 * h + 4 * (th & 3); };
-    auto load = [&](int c) {
-        float4 v = *reinterpret_cast<const float4 *>(g.x + c);
-        if (g.up) {  // h = silu(gate) * up, as the reference's FFN
-            const float4 u = *reinterpret_cast<const float4 *>(g.up + c);
-            v = make_float4((v.x / (1.0f + expf(-v.x))) * u.x, (v.y / (1.0f + expf(-v.y))) * u.y,
-                            (v.z / (1.0f + expf(-v.z))) * u.z, (v.w / (1.0f + expf(-v.w))) * u.w);
+    // every input value this thread quantizes (units th = tid + 512 e, e < kMaxUnits),
+    // loaded with all requests in flight at once; the gain was loaded before the wait
+    float4 xv[kMaxUnits][2], uv[kMaxUnits][2];
+    const int units = steps * 4;
+#pragma unroll
+    for (int e = 0; e < kMaxUnits; e++) {
+        const int th = threadIdx.x + e * kThreads;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            xv[e][h] = uv[e][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (th < units) {
+                xv[e][h] = *reinterpret_cast<const float4 *>(g.x + col_of(th, h));
+                if (g.up) uv[e][h] = *reinterpret_cast<const float4 *>(g.up + col_of(th, h));
+            }
         }
-        return v;
-    };
+    }
     float sc = 1.f;
     if (g.gain) {
         float ss = 0.f;
-        for (int th = threadIdx.x; th < steps * 4; th += kThreads)
+#pragma unroll
+        for (int e = 0; e < kMaxUnits; e++)
+#pragma unroll
             for (int h = 0; h < 2; h++) {
-                const float4 v = *reinterpret_cast<const float4 *>(g.x + col_of(th, h));
+                const float4 v = xv[e][h];
                 ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
             }
         ss = mb::warp_sum(ss);
@@ -608,18 +626,23 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
         for (int w = 0; w < kWarps; w++) tot += red[w];
         sc = 1.0f / sqrtf(tot / g.cols + g.eps);
     }
-    for (int base = 0; base < steps * 4; base += kThreads) {
-        const int th = base + threadIdx.x;
-        if (base + (threadIdx.x & ~31) >= steps * 4) break;  // whole warps: steps * 4 % 32 == 0
+#pragma unroll
+    for (int e = 0; e < kMaxUnits; e++) {
+        const int th = threadIdx.x + e * kThreads;
+        if (e * kThreads + (threadIdx.x & ~31) >= units) break;  // whole warps: units % 32 == 0
         const int s = th >> 2, tq = th & 3;
         float v[2][4];
         float m = 0.f, sum = 0.f;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            const int c0 = col_of(th, h);
-            float4 x = load(c0);
+            float4 x = xv[e][h];
+            if (g.up) {  // h = silu(gate) * up, as the reference's FFN
+                const float4 u = uv[e][h];
+                x = make_float4((x.x / (1.0f + expf(-x.x))) * u.x, (x.y / (1.0f + expf(-x.y))) * u.y,
+                                (x.z / (1.0f + expf(-x.z))) * u.z, (x.w / (1.0f + expf(-x.w))) * u.w);
+            }
             if (g.gain) {
-                const float4 gn = *reinterpret_cast<const float4 *>(g.gain + c0);
+                const float4 gn = gv[h];
                 x = make_float4(x.x * sc * gn.x, x.y * sc * gn.y, x.z * sc * gn.z, x.w * sc * gn.w);
             }
             v[h][0] = x.x;
@@ -787,6 +810,12 @@ int enqueue_gemv_mma(const MultiGemvMma &in, cudaStream_t s)
         g.y[i] = in.y[i];
         tiles += in.m[i].rows / 16;
         g.tile_end[i] = tiles;
+    }
+    // input units of 8 columns: at most kMaxUnits per thread, one when normed (the gain
+    // of one unit is loaded before the wait)
+    if (in.cols > kMaxUnits * kThreads * 8 || (in.gain && in.cols > kThreads * 8)) {
+        fprintf(stderr, "gguf mma gemv: %d input columns exceed the kernel's staging\n", in.cols);
+        return 1;
     }
     g.n = in.n;
     g.cols = in.cols;
