@@ -195,34 +195,44 @@ int pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args &&
 
 constexpr int kMaxHeadDim = 128;
 
-// QKV post-processing and attention of one query head (one CTA of 256 threads per head):
+// QKV post-processing and attention of one query head, split over the positions: CTA
+// (h, j) of kFaSplits per head takes positions [j c, j c + c), c = ceil((pos+1)/kFaSplits):
 //   post    the head's q and its KV head's k get the biases and RoPE exactly as
-//           k_qkv_post computes them, v its bias; the first query head of each KV group
-//           writes k and v to the cache; all three stay in shared memory (the cache row
-//           at `pos` is read from there, so no CTA reads a row another is writing);
+//           k_qkv_post computes them, v its bias; the split holding pos keeps k and v in
+//           shared memory and, for the first query head of each KV group, writes them to
+//           the cache (no split reads a cache row another is writing: the row at pos is
+//           used only by its own split);
 //   scores  one position per thread: the key row against q (float4 loads), times
 //           1/sqrt(head_dim);
-//   softmax block max, exp(s - max) in place, block sum;
+//   softmax split max m, exp(s - m) in place, split sum l;
 //   P V     warp w takes positions w, w + 8, ...; lane l accumulates dims l + 32 j
-//           (coalesced key rows), the 8 warp partials are added in warp order.
-// One launch per layer instead of two, and no per-position warp reductions.
-constexpr int kFaThreads = 256, kFaWarps = kFaThreads / 32, kFaContext = 1024;
+//           (coalesced key rows), the 8 warp partials are added in warp order;
+//   combine the split writes (m, l, acc) and takes a ticket; the last split of the head
+//           adds the splits' acc e^(m - M) / sum l e^(m - M) in split order (M their max)
+//           and resets the ticket for the next launch.
+// One launch per layer; kFaSplits x heads CTAs instead of one per head (12 for Qwen2.5-1.5B).
+constexpr int kFaThreads = 256, kFaWarps = kFaThreads / 32, kFaContext = 1024, kFaSplits = 8;
+constexpr int kFaSpan = kFaContext / kFaSplits;  // positions of one split at most
 
 __global__ void __launch_bounds__(kFaThreads)
     k_attention_fused(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                       const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
                       RopeArgs ra, const int *__restrict__ pos_ptr, float *__restrict__ kc, float *__restrict__ vc,
-                      int layer, float *__restrict__ out)
+                      int layer, float *__restrict__ out, float *__restrict__ part, unsigned *__restrict__ ticket)
 {
     pdl_enter();
     __shared__ __align__(16) float qs[kMaxHeadDim], kn[kMaxHeadDim];
     __shared__ float vn[kMaxHeadDim];
-    __shared__ float sc[kFaContext];
+    __shared__ float sc[kFaSpan];
     __shared__ float red[kFaWarps];
     __shared__ float wacc[kFaWarps][kMaxHeadDim];
-    const int h = blockIdx.x, hd = ra.head_dim, half = hd / 2, gqa = ra.heads / ra.kv_heads, kvh = h / gqa;
+    __shared__ int last;
+    const int h = blockIdx.x, j = blockIdx.y, hd = ra.head_dim, half = hd / 2, gqa = ra.heads / ra.kv_heads;
+    const int kvh = h / gqa;
     const int pos = min(*pos_ptr, ra.context - 1), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool writer = h % gqa == 0;
+    const int chunk = (pos + kFaSplits) / kFaSplits, p0 = j * chunk, p1 = min(pos + 1, p0 + chunk);
+    const bool holds_pos = p0 <= pos && pos < p1;
+    const bool writer = h % gqa == 0 && holds_pos;
     const size_t row = ((size_t)layer * ra.kv_heads + kvh) * ra.context;
     if (tid < half) {
         // NORM: pairs (2i, 2i+1); NEOX: pairs (i, i + half)
@@ -235,22 +245,24 @@ __global__ void __launch_bounds__(kFaThreads)
         }
         qs[a] = x0 * cs - x1 * sn;
         qs[b] = x0 * sn + x1 * cs;
-        x0 = k[kvh * hd + a];
-        x1 = k[kvh * hd + b];
-        if (bk) {
-            x0 += bk[kvh * hd + a];
-            x1 += bk[kvh * hd + b];
-        }
-        const float y0 = x0 * cs - x1 * sn, y1 = x0 * sn + x1 * cs;
-        kn[a] = y0;
-        kn[b] = y1;
-        if (writer) {
-            float *kd = kc + (row + pos) * hd;
-            kd[a] = y0;
-            kd[b] = y1;
+        if (holds_pos) {
+            x0 = k[kvh * hd + a];
+            x1 = k[kvh * hd + b];
+            if (bk) {
+                x0 += bk[kvh * hd + a];
+                x1 += bk[kvh * hd + b];
+            }
+            const float y0 = x0 * cs - x1 * sn, y1 = x0 * sn + x1 * cs;
+            kn[a] = y0;
+            kn[b] = y1;
+            if (writer) {
+                float *kd = kc + (row + pos) * hd;
+                kd[a] = y0;
+                kd[b] = y1;
+            }
         }
     }
-    if (tid < hd) {
+    if (tid < hd && holds_pos) {
         const float vv = v[kvh * hd + tid] + (bv ? bv[kvh * hd + tid] : 0.f);
         vn[tid] = vv;
         if (writer) vc[(row + pos) * hd + tid] = vv;
@@ -259,19 +271,19 @@ __global__ void __launch_bounds__(kFaThreads)
     const float scale = 1.0f / sqrtf((float)hd);
     const float *kb = kc + row * hd, *vb = vc + row * hd;
     float mloc = -INFINITY;
-    for (int p = tid; p <= pos; p += kFaThreads) {
+    for (int p = p0 + tid; p < p1; p += kFaThreads) {
         const float4 *kr = reinterpret_cast<const float4 *>(p == pos ? kn : kb + (size_t)p * hd);
         const float4 *qr = reinterpret_cast<const float4 *>(qs);
         float z = 0.f;
-        for (int j = 0; j < hd / 4; j++) {
-            const float4 kv = kr[j], qv = qr[j];
+        for (int jj = 0; jj < hd / 4; jj++) {
+            const float4 kv = kr[jj], qv = qr[jj];
             z = fmaf(qv.x, kv.x, z);
             z = fmaf(qv.y, kv.y, z);
             z = fmaf(qv.z, kv.z, z);
             z = fmaf(qv.w, kv.w, z);
         }
         z *= scale;
-        sc[p] = z;
+        sc[p - p0] = z;
         mloc = fmaxf(mloc, z);
     }
     mloc = mb::warp_max(mloc);
@@ -282,9 +294,9 @@ __global__ void __launch_bounds__(kFaThreads)
     for (int w = 1; w < kFaWarps; w++) m = fmaxf(m, red[w]);
     __syncthreads();  // red is reused for the sums
     float lloc = 0.f;
-    for (int p = tid; p <= pos; p += kFaThreads) {
-        const float e = expf(sc[p] - m);
-        sc[p] = e;
+    for (int p = p0 + tid; p < p1; p += kFaThreads) {
+        const float e = expf(sc[p - p0] - m);
+        sc[p - p0] = e;
         lloc += e;
     }
     lloc = mb::warp_sum(lloc);
@@ -296,24 +308,57 @@ __global__ void __launch_bounds__(kFaThreads)
     const int per = hd / 32;  // dims per lane (2 or 4)
     float acc[kMaxHeadDim / 32];
 #pragma unroll
-    for (int j = 0; j < kMaxHeadDim / 32; j++) acc[j] = 0.f;
-    for (int p = warp; p <= pos; p += kFaWarps) {
-        const float e = sc[p];
+    for (int jj = 0; jj < kMaxHeadDim / 32; jj++) acc[jj] = 0.f;
+    for (int p = p0 + warp; p < p1; p += kFaWarps) {
+        const float e = sc[p - p0];
         const float *vr = p == pos ? vn : vb + (size_t)p * hd;
 #pragma unroll
-        for (int j = 0; j < kMaxHeadDim / 32; j++)
-            if (j < per) acc[j] = fmaf(e, vr[lane + 32 * j], acc[j]);
+        for (int jj = 0; jj < kMaxHeadDim / 32; jj++)
+            if (jj < per) acc[jj] = fmaf(e, vr[lane + 32 * jj], acc[jj]);
     }
 #pragma unroll
-    for (int j = 0; j < kMaxHeadDim / 32; j++)
-        if (j < per) wacc[warp][lane + 32 * j] = acc[j];
+    for (int jj = 0; jj < kMaxHeadDim / 32; jj++)
+        if (jj < per) wacc[warp][lane + 32 * jj] = acc[jj];
     __syncthreads();
+    // this split's (m, l, unnormalised output), then the ticket
+    float *mine = part + ((size_t)h * kFaSplits + j) * (kMaxHeadDim + 2);
     for (int d = tid; d < hd; d += kFaThreads) {
         float a = 0.f;
 #pragma unroll
         for (int w = 0; w < kFaWarps; w++) a += wacc[w][d];
-        out[h * hd + d] = a / l;
+        mine[2 + d] = a;
     }
+    if (tid == 0) {
+        mine[0] = m;  // -inf for an empty split (l = 0)
+        mine[1] = l;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last = atomicAdd(ticket + h, 1u) == (unsigned)(kFaSplits - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float *hp = part + (size_t)h * kFaSplits * (kMaxHeadDim + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int jj = 0; jj < kFaSplits; jj++) M = fmaxf(M, __ldcg(hp + jj * (kMaxHeadDim + 2)));
+    float L = 0.f, f[kFaSplits];
+#pragma unroll
+    for (int jj = 0; jj < kFaSplits; jj++) {
+        const float ms = __ldcg(hp + jj * (kMaxHeadDim + 2));
+        f[jj] = ms == -INFINITY ? 0.f : expf(ms - M);
+        L = fmaf(f[jj], __ldcg(hp + jj * (kMaxHeadDim + 2) + 1), L);
+    }
+    for (int d = tid; d < hd; d += kFaThreads) {
+        float a = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < kFaSplits; jj++)
+            if (f[jj] != 0.f) a = fmaf(f[jj], __ldcg(hp + jj * (kMaxHeadDim + 2) + 2 + d), a);
+        out[h * hd + d] = a / L;
+    }
+    if (tid == 0) ticket[h] = 0u;  // every split of this launch has taken its ticket
 }
 
 __global__ void k_swiglu(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ h, int n)
@@ -364,6 +409,8 @@ struct mocha_gguf {
     RopeArgs rope{};
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
           *u = nullptr, *h = nullptr, *logits = nullptr, *kc = nullptr, *vc = nullptr;
+    float *apart = nullptr;      // attention split partials [heads][kFaSplits][head_dim max + 2]
+    unsigned *aticket = nullptr; // attention splits done per head (reset by the last split)
     int *state = nullptr;     // device [token, pos]
     int *h_state = nullptr;   // pinned staging
     int *prompt = nullptr;
@@ -434,8 +481,8 @@ int enqueue_forward(mocha_gguf *m, bool project)
         // RMSNorm folded into the fused q|k|v GEMV
         rc = (tc ? mmv({{&L.mq, m->q}, {&L.mk, m->k}, {&L.mv, m->v}}, m->x, L.attn_norm, false)
                  : multi({{&L.q, m->q}, {&L.k, m->k}, {&L.v, m->v}}, m->x, L.attn_norm, false)) ||
-             pdl(k_attention_fused, dim3(in.heads), dim3(kFaThreads), s, m->q, m->k, m->v, L.bq, L.bk, L.bv,
-                 m->rope, m->state + 1, m->kc, m->vc, l, m->att) ||
+             pdl(k_attention_fused, dim3(in.heads, kFaSplits), dim3(kFaThreads), s, m->q, m->k, m->v, L.bq, L.bk,
+                 L.bv, m->rope, m->state + 1, m->kc, m->vc, l, m->att, m->apart, m->aticket) ||
              (tc ? mmv({{&L.mo, m->x}}, m->att, nullptr, true) : multi({{&L.o, m->x}}, m->att, nullptr, true)) ||
              (tc ? mmv({{&L.mgate, m->g}, {&L.mup, m->u}}, m->x, L.ffn_norm, false)
                  : multi({{&L.gate, m->g}, {&L.up, m->u}}, m->x, L.ffn_norm, false)) ||
@@ -671,6 +718,8 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
         dev_alloc(m, (void **)&m->logits, sizeof(float) * in.vocab) ||
         dev_alloc(m, (void **)&m->kc, sizeof(float) * kv_elems) ||
         dev_alloc(m, (void **)&m->vc, sizeof(float) * kv_elems) || dev_alloc(m, (void **)&m->state, sizeof(int) * 2) ||
+        dev_alloc(m, (void **)&m->apart, sizeof(float) * in.heads * kFaSplits * (kMaxHeadDim + 2)) ||
+        dev_alloc(m, (void **)&m->aticket, sizeof(unsigned) * in.heads) ||
         dev_alloc(m, (void **)&m->prompt, sizeof(int) * in.context) ||
         dev_alloc(m, (void **)&m->seq, sizeof(sampling::SeqState)) ||
         dev_alloc(m, (void **)&m->params, sizeof(sampling::Params)) ||
@@ -679,6 +728,7 @@ int open_model(mocha_gguf *m, int device, const uint8_t *file, size_t bytes)
         return 1;
     TRY(cudaMemset(m->kc, 0, sizeof(float) * kv_elems));
     TRY(cudaMemset(m->vc, 0, sizeof(float) * kv_elems));
+    TRY(cudaMemset(m->aticket, 0, sizeof(unsigned) * in.heads));  // the attention splits' tickets
     TRY(cudaMallocHost(&m->h_state, sizeof(int) * 2));
     TRY(cudaMallocHost(&m->h_params, sizeof(sampling::Params)));
     TRY(cudaHostAlloc(&m->h_out, sizeof(int) * sampling::kOutRing, cudaHostAllocMapped));
