@@ -90,6 +90,12 @@ constexpr float kFixInv = 1.0f / 4294967296.0f;
 // reader sees from the word alone when every contributor's addition has landed.  Each
 // addition is (q << 8) + 1, q = rint(v * 2^32): the low byte only ever gains the +1s,
 // and the sum is the word shifted right arithmetically by 8 (|sum| < 2^23 fits).
+// Every accumulator has kAccRep copies and writer w adds into copy w % kAccRep: the L2
+// slice that owns a line serves its red operations one by one, and 148 writers on one
+// copy queue behind each other; readers add the copies' integer sums (exact, so the
+// result does not depend on the split).  Two copies measured best: each further copy
+// costs the 148 readers one more 32-byte poll per round.
+constexpr int kAccRep = 2;
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
@@ -554,31 +560,49 @@ MB_DEV size_t kv_index(int layer, int kvh, int pos)
     return (((size_t)layer * KV_HEADS + kvh) * CONTEXT + pos) * HEAD_DIM;
 }
 
-// S.xs += the 896 counted fixed-point sums at acc once each holds `count` additions:
-// thread t < 224 polls its four words (one 32-byte request per round).  Every consumer
-// thread returns the same verdict (ends with a barrier).
+// S.xs += the 896 counted fixed-point sums at acc once they hold `count` additions in
+// all: writer w adds to copy w % kAccRep (copies DIM words apart), so copy r waits for
+// ceil((count - r) / kAccRep) of them.  Thread t < 224 polls its four words of every
+// copy (one 32-byte request per copy and round).  Every consumer thread returns the
+// same verdict (ends with a barrier).
 MB_DEV bool add_sums(Ctx &c, const unsigned long long *acc, unsigned count)
 {
     int ok = 1;
     if (c.ct < DIM / 4) {
-        unsigned long long v[4];
-        dw_load4(acc + 4 * c.ct, v);
+        unsigned long long v[kAccRep][4];
+        unsigned need[kAccRep];
+#pragma unroll
+        for (int r = 0; r < kAccRep; r++) {
+            need[r] = (count + kAccRep - 1 - r) / kAccRep;
+            dw_load4(acc + r * DIM + 4 * c.ct, v[r]);
+        }
         long long t0 = 0;
-        while ((unsigned)(v[0] & 0xFFu) != count || (unsigned)(v[1] & 0xFFu) != count ||
-               (unsigned)(v[2] & 0xFFu) != count || (unsigned)(v[3] & 0xFFu) != count) {
+        for (;;) {
+            bool done = true;
+#pragma unroll
+            for (int r = 0; r < kAccRep; r++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) done = done && (unsigned)(v[r][j] & 0xFFu) == need[r];
+            if (done) break;
             if (t0 == 0) {
                 t0 = clock64();
             } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
                 ok = 0;
                 break;
             }
-            dw_load4(acc + 4 * c.ct, v);
+#pragma unroll
+            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * DIM + 4 * c.ct, v[r]);
         }
+        long long s[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int r = 0; r < kAccRep; r++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) s[j] += (long long)v[r][j] >> 8;
         float4 x = *reinterpret_cast<const float4 *>(c.S.xs + 4 * c.ct);
-        x.x += __ll2float_rn((long long)v[0] >> 8) * kFixInv;
-        x.y += __ll2float_rn((long long)v[1] >> 8) * kFixInv;
-        x.z += __ll2float_rn((long long)v[2] >> 8) * kFixInv;
-        x.w += __ll2float_rn((long long)v[3] >> 8) * kFixInv;
+        x.x += __ll2float_rn(s[0]) * kFixInv;
+        x.y += __ll2float_rn(s[1]) * kFixInv;
+        x.z += __ll2float_rn(s[2]) * kFixInv;
+        x.w += __ll2float_rn(s[3]) * kFixInv;
         *reinterpret_cast<float4 *>(c.S.xs + 4 * c.ct) = x;
     }
     return cbar_and(ok) != 0;
@@ -787,12 +811,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     // share of the other set, which the next step uses (the last step that used it has
     // finished: it was the previous launch on this stream)
     const int set = (int)(epoch & 1u);
-    unsigned long long *dacc = scr.dacc + (size_t)set * LAYERS * DIM;
-    unsigned long long *xacc = scr.xacc + (size_t)set * LAYERS * DIM;
+    unsigned long long *dacc = scr.dacc + (size_t)set * kAccRep * LAYERS * DIM;
+    unsigned long long *xacc = scr.xacc + (size_t)set * kAccRep * LAYERS * DIM;
     {
-        unsigned long long *od = scr.dacc + (size_t)(set ^ 1) * LAYERS * DIM;
-        unsigned long long *ox = scr.xacc + (size_t)(set ^ 1) * LAYERS * DIM;
-        const int lo = LAYERS * DIM * cta / kCTAs, hi = LAYERS * DIM * (cta + 1) / kCTAs;
+        unsigned long long *od = scr.dacc + (size_t)(set ^ 1) * kAccRep * LAYERS * DIM;
+        unsigned long long *ox = scr.xacc + (size_t)(set ^ 1) * kAccRep * LAYERS * DIM;
+        const int lo = kAccRep * LAYERS * DIM * cta / kCTAs, hi = kAccRep * LAYERS * DIM * (cta + 1) / kCTAs;
         for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) {
             od[i] = 0ull;
             ox[i] = 0ull;
@@ -1094,8 +1118,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 for (int i = 0; i < 4; i++) {
                     if (i < otn && (c.lane & 3) == 0) {
                         const int r0 = 16 * (ot0 + i) + g, r1 = r0 + 8;
-                        fix_add(xacc + (size_t)l * DIM + r0, pacc[i][0] * f);
-                        fix_add(xacc + (size_t)l * DIM + r1, pacc[i][1] * f);
+                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0] * f);
+                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1] * f);
                     }
                 }
             }
@@ -1104,7 +1128,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 2);
 
         // ---- x_mid = x_in + the attention block, all-reduced over the attention CTAs
-        if (!add_sums(c, xacc + (size_t)l * DIM, (unsigned)(HEADS * splits))) return drain(c, cur);
+        if (!add_sums(c, xacc + (size_t)kAccRep * l * DIM, (unsigned)(HEADS * splits))) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
 
         // ---- RMSNorm -> gate/up -> SwiGLU
@@ -1186,8 +1210,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     for (int i = 0; i < 4; i++) {
                         if (i < n && (c.lane & 3) == 0) {
                             const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
-                            fix_add(dacc + (size_t)l * DIM + r0, pacc[i][0] * f);
-                            fix_add(dacc + (size_t)l * DIM + r1, pacc[i][1] * f);
+                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0] * f);
+                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1] * f);
                         }
                     }
                 }
@@ -1199,7 +1223,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
         // all-reduce: once all 148 CTAs' additions are complete every CTA adds the sums
         // to its x_mid -- the next layer's input
-        if (!add_sums(c, dacc + (size_t)l * DIM, kCTAs)) return drain(c, cur);
+        if (!add_sums(c, dacc + (size_t)kAccRep * l * DIM, kCTAs)) return drain(c, cur);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
     }
 
@@ -1424,7 +1448,7 @@ size_t smem_bytes() { return sizeof(Smem); }
 
 size_t scratch_words()
 {
-    return (size_t)DIM + (size_t)kReplicas * kStrideKv + kPartWords + 4 * (size_t)LAYERS * DIM;
+    return (size_t)DIM + (size_t)kReplicas * kStrideKv + kPartWords + 4 * (size_t)kAccRep * LAYERS * DIM;
 }
 
 void carve_scratch(unsigned long long *base, Scratch *scr)
@@ -1433,7 +1457,7 @@ void carve_scratch(unsigned long long *base, Scratch *scr)
     scr->kv = scr->q + DIM;
     scr->part = scr->kv + kReplicas * kStrideKv;
     scr->dacc = scr->part + kPartWords;
-    scr->xacc = scr->dacc + 2 * (size_t)LAYERS * DIM;
+    scr->xacc = scr->dacc + 2 * (size_t)kAccRep * LAYERS * DIM;
 
 }
 
