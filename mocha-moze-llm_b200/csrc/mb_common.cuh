@@ -26,11 +26,14 @@ MB_DEV float warp_sum(float v)
     return v;
 }
 
+// Maximum over the warp in one instruction (sm_100a's floating-point redux): the
+// result is one of the inputs, as a tree of fmaxf would give, but without five
+// dependent shuffles.  NaN inputs are skipped, as fmaxf skips them.
 MB_DEV float warp_max(float v)
 {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
 }
 
 // Weights are read once per token: bypass L1 and give the L2 lines an evict-first

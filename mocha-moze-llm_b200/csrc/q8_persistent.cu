@@ -79,6 +79,8 @@ constexpr int kOStepBytes = kDownTiles * 512;        // one 32-column step of a 
 constexpr int kOHeadBytes = 2 * kOStepBytes;
 constexpr int kGpStride = kConsumerWarps + 1;  // padded: conflict-free row sums
 constexpr int kKStride = HEAD_DIM + 4;         // cached key row in shared memory: conflict-free float4 reads
+constexpr int kMaxAttnWarps = (kAttnLenMax + 7) / 8;  // warps holding positions of a split (8 each)
+static_assert(kMaxAttnWarps <= kConsumerWarps, "attention warps");
 constexpr int kStrideKv = replica_stride(2 * KV);
 constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: v + kMagic rounds v to an integer (|v| < 2^22)
 static_assert(DIM % 64 == 0 && kCTAs % 4 == 0, "layout");
@@ -106,14 +108,13 @@ struct Smem {
             float k[kAttnLenMax][kKStride];
             float v[kAttnLenMax][HEAD_DIM];
             float q[HEAD_DIM];
-            float wp[kConsumerWarps][HEAD_DIM + 4];  // per-warp partials: max, sum of weights, 64 accumulators
+            float wp[kConsumerWarps][HEAD_DIM + 4];  // per-warp partials: max, sum of weights, -, -, 64 accumulators
         } att;
         float hl[kHeadSlice];      // this CTA's slice of the logits
     } u;
     __align__(16) uint2 bf[kSteps][32];  // B fragments of the current 896-wide input (lanes 12..31 zero)
     __align__(16) uint2 bfh[2][32];      // B fragments of the SwiGLU slice (lanes 12..31 zero)
     __align__(16) uint2 bfo[2][32];      // B fragments of this split's attention output (64 dims)
-    __align__(16) float ost[2][32];      // that output, unnormalised, before quantization
     float so;                            // its scale / 254
     float att_m, att_l, att_w;           // this split's max and sum of weights; its weight in the head
     float gp[5 * 16][kGpStride];   // per-warp partial row sums of the current job (<= 5 tiles)
@@ -123,6 +124,11 @@ struct Smem {
     __align__(16) float red[kConsumerWarps][8];  // also read as 64-bit keys (block_max)
     float rc[HEAD_DIM / 2], rs[HEAD_DIM / 2];  // RoPE cos/sin at pos
     Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors
+    // pointers the layer loop needs, copied from global memory once: a pointer load from
+    // global memory feeding a second load puts two L2 round trips on the path
+    const float *gain[2][LAYERS];  // RMSNorm gains: [0] attention, [1] FFN
+    const uint8_t *ofrag;          // the plan's O-by-head fragments and scales
+    const float *oscale;
     unsigned long long full[kSlots];
     int flag;
     int token, pos;
@@ -362,11 +368,13 @@ MB_DEV void put_limbs(Smem &S, int t, const float (&n)[4], float m)
     b[2 * (8 + tig) + h] = p2;
 }
 
+// Maximum of m >= 0 over each aligned 16-lane half of the warp (two whole-warp reduxes,
+// each seeing the other half as zeros).
 MB_DEV float group_max16(float m)
 {
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    return m;
+    const bool lo = (threadIdx.x & 16) == 0;
+    const float a = mb::warp_max(lo ? m : 0.f), b = mb::warp_max(lo ? 0.f : m);
+    return lo ? a : b;
 }
 
 // The four gain values of thread ct's columns (see norm_quantize), loaded ahead of use.
@@ -455,11 +463,15 @@ struct Tiles {
 };
 
 // Units (tile, group), U = kGroups * T, warp cw takes [U cw/16, U (cw+1)/16); its row
-// sums go to S.gp[row][cw] and row_sum() adds the warps of a row in order.
+// sums go to S.gp[row][cw] and row_sum() adds the warps of a row in order.  MAXU >= the
+// units of any warp.  Every one of the MAXU iterations loads and multiplies (an
+// iteration past the warp's last unit reads the job's last unit and adds zeros): with
+// no branch around the shared-memory loads they are all issued up front, and the
+// units' MMA and shuffle latencies overlap instead of adding up.
+template <int MAXU>
 MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
 {
     Smem &S = *Sp;
-    constexpr int MAXU = 5;  // units per warp for T <= 5
     const int U = kGroups * tl.T;
     const int u0 = U * cw / kConsumerWarps, n = U * (cw + 1) / kConsumerWarps - u0;
     const int g = lane >> 2, tig = lane & 3;
@@ -467,39 +479,37 @@ MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
     for (int i = 0; i < MAXU; i++) {
-        if (i < n) {
-            const int u = u0 + i, t = u / kGroups, grp = u - t * kGroups, ch = t >> 1;
-            const uint8_t *fr = ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2];
-            const float *sc = ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2];
-            fr += (t & 1) * kTileBytes;
-            sc += (t & 1) * 16 * kGroups;
-            int d[4] = {0, 0, 0, 0};
+        const bool live = i < n;
+        const int u = min(u0 + i, U - 1), t = u / kGroups, grp = u - t * kGroups, ch = t >> 1;
+        const uint8_t *fr = ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2];
+        const float *sc = ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2];
+        fr += (t & 1) * kTileBytes;
+        sc += (t & 1) * 16 * kGroups;
+        int d[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int ks = 2 * grp + h;
-                uint4 a;
-                if (tl.half) {
-                    const uint2 v = *reinterpret_cast<const uint2 *>(fr + ((size_t)ks * 32 + lane) * 8);
-                    a = make_uint4(v.x, 0u, v.y, 0u);
-                } else {
-                    a = *reinterpret_cast<const uint4 *>(fr + ((size_t)ks * 32 + lane) * 16);
-                }
-                mma_s8(d, a, S.bf[ks][lane]);
+        for (int h = 0; h < 2; h++) {
+            const int ks = 2 * grp + h;
+            uint4 a;
+            if (tl.half) {
+                const uint2 v = *reinterpret_cast<const uint2 *>(fr + ((size_t)ks * 32 + lane) * 8);
+                a = make_uint4(v.x, 0u, v.y, 0u);
+            } else {
+                a = *reinterpret_cast<const uint4 *>(fr + ((size_t)ks * 32 + lane) * 16);
             }
-            float v0, v1;
-            combine(d, v0, v1);
-            if (tig == 0) {
-                const float f = S.sxs[grp];
-                const float p0 = v0 * (sc[g * kGroups + grp] * f);
-                const float p1 = tl.half ? 0.f : v1 * (sc[(g + 8) * kGroups + grp] * f);
-                if (t == t0) {
-                    acc[0][0] += p0;
-                    acc[0][1] += p1;
-                } else {
-                    acc[1][0] += p0;
-                    acc[1][1] += p1;
-                }
-            }
+            mma_s8(d, a, S.bf[ks][lane]);
+        }
+        float v0, v1;
+        combine(d, v0, v1);
+        // (a half tile has 8 rows of scales: row g stands in for the absent row g + 8)
+        const float f = S.sxs[grp];
+        const float s0 = sc[g * kGroups + grp], s1 = sc[(tl.half ? g : g + 8) * kGroups + grp];
+        if (tig == 0) {
+            const float p0 = live ? v0 * (s0 * f) : 0.f;
+            const float p1 = live && !tl.half ? v1 * (s1 * f) : 0.f;
+            acc[0][0] += t == t0 ? p0 : 0.f;
+            acc[0][1] += t == t0 ? p1 : 0.f;
+            acc[1][0] += t == t0 ? 0.f : p0;
+            acc[1][1] += t == t0 ? 0.f : p1;
         }
     }
     if (tig == 0 && n == 0) {  // fewer units than warps (T = 1): an empty contribution
@@ -535,23 +545,24 @@ MB_DEV float row_sum(const Ctx &c, int T, int row)
 
 // Down projection, one 32-column step of this CTA's hidden units for all 896 rows
 // ([kDownTiles][32 lanes][16 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
-// partials (v * weight scale) are added to acc[tile][row g | row g + 8].
+// partials (v * weight scale) are added to acc[tile][row g | row g + 8].  A warp with
+// three tiles also multiplies a fourth (the next warp's first) into an acc entry its
+// caller ignores: no branch around the loads.
 MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float (&acc)[4][2])
 {
-    const int t0 = kDownTiles * c.cw / kConsumerWarps, n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
+    const int t0 = kDownTiles * c.cw / kConsumerWarps;
     const uint2 b = bfs[c.lane];
     const int g = c.lane >> 2;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        if (i < n) {
-            int d[4] = {0, 0, 0, 0};
-            mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)(t0 + i) * 32 + c.lane) * 16), b);
-            float v0, v1;
-            combine(d, v0, v1);
-            const int r0 = 16 * (t0 + i) + g;
-            acc[i][0] = fmaf(v0, sw[r0], acc[i][0]);
-            acc[i][1] = fmaf(v1, sw[r0 + 8], acc[i][1]);
-        }
+        const int t = min(t0 + i, kDownTiles - 1);
+        int d[4] = {0, 0, 0, 0};
+        mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16), b);
+        float v0, v1;
+        combine(d, v0, v1);
+        const int r0 = 16 * t + g;
+        acc[i][0] = fmaf(v0, sw[r0], acc[i][0]);
+        acc[i][1] = fmaf(v1, sw[r0 + 8], acc[i][1]);
     }
 }
 
@@ -784,6 +795,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     const uint32_t c_end = project ? c1 : a.P->head_begin[cta];  // head chunks only when projecting
     for (uint32_t j = threadIdx.x; j < c_end - c0 && j < (uint32_t)kMaxChunksPerCta; j += kThreads)
         S.desc[j] = a.P->chunks[c0 + j];
+    if (threadIdx.x < 2 * LAYERS) {
+        const q8::Layer &ly = a.M->layer[threadIdx.x >> 1];
+        S.gain[threadIdx.x & 1][threadIdx.x >> 1] = (threadIdx.x & 1) ? ly.ffn_norm : ly.attn_norm;
+    }
+    if (threadIdx.x == 2 * LAYERS) {
+        S.ofrag = a.P->ofrag;
+        S.oscale = a.P->oscale;
+    }
     __syncthreads();
     Ctx c{S,
           a.sy,
@@ -854,7 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 
     // the RMSNorm gains are loaded a layer ahead and carried in registers (a load placed
     // next to its use would put two dependent L2 round trips on the critical path)
-    float4 g_attn = load_gain(c.ct, M->layer[0].attn_norm), g_ffn = load_gain(c.ct, M->layer[0].ffn_norm);
+    float4 g_attn = load_gain(c.ct, S.gain[0][0]), g_ffn = load_gain(c.ct, S.gain[1][0]);
     for (int l = 0; l < LAYERS; l++) {
         // K/V of past positions for this CTA's attention split: no dependency on this
         // step, copied asynchronously while the QKV phase runs
@@ -871,8 +890,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             asm volatile("cp.async.commit_group;" ::: "memory");
             // this head's O columns and scales, wanted after the attention: into L2 now
             if (c.ct == 0) {
-                const uint8_t *of = a.P->ofrag + (size_t)(l * HEADS + unit.head) * kOHeadBytes;
-                const float *os = a.P->oscale + (size_t)(l * HEADS + unit.head) * DIM;
+                const uint8_t *of = S.ofrag + (size_t)(l * HEADS + unit.head) * kOHeadBytes;
+                const float *os = S.oscale + (size_t)(l * HEADS + unit.head) * DIM;
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(of), "r"(kOHeadBytes) : "memory");
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(os), "r"(DIM * 4) : "memory");
             }
@@ -881,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
             norm_quantize(&S, c.ct, g_attn, 0);
-            g_attn = load_gain(c.ct, M->layer[min(l + 1, LAYERS - 1)].attn_norm);
+            g_attn = load_gain(c.ct, S.gain[0][min(l + 1, LAYERS - 1)]);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 12);
             const uint8_t *w = take(c, cur, QKV);
             if (!w) return drain(c, cur);
@@ -891,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             const uint8_t *frag = w + sizeof(ChunkHdr);
             const float *sc = reinterpret_cast<const float *>(frag + kHalfBytes);
             const float *bias = sc + 8 * kGroups;
-            gemv_mma(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
+            gemv_mma<1>(&S, c.cw, c.lane, Tiles{{frag, frag, frag}, {sc, sc, sc}, 1, 1});
             cbar();
             if (c.ct < npair) {
                 stamp(a, cta, c.ct, 2 + l * kTraceLayer + 13);
@@ -944,8 +963,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             uint4 ofr[2][4];
             float osc[4][2];
             {
-                const uint8_t *of = a.P->ofrag + (size_t)(l * HEADS + h) * kOHeadBytes;
-                const float *os = a.P->oscale + (size_t)(l * HEADS + h) * DIM;
+                const uint8_t *of = S.ofrag + (size_t)(l * HEADS + h) * kOHeadBytes;
+                const float *os = S.oscale + (size_t)(l * HEADS + h) * DIM;
                 const int g = c.lane >> 2;
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -1017,17 +1036,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const float lw = mb::warp_sum(qd == 0 ? e : 0.f);  // each position sits in four lanes
                 float a0 = 0.f, a1 = 0.f;
                 const float *vb = S.u.att.v[8 * c.cw];
+                // rows past np read the next rows of the buffer (or, for row 8 * 12 + 7 =
+                // kAttnLenMax, the query after it) and enter as zeros: no branch around
+                // the loads
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     const float ej = __shfl_sync(0xffffffffu, e, j);  // lane j holds position 8 cw + j
-                    if (8 * c.cw + j < np) {
-                        a0 = fmaf(ej, vb[j * HEAD_DIM + c.lane], a0);
-                        a1 = fmaf(ej, vb[j * HEAD_DIM + 32 + c.lane], a1);
-                    }
+                    const bool in = 8 * c.cw + j < np;
+                    const float x0 = vb[j * HEAD_DIM + c.lane], x1 = vb[j * HEAD_DIM + 32 + c.lane];
+                    a0 = fmaf(ej, in ? x0 : 0.f, a0);
+                    a1 = fmaf(ej, in ? x1 : 0.f, a1);
                 }
                 float *wp = S.u.att.wp[c.cw];
-                wp[2 + c.lane] = a0;
-                wp[2 + 32 + c.lane] = a1;
+                wp[4 + c.lane] = a0;
+                wp[4 + 32 + c.lane] = a1;
                 if (c.lane == 0) {
                     wp[0] = m;
                     wp[1] = lw;
@@ -1035,17 +1057,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             }
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 16);
-            if (c.ct < HEAD_DIM) {
-                float mx = -INFINITY;
-                for (int w = 0; w < nw; w++) mx = fmaxf(mx, S.u.att.wp[w][0]);
-                float lsum = 0.f, acc = 0.f;
-                for (int w = 0; w < nw; w++) {
-                    const float f = expf(S.u.att.wp[w][0] - mx);
-                    lsum = fmaf(f, S.u.att.wp[w][1], lsum);
-                    acc = fmaf(f, S.u.att.wp[w][2 + c.ct], acc);
+            // Warp 0 merges the warps' partials at the split's max and quantizes the
+            // result straight into S.bfo: lane t (t = lane % 16; both halves compute the
+            // same) owns dims 32 ks + 16 hh + 4 tig + {0..3}, ks = t >> 3, tig = (t >> 1) & 3,
+            // hh = t & 1 -- its limbs' place in the B fragments, as in quantize_slice.
+            // Lane w < nw holds warp w's max and its factor exp(m_w - max) (one expf per
+            // lane); the sums run over w in order with the factors shuffled in, and rows
+            // of idle warps enter as zeros (no branch around the loads).
+            if (c.cw == 0) {
+                const float mw = c.lane < nw ? S.u.att.wp[c.lane][0] : -INFINITY;
+                const float mx = mb::warp_max(mw);
+                const float fw = c.lane < nw ? expf(mw - mx) : 0.f;
+                const int t = c.lane & 15, ks = t >> 3, tig = (t >> 1) & 3, hh = t & 1;
+                const int d0 = 32 * ks + 16 * hh + 4 * tig;
+                float lsum = 0.f;
+                float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int w = 0; w < kMaxAttnWarps; w++) {
+                    const float f = __shfl_sync(0xffffffffu, fw, w);
+                    const bool in = w < nw;
+                    const float lw = S.u.att.wp[w][1];
+                    const float4 p = *reinterpret_cast<const float4 *>(&S.u.att.wp[w][4 + d0]);
+                    lsum = fmaf(f, in ? lw : 0.f, lsum);
+                    o[0] = fmaf(f, in ? p.x : 0.f, o[0]);
+                    o[1] = fmaf(f, in ? p.y : 0.f, o[1]);
+                    o[2] = fmaf(f, in ? p.z : 0.f, o[2]);
+                    o[3] = fmaf(f, in ? p.w : 0.f, o[3]);
                 }
-                S.ost[c.ct >> 5][c.ct & 31] = acc;
-                if (c.ct == 0) {
+                if (c.lane == 0) {
                     S.att_m = mx;
                     S.att_l = lsum;
                     if (splits > 1) {  // for the other splits of this head
@@ -1055,9 +1094,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                         dw_store(ml + 1, lsum, ptag);
                     }
                 }
+                const float m = mb::warp_max(fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3]))));
+                const float inv = m > 0.f ? 127.f / m : 0.f;
+                const float q[4] = {o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv};
+                uint32_t p0, p1, p2;
+                limbs4(q, p0, p1, p2);
+                if (c.lane < 16) {
+                    uint32_t *b = reinterpret_cast<uint32_t *>(&S.bfo[ks][0]);
+                    b[2 * tig + hh] = p0;
+                    b[2 * (4 + tig) + hh] = p1;
+                    b[2 * (8 + tig) + hh] = p2;
+                }
+                if (c.lane == 0) S.so = m / (127.f * 254.f);
             }
             cbar();
-            quantize_slice(c, S.ost, 2, S.bfo, &S.so);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 3);
             // warp 0 starts reading the splits' (max, sum) before the products
             const uint32_t ptag = make_tag(epoch, l, PH_ATTN);
@@ -1068,19 +1118,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 w1 = dw_load(ml + 1);
             }
             // the unnormalised output through O's 64 columns of this head: P = O_h acc
+            // (a warp with three tiles also multiplies a copy of its last; unused)
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+            const uint2 bo[2] = {S.bfo[0][c.lane], S.bfo[1][c.lane]};
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                if (i < otn) {
 #pragma unroll
-                    for (int ks = 0; ks < 2; ks++) {
-                        int d[4] = {0, 0, 0, 0};
-                        mma_s8(d, ofr[ks][i], S.bfo[ks][c.lane]);
-                        float v0, v1;
-                        combine(d, v0, v1);
-                        pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
-                        pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
-                    }
+                for (int ks = 0; ks < 2; ks++) {
+                    int d[4] = {0, 0, 0, 0};
+                    mma_s8(d, ofr[ks][i], bo[ks]);
+                    float v0, v1;
+                    combine(d, v0, v1);
+                    pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
+                    pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
                 }
             }
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
@@ -1134,7 +1184,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         // ---- RMSNorm -> gate/up -> SwiGLU
         {
             norm_quantize(&S, c.ct, g_ffn, 0);
-            g_ffn = load_gain(c.ct, M->layer[min(l + 1, LAYERS - 1)].ffn_norm);
+            g_ffn = load_gain(c.ct, S.gain[1][min(l + 1, LAYERS - 1)]);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
             // this layer's gate/up chunks (2 or 3, all resident in the ring together):
             // slots cur.k .. cur.k + ngu - 1
@@ -1167,7 +1217,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             tl.sc[0] = reinterpret_cast<const float *>(tl.frag[0] + (size_t)min(2, T) * kTileBytes);
             tl.sc[1] = reinterpret_cast<const float *>(tl.frag[1] + (size_t)max(1, min(2, T - 2)) * kTileBytes);
             tl.sc[2] = reinterpret_cast<const float *>(tl.frag[2] + (size_t)max(1, min(2, T - 4)) * kTileBytes);
-            gemv_mma(&S, c.cw, c.lane, tl);
+            gemv_mma<5>(&S, c.cw, c.lane, tl);
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 18);
             // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and

@@ -46,7 +46,7 @@ struct Plan {
     uint32_t head_lo[kCTAs + 1];           // contiguous vocabulary rows per CTA
 };
 
-constexpr int kMaxChunksPerCta = 232;
+constexpr int kMaxChunksPerCta = 184;  // >= 24 layers x 6 + 33 head chunks
 
 struct Sync {
     unsigned epoch;  // 1 .. 2^24-1, tags the step's data words
