@@ -78,6 +78,10 @@ constexpr int kPartWords = HEADS * kMaxSplit * 2;   // (max, sum of weights) of 
 constexpr int kOStepBytes = kDownTiles * 512;        // one 32-column step of a head's O columns, all 896 rows
 constexpr int kOHeadBytes = 2 * kOStepBytes;
 constexpr int kGpStride = kConsumerWarps + 1;  // padded: conflict-free row sums
+// The thread that starts the ring's bulk copies in the layer loop: lane 0 of the last
+// warp, which has the least work on the critical path (warp 0 merges and quantizes;
+// warps 14 and 15 sit out the grouped matrix-vector products).
+constexpr int kIssuer = kNT - 32;
 constexpr int kKStride = HEAD_DIM + 4;         // cached key row in shared memory: conflict-free float4 reads
 constexpr int kMaxAttnWarps = (kAttnLenMax + 7) / 8;  // warps holding positions of a split (8 each)
 static_assert(kMaxAttnWarps <= kConsumerWarps, "attention warps");
@@ -117,7 +121,7 @@ struct Smem {
     __align__(16) uint2 bfo[2][32];      // B fragments of this split's attention output (64 dims)
     float so;                            // its scale / 254
     float att_m, att_l, att_w;           // this split's max and sum of weights; its weight in the head
-    float gp[5 * 16][kGpStride];   // per-warp partial row sums of the current job (<= 5 tiles)
+    float gp[5 * 16][kGpStride];   // per-group partial row sums of the current job (<= 5 tiles)
     float sxs[kGroups];            // input scale / 254 per group
     __align__(16) float hst[2][32];  // this CTA's SwiGLU outputs at their column in each down step
     float sh;                      // their scale / 254
@@ -278,10 +282,17 @@ MB_DEV unsigned long long dw_load(const unsigned long long *p)
     return w;
 }
 
-// one counted fixed-point addition (the result is not returned: a reduction in L2)
+// One counted fixed-point addition (the result is not returned: a reduction in L2).
+// rint(v * 2^32) from two 32-bit conversions, which issue faster than one 64-bit one:
+// hi = rint(v * 2^8), then the remainder v * 2^8 - hi (exact, |.| <= 1/2) scaled by 2^24;
+// hi * 2^24 is even, so rint(hi * 2^24 + r * 2^24) = hi * 2^24 + rint(r * 2^24), ties
+// included.  Exact for |v| < 2^23, the format's range.
 MB_DEV void fix_add(unsigned long long *p, float v)
 {
-    const unsigned long long q = (unsigned long long)__float2ll_rn(v * kFixScale);
+    const float x = v * 256.f;
+    const int hi = __float2int_rn(x);
+    const int lo = __float2int_rn((x - (float)hi) * 16777216.f);
+    const unsigned long long q = (unsigned long long)(((long long)hi << 24) + lo);
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((q << 8) + 1ull) : "memory");
 }
 
@@ -353,15 +364,19 @@ MB_DEV void limbs4(const float (&q)[4], uint32_t &p0, uint32_t &p1, uint32_t &p2
 MB_DEV int quant_col(int t) { return 32 * (t >> 3) + 16 * (t & 1) + 4 * ((t >> 1) & 3); }
 
 // Four values n[] of thread t (group max m already reduced over its 16 lanes) -> limbs
-// into S.bf and, from the group's first thread, the group scale / 254.
+// into S.bf and, from the group's first thread, the group scale / 254.  127 / m comes
+// from the fast divide (within 2 ulp: |q| stays <= 127 to within rounding), so the
+// values the limbs stand for are off by about 1e-7 relative, the order of the limbs'
+// own resolution; an IEEE division here cost two of them per quantization on the
+// critical path.
 MB_DEV void put_limbs(Smem &S, int t, const float (&n)[4], float m)
 {
     const int ks = t >> 3, tig = (t >> 1) & 3, h = t & 1;
-    const float inv = m > 0.f ? 127.f / m : 0.f;
+    const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
     const float q[4] = {n[0] * inv, n[1] * inv, n[2] * inv, n[3] * inv};
     uint32_t p0, p1, p2;
     limbs4(q, p0, p1, p2);
-    if ((t & 15) == 0) S.sxs[ks >> 1] = m / (127.f * 254.f);
+    if ((t & 15) == 0) S.sxs[ks >> 1] = m * (1.0f / (127.f * 254.f));
     uint32_t *b = reinterpret_cast<uint32_t *>(&S.bf[ks][0]);
     b[2 * tig + h] = p0;
     b[2 * (4 + tig) + h] = p1;
@@ -385,7 +400,8 @@ MB_DEV float4 load_gain(int ct, const float *gain)
 }
 
 // RMSNorm of S.xs with the gain g (this thread's four columns, from load_gain), in the
-// reference's rounding ((x * s) * g, s = 1/sqrt(sum x^2 / DIM + eps)), quantized
+// reference's form ((x * s) * g, s = 1/sqrt(sum x^2 / DIM + eps)) with s from the
+// hardware reciprocal square root (within 2 ulp of the rounded 1/sqrtf), quantized
 // straight into S.bf / S.sxs; with keep the normalised vector also goes to S.ns.
 // Consumer threads ct < 256 (warps 0..7) work; every consumer thread calls it (two
 // consumer barriers).
@@ -409,7 +425,7 @@ MB_DEV void norm_quantize(Smem *Sp, int ct, float4 g, int keep)
         float sum = 0.f;
 #pragma unroll
         for (int w = 0; w < 7; w++) sum += S.red[w][0];
-        const float s = 1.0f / sqrtf(sum / DIM + RMS_EPS);
+        const float s = rsqrtf(sum * (1.0f / DIM) + RMS_EPS);
         const float n[4] = {(x.x * s) * g.x, (x.y * s) * g.y, (x.z * s) * g.z, (x.w * s) * g.w};
         if (keep) *reinterpret_cast<float4 *>(S.ns + col) = make_float4(n[0], n[1], n[2], n[3]);
         put_limbs(S, t, n, pm * s);
@@ -428,7 +444,7 @@ MB_DEV void quantize_slice(Ctx &c, const float (*src)[32], int nks, uint2 (*bf)[
         if (live) v = *reinterpret_cast<const float4 *>(&src[ks][16 * h + 4 * tig]);
         float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         m = mb::warp_max(m);
-        const float inv = m > 0.f ? 127.f / m : 0.f;
+        const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
         const float q[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
         uint32_t p0, p1, p2;
         limbs4(q, p0, p1, p2);
@@ -438,7 +454,7 @@ MB_DEV void quantize_slice(Ctx &c, const float (*src)[32], int nks, uint2 (*bf)[
             b[2 * (4 + tig) + h] = p1;
             b[2 * (8 + tig) + h] = p2;
         }
-        if (c.lane == 0) *scale = m / (127.f * 254.f);
+        if (c.lane == 0) *scale = m * (1.0f / (127.f * 254.f));
     }
     cbar();
 }
@@ -462,84 +478,56 @@ struct Tiles {
     int T, half;
 };
 
-// Units (tile, group), U = kGroups * T, warp cw takes [U cw/16, U (cw+1)/16); its row
-// sums go to S.gp[row][cw] and row_sum() adds the warps of a row in order.  MAXU >= the
-// units of any warp.  Every one of the MAXU iterations loads and multiplies (an
-// iteration past the warp's last unit reads the job's last unit and adds zeros): with
-// no branch around the shared-memory loads they are all issued up front, and the
-// units' MMA and shuffle latencies overlap instead of adding up.
-template <int MAXU>
+// Tiles x groups: warp w < kGroups takes group w (k-steps 2w, 2w + 1) of every tile, so
+// it loads its two B fragments and its input scale once and reuses them across the tiles
+// (shared-memory bandwidth, not latency, bounds this loop); its row sums go to
+// S.gp[row][w] and row_sum() adds the 14 groups of a row in order.  MAXT >= T; an
+// iteration t >= T repeats tile T - 1 (no branch around the loads) and stores nothing.
+template <int MAXT>
 MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
 {
     Smem &S = *Sp;
-    const int U = kGroups * tl.T;
-    const int u0 = U * cw / kConsumerWarps, n = U * (cw + 1) / kConsumerWarps - u0;
-    const int g = lane >> 2, tig = lane & 3;
-    const int t0 = u0 / kGroups;
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    if (cw >= kGroups) return;
+    const int g = lane >> 2, tig = lane & 3, grp = cw;
+    const uint2 b0 = S.bf[2 * grp][lane], b1 = S.bf[2 * grp + 1][lane];
+    const float f = S.sxs[grp];
 #pragma unroll
-    for (int i = 0; i < MAXU; i++) {
-        const bool live = i < n;
-        const int u = min(u0 + i, U - 1), t = u / kGroups, grp = u - t * kGroups, ch = t >> 1;
-        const uint8_t *fr = ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2];
-        const float *sc = ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2];
-        fr += (t & 1) * kTileBytes;
-        sc += (t & 1) * 16 * kGroups;
-        int d[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int ks = 2 * grp + h;
-            uint4 a;
-            if (tl.half) {
-                const uint2 v = *reinterpret_cast<const uint2 *>(fr + ((size_t)ks * 32 + lane) * 8);
-                a = make_uint4(v.x, 0u, v.y, 0u);
-            } else {
-                a = *reinterpret_cast<const uint4 *>(fr + ((size_t)ks * 32 + lane) * 16);
-            }
-            mma_s8(d, a, S.bf[ks][lane]);
+    for (int i = 0; i < MAXT; i++) {
+        const int t = min(i, tl.T - 1), ch = t >> 1;
+        const uint8_t *fr = (ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2]) + (t & 1) * kTileBytes;
+        const float *sc = (ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2]) + (t & 1) * 16 * kGroups;
+        uint4 a0, a1;
+        if (tl.half) {
+            const uint2 x0 = *reinterpret_cast<const uint2 *>(fr + ((size_t)(2 * grp) * 32 + lane) * 8);
+            const uint2 x1 = *reinterpret_cast<const uint2 *>(fr + ((size_t)(2 * grp + 1) * 32 + lane) * 8);
+            a0 = make_uint4(x0.x, 0u, x0.y, 0u);
+            a1 = make_uint4(x1.x, 0u, x1.y, 0u);
+        } else {
+            a0 = *reinterpret_cast<const uint4 *>(fr + ((size_t)(2 * grp) * 32 + lane) * 16);
+            a1 = *reinterpret_cast<const uint4 *>(fr + ((size_t)(2 * grp + 1) * 32 + lane) * 16);
         }
+        int d[4] = {0, 0, 0, 0};
+        mma_s8(d, a0, b0);
+        mma_s8(d, a1, b1);
         float v0, v1;
         combine(d, v0, v1);
         // (a half tile has 8 rows of scales: row g stands in for the absent row g + 8)
-        const float f = S.sxs[grp];
         const float s0 = sc[g * kGroups + grp], s1 = sc[(tl.half ? g : g + 8) * kGroups + grp];
-        if (tig == 0) {
-            const float p0 = live ? v0 * (s0 * f) : 0.f;
-            const float p1 = live && !tl.half ? v1 * (s1 * f) : 0.f;
-            acc[0][0] += t == t0 ? p0 : 0.f;
-            acc[0][1] += t == t0 ? p1 : 0.f;
-            acc[1][0] += t == t0 ? 0.f : p0;
-            acc[1][1] += t == t0 ? 0.f : p1;
-        }
-    }
-    if (tig == 0 && n == 0) {  // fewer units than warps (T = 1): an empty contribution
-        S.gp[g][cw] = 0.f;
-        S.gp[g + 8][cw] = 0.f;
-    }
-    if (tig == 0 && n > 0) {
-        const int t1 = (u0 + n - 1) / kGroups;
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            if (t0 + j <= t1) {
-                S.gp[16 * (t0 + j) + g][cw] = acc[j][0];
-                if (!tl.half) S.gp[16 * (t0 + j) + g + 8][cw] = acc[j][1];
-            }
+        if (tig == 0 && i < tl.T) {
+            S.gp[16 * t + g][cw] = v0 * (s0 * f);
+            if (!tl.half) S.gp[16 * t + g + 8][cw] = v1 * (s1 * f);
         }
     }
 }
 
-// Row `row` of a job of T tiles: the partial sums of the warps whose units cover its
-// tile -- warps wa..wb, the warps holding the tile's first and last unit -- in warp
-// order (after a consumer barrier).
-MB_DEV float row_sum(const Ctx &c, int T, int row)
+// Row `row` of the current job: its 14 group partials in group order (after a
+// consumer barrier).
+MB_DEV float row_sum(const Ctx &c, int row)
 {
-    const int U = kGroups * T, t = row >> 4;
-    const int wa = (kConsumerWarps * (kGroups * t + 1) - 1) / U;
-    const int wb = (kConsumerWarps * (kGroups * t + kGroups) - 1) / U;
     const float *v = c.S.gp[row];
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) s += (w >= wa && w <= wb) ? v[w] : 0.f;
+    for (int w = 0; w < kGroups; w++) s += v[w];
     return s;
 }
 
@@ -678,7 +666,7 @@ MB_DEV const uint8_t *peek(Ctx &c, const Cursor &cur, int ahead)
     return c.S.ring[slot];
 }
 
-// Thread ct == 0, after a consumer barrier: start the bulk copy of chunk k (if any)
+// The issuing thread, after a consumer barrier: start the bulk copy of chunk k (if any)
 // into slot k % kSlots, whose previous chunk every consumer has finished reading.
 MB_DEV void issue(Ctx &c, uint32_t k, bool shared_issuers = false)
 {
@@ -701,7 +689,7 @@ MB_DEV void issue(Ctx &c, uint32_t k, bool shared_issuers = false)
 MB_DEV void give_back(Ctx &c, Cursor &cur)
 {
     cbar();
-    if (c.ct == 0) issue(c, cur.k + kSlots);
+    if (c.ct == kIssuer) issue(c, cur.k + kSlots);
     cur.k++;
 }
 
@@ -709,7 +697,7 @@ MB_DEV void give_back(Ctx &c, Cursor &cur)
 // landed, so no copy is still writing shared memory when the CTA exits.
 MB_DEV void drain(Ctx &c, const Cursor &cur)
 {
-    if (c.ct == 0) {
+    if (c.ct == kIssuer) {  // the thread that recorded S.issued
         const int issued = c.S.issued;
         for (int k = (int)cur.k; k < issued; k++) {
             const long long t1 = clock64();
@@ -816,7 +804,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
           c_end - c0,
           mb::evict_first_policy()};
     // the first kSlots chunks; every later one is started when a slot is given back
-    if (c.ct == 0)
+    if (c.ct == kIssuer)
         for (uint32_t k = 0; k < (uint32_t)kSlots; k++) issue(c, k);
     const int pos = S.pos;
     Cursor cur{0};
@@ -921,8 +909,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 else if (pair < DIM / 2 + KV / 2) { kind = 1; t = pair - DIM / 2; }
                 else { kind = 2; t = pair - DIM / 2 - KV / 2; }
                 const int head = t / 32, i = t % 32, r0 = head * HEAD_DIM + i;
-                const float v0 = row_sum(c, 1, 2 * c.ct) + bias[2 * c.ct];
-                const float v1 = row_sum(c, 1, 2 * c.ct + 1) + bias[2 * c.ct + 1];
+                const float v0 = row_sum(c, 2 * c.ct) + bias[2 * c.ct];
+                const float v1 = row_sum(c, 2 * c.ct + 1) + bias[2 * c.ct + 1];
                 if (kind == 2) {
                     float *v = a.b.vc + kv_index(l, head, pos);
                     v[i] = v0;
@@ -1095,7 +1083,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     }
                 }
                 const float m = mb::warp_max(fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3]))));
-                const float inv = m > 0.f ? 127.f / m : 0.f;
+                const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
                 const float q[4] = {o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv};
                 uint32_t p0, p1, p2;
                 limbs4(q, p0, p1, p2);
@@ -1105,7 +1093,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     b[2 * (4 + tig) + hh] = p1;
                     b[2 * (8 + tig) + hh] = p2;
                 }
-                if (c.lane == 0) S.so = m / (127.f * 254.f);
+                if (c.lane == 0) S.so = m * (1.0f / (127.f * 254.f));
             }
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 3);
@@ -1155,7 +1143,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                     const float lv = c.lane < splits ? __uint_as_float((uint32_t)w1) : 0.f;
                     const float M = mb::warp_max(m);
                     const float L = mb::warp_sum(c.lane < splits ? expf(m - M) * lv : 0.f);
-                    wgt = expf(S.att_m - M) / L;
+                    wgt = __fdividef(expf(S.att_m - M), L);
                 }
                 if (c.lane == 0) S.att_w = wgt;
             }
@@ -1186,26 +1174,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             norm_quantize(&S, c.ct, g_ffn, 0);
             g_ffn = load_gain(c.ct, S.gain[1][min(l + 1, LAYERS - 1)]);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
-            // this layer's gate/up chunks (2 or 3, all resident in the ring together):
-            // slots cur.k .. cur.k + ngu - 1
-            // (a CTA without a spare piece has two: waiting for a third slot would wait
-            // for the down chunk behind them)
-            int ngu = 0, T = 0;
-            const int want = has_spare(cta) ? 3 : 2;
-            while (ngu < want && ngu < remaining) {
-                if (!peek(c, cur, ngu)) return drain(c, cur);
-                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + ngu) % kSlots]);
-                if (h->kind != GATEUP || h->layer != (uint32_t)l) break;
-                if ((h->count != 8 && h->count != 16) || (ngu > 0 && T % 2)) {
+            // this layer's gate/up chunks, all resident in the ring together in slots
+            // cur.k .. cur.k + ngu - 1: the plan gives every CTA two 16-unit chunks, then
+            // its 8-unit piece if it has one; their barriers are tested together (the
+            // waits overlap), then their headers checked
+            const int ngu = has_spare(cta) ? 3 : 2;
+            int T = 0;
+            {
+                bool landed = ngu <= remaining;
+#pragma unroll
+                for (int i = 0; i < 3; i++)
+                    if (i < ngu) landed = mbar_test(&S.full[(cur.k + i) % kSlots], ((cur.k + i) / kSlots) & 1) && landed;
+                if (!landed)
+                    for (int i = 0; i < ngu; i++)
+                        if (i >= remaining || !peek(c, cur, i)) {
+                            if (c.ct == 0 && i >= remaining) fail(c.sy, c.host_error, 4);
+                            return drain(c, cur);
+                        }
+                bool ok = true;
+#pragma unroll
+                for (int i = 0; i < 3; i++) {
+                    if (i < ngu) {
+                        const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + i) % kSlots]);
+                        ok = ok && h->kind == GATEUP && h->layer == (uint32_t)l && h->count == (i < 2 ? 16u : 8u);
+                        T += (int)h->count / 8;
+                    }
+                }
+                if (!ok) {
                     if (c.ct == 0) fail(c.sy, c.host_error, 4);
                     return drain(c, cur);
                 }
-                ngu++;
-                T += h->count / 8;
-            }
-            if (ngu == 0 || T > 5) {
-                if (c.ct == 0) fail(c.sy, c.host_error, 4);
-                return drain(c, cur);
             }
             const uint32_t s0 = cur.k % kSlots, s1 = (cur.k + 1) % kSlots, s2 = (cur.k + (ngu > 2 ? 2 : 0)) % kSlots;
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 9);
@@ -1217,7 +1215,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             tl.sc[0] = reinterpret_cast<const float *>(tl.frag[0] + (size_t)min(2, T) * kTileBytes);
             tl.sc[1] = reinterpret_cast<const float *>(tl.frag[1] + (size_t)max(1, min(2, T - 2)) * kTileBytes);
             tl.sc[2] = reinterpret_cast<const float *>(tl.frag[2] + (size_t)max(1, min(2, T - 4)) * kTileBytes);
-            gemv_mma<5>(&S, c.cw, c.lane, tl);
+            if (T > 4)
+                gemv_mma<5>(&S, c.cw, c.lane, tl);
+            else
+                gemv_mma<4>(&S, c.cw, c.lane, tl);
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 18);
             // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and
@@ -1226,11 +1227,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const int t = c.ct >> 3, j = c.ct & 7;
                 const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(t >> 1) == 0 ? s0 : (t >> 1) == 1 ? s1 : s2]);
                 const int unit = (int)h->first + 8 * (t & 1) + j;
-                const float g = row_sum(c, T, 16 * t + j), u = row_sum(c, T, 16 * t + 8 + j);
-                S.hst[(unit >> 5) == cta ? 0 : 1][unit & 31] = (g / (1.0f + expf(-g))) * u;
+                const float g = row_sum(c, 16 * t + j), u = row_sum(c, 16 * t + 8 + j);
+                S.hst[(unit >> 5) == cta ? 0 : 1][unit & 31] = __fdividef(g, 1.0f + expf(-g)) * u;
             }
             cbar();
-            if (c.ct == 0)
+            if (c.ct == kIssuer)
                 for (int i = 0; i < ngu; i++) issue(c, cur.k + i + kSlots);
             cur.k += ngu;
             remaining -= ngu;

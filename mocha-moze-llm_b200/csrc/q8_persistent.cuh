@@ -11,7 +11,7 @@ namespace q8p {
 
 constexpr int kCTAs = 148;                // one CTA per SM
 constexpr int kConsumerWarps = 16;
-constexpr int kThreads = 32 * kConsumerWarps;  // every thread consumes; thread 0 also issues the weight copies
+constexpr int kThreads = 32 * kConsumerWarps;  // every thread consumes; one also issues the weight copies
 constexpr int kSlots = 4;                 // shared-memory ring slots
 constexpr int kSlotBytes = 36864;
 constexpr int kGainBytes = q8::DIM * 4;   // RMSNorm gain delivered with some chunks
