@@ -1058,20 +1058,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const float fw = c.lane < nw ? expf(mw - mx) : 0.f;
                 const int t = c.lane & 15, ks = t >> 3, tig = (t >> 1) & 3, hh = t & 1;
                 const int d0 = 32 * ks + 16 * hh + 4 * tig;
+                // lanes 0..15 sum warps [0, kHalf), lanes 16..31 warps [kHalf, 2 kHalf); the
+                // halves are then added (both lanes of a pair get the same sum)
+                constexpr int kHalf = (kMaxAttnWarps + 1) / 2;
                 float lsum = 0.f;
                 float o[4] = {0.f, 0.f, 0.f, 0.f};
+                const int wb = (c.lane >> 4) * kHalf;
 #pragma unroll
-                for (int w = 0; w < kMaxAttnWarps; w++) {
+                for (int i = 0; i < kHalf; i++) {
+                    const int w = wb + i;
                     const float f = __shfl_sync(0xffffffffu, fw, w);
                     const bool in = w < nw;
-                    const float lw = S.u.att.wp[w][1];
-                    const float4 p = *reinterpret_cast<const float4 *>(&S.u.att.wp[w][4 + d0]);
+                    const float lw = S.u.att.wp[min(w, kConsumerWarps - 1)][1];
+                    const float4 p = *reinterpret_cast<const float4 *>(&S.u.att.wp[min(w, kConsumerWarps - 1)][4 + d0]);
                     lsum = fmaf(f, in ? lw : 0.f, lsum);
                     o[0] = fmaf(f, in ? p.x : 0.f, o[0]);
                     o[1] = fmaf(f, in ? p.y : 0.f, o[1]);
                     o[2] = fmaf(f, in ? p.z : 0.f, o[2]);
                     o[3] = fmaf(f, in ? p.w : 0.f, o[3]);
                 }
+                lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
+#pragma unroll
+                for (int j = 0; j < 4; j++) o[j] += __shfl_xor_sync(0xffffffffu, o[j], 16);
                 if (c.lane == 0) {
                     S.att_m = mx;
                     S.att_l = lsum;
