@@ -124,7 +124,7 @@ struct Smem {
     float gp[5 * 16][kGpStride];   // per-group partial row sums of the current job (<= 5 tiles)
     float sxs[kGroups];            // input scale / 254 per group
     __align__(16) float hst[2][32];  // this CTA's SwiGLU outputs at their column in each down step
-    float sh;                      // their scale / 254
+    float sh[2];                   // their scale / 254, per down step
     __align__(16) float red[kConsumerWarps][8];  // also read as 64-bit keys (block_max)
     float rc[HEAD_DIM / 2], rs[HEAD_DIM / 2];  // RoPE cos/sin at pos
     Chunk desc[kMaxChunksPerCta];  // this CTA's chunk descriptors
@@ -433,32 +433,6 @@ MB_DEV void norm_quantize(Smem *Sp, int ct, float4 g, int keep)
     cbar();
 }
 
-// src[ks][0..32) for ks < nks (one scale for all) -> B fragments bf[ks] and the scale
-// / 254; warp 0.
-MB_DEV void quantize_slice(Ctx &c, const float (*src)[32], int nks, uint2 (*bf)[32], float *scale)
-{
-    if (c.cw == 0) {
-        const int t = c.lane & 15, ks = t >> 3, tig = (t >> 1) & 3, h = t & 1;
-        const bool live = c.lane < 16 && ks < nks;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live) v = *reinterpret_cast<const float4 *>(&src[ks][16 * h + 4 * tig]);
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        m = mb::warp_max(m);
-        const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
-        const float q[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
-        uint32_t p0, p1, p2;
-        limbs4(q, p0, p1, p2);
-        if (live) {
-            uint32_t *b = reinterpret_cast<uint32_t *>(&bf[ks][0]);
-            b[2 * tig + h] = p0;
-            b[2 * (4 + tig) + h] = p1;
-            b[2 * (8 + tig) + h] = p2;
-        }
-        if (c.lane == 0) *scale = m * (1.0f / (127.f * 254.f));
-    }
-    cbar();
-}
-
 // D fragments of one group -> the limb combination (254 D0 + D1 + D2/254) of rows g
 // (v0) and g + 8 (v1); valid in lanes with tig == 0 (limb 2 comes from lane + 1).
 MB_DEV void combine(const int (&d)[4], float &v0, float &v1)
@@ -533,10 +507,12 @@ MB_DEV float row_sum(const Ctx &c, int row)
 
 // Down projection, one 32-column step of this CTA's hidden units for all 896 rows
 // ([kDownTiles][32 lanes][16 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
-// partials (v * weight scale) are added to acc[tile][row g | row g + 8].  A warp with
+// partials (v * weight scale * input scale sx) are added to acc[tile][row g | row g + 8].
+// A warp with
 // three tiles also multiplies a fourth (the next warp's first) into an acc entry its
 // caller ignores: no branch around the loads.
-MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float (&acc)[4][2])
+MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float sx,
+                      float (&acc)[4][2])
 {
     const int t0 = kDownTiles * c.cw / kConsumerWarps;
     const uint2 b = bfs[c.lane];
@@ -549,8 +525,8 @@ MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 
         float v0, v1;
         combine(d, v0, v1);
         const int r0 = 16 * t + g;
-        acc[i][0] = fmaf(v0, sw[r0], acc[i][0]);
-        acc[i][1] = fmaf(v1, sw[r0 + 8], acc[i][1]);
+        acc[i][0] = fmaf(v0, sw[r0] * sx, acc[i][0]);
+        acc[i][1] = fmaf(v1, sw[r0 + 8] * sx, acc[i][1]);
     }
 }
 
@@ -1048,7 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             // Warp 0 merges the warps' partials at the split's max and quantizes the
             // result straight into S.bfo: lane t (t = lane % 16; both halves compute the
             // same) owns dims 32 ks + 16 hh + 4 tig + {0..3}, ks = t >> 3, tig = (t >> 1) & 3,
-            // hh = t & 1 -- its limbs' place in the B fragments, as in quantize_slice.
+            // hh = t & 1 -- its limbs' place in the B fragments, as in put_limbs.
             // Lane w < nw holds warp w's max and its factor exp(m_w - max) (one expf per
             // lane); the sums run over w in order with the factors shuffled in, and rows
             // of idle warps enter as zeros (no branch around the loads).
@@ -1183,29 +1159,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             g_ffn = load_gain(c.ct, S.gain[1][min(l + 1, LAYERS - 1)]);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
             // this layer's gate/up chunks, all resident in the ring together in slots
-            // cur.k .. cur.k + ngu - 1: the plan gives every CTA two 16-unit chunks, then
-            // its 8-unit piece if it has one; their barriers are tested together (the
-            // waits overlap), then their headers checked
+            // cur.k .. cur.k + ngu - 1 -- the plan gives every CTA two 16-unit chunks, then
+            // its 8-unit piece if it has one -- and the first down chunk after them (ngu
+            // + 1 <= kSlots): their barriers are tested together (the waits overlap), then
+            // their headers checked
             const int ngu = has_spare(cta) ? 3 : 2;
             int T = 0;
             {
-                bool landed = ngu <= remaining;
+                bool landed = ngu + 1 <= remaining;
 #pragma unroll
-                for (int i = 0; i < 3; i++)
-                    if (i < ngu) landed = mbar_test(&S.full[(cur.k + i) % kSlots], ((cur.k + i) / kSlots) & 1) && landed;
+                for (int i = 0; i < 4; i++)
+                    if (i <= ngu) landed = mbar_test(&S.full[(cur.k + i) % kSlots], ((cur.k + i) / kSlots) & 1) && landed;
                 if (!landed)
-                    for (int i = 0; i < ngu; i++)
+                    for (int i = 0; i <= ngu; i++)
                         if (i >= remaining || !peek(c, cur, i)) {
                             if (c.ct == 0 && i >= remaining) fail(c.sy, c.host_error, 4);
                             return drain(c, cur);
                         }
                 bool ok = true;
 #pragma unroll
-                for (int i = 0; i < 3; i++) {
+                for (int i = 0; i < 4; i++) {
+                    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + i) % kSlots]);
                     if (i < ngu) {
-                        const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + i) % kSlots]);
                         ok = ok && h->kind == GATEUP && h->layer == (uint32_t)l && h->count == (i < 2 ? 16u : 8u);
                         T += (int)h->count / 8;
+                    } else if (i == ngu) {
+                        ok = ok && h->kind == DOWN && h->layer == (uint32_t)l && h->first == 0 && h->count == (uint32_t)nks;
                     }
                 }
                 if (!ok) {
@@ -1229,54 +1208,74 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 gemv_mma<4>(&S, c.cw, c.lane, tl);
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 18);
-            // hidden unit k of the job: tile t = k / 8 holds its gate row 16 t + k % 8 and
-            // its up row 8 below; it lands at its column of down step 0 (own block) or 1
-            if (c.ct < 8 * T) {
-                const int t = c.ct >> 3, j = c.ct & 7;
-                const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(t >> 1) == 0 ? s0 : (t >> 1) == 1 ? s1 : s2]);
-                const int unit = (int)h->first + 8 * (t & 1) + j;
-                const float g = row_sum(c, 16 * t + j), u = row_sum(c, 16 * t + 8 + j);
-                S.hst[(unit >> 5) == cta ? 0 : 1][unit & 31] = __fdividef(g, 1.0f + expf(-g)) * u;
-            }
-            cbar();
+            // the products are in S.gp: the gate/up chunks go back at once
             if (c.ct == kIssuer)
                 for (int i = 0; i < ngu; i++) issue(c, cur.k + i + kSlots);
             cur.k += ngu;
             remaining -= ngu;
+            // h = silu(gate) * up, each down step's 32 columns in one warp, quantized there
+            // with the step's own scale (no block barrier between SwiGLU and limbs): warp 0
+            // the CTA's block, unit 32 cta + lane at column lane (tile lane / 8 holds its
+            // gate row 16 t + lane % 8 and its up row 8 below); warp 1, for a CTA with a
+            // piece, the piece's 8 units from tile 4 at their columns of the spare block
+            if (c.cw < nks) {
+                const int t = c.cw == 0 ? c.lane >> 3 : 4, j = c.lane & 7;
+                const bool live = c.cw == 0 || c.lane < 8;
+                const int col = c.cw == 0 ? c.lane : (spare_lo(cta) & 31) + j;
+                float hv = 0.f;
+                if (live) {
+                    const float g = row_sum(c, 16 * t + j), u = row_sum(c, 16 * t + 8 + j);
+                    hv = __fdividef(g, 1.0f + expf(-g)) * u;
+                    S.hst[c.cw][col] = hv;
+                }
+                __syncwarp();
+                const float m = mb::warp_max(fabsf(hv));
+                if (c.lane < 8) {  // columns 16 h + 4 tig + {0..3}: B-fragment register h of lanes 4 n + tig
+                    const int tig = c.lane >> 1, h = c.lane & 1;
+                    const float4 v = *reinterpret_cast<const float4 *>(&S.hst[c.cw][16 * h + 4 * tig]);
+                    const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
+                    const float q[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
+                    uint32_t p0, p1, p2;
+                    limbs4(q, p0, p1, p2);
+                    uint32_t *b = reinterpret_cast<uint32_t *>(&S.bfh[c.cw][0]);
+                    b[2 * tig + h] = p0;
+                    b[2 * (4 + tig) + h] = p1;
+                    b[2 * (8 + tig) + h] = p2;
+                }
+                if (c.lane == 0) S.sh[c.cw] = m * (1.0f / (127.f * 254.f));
+            }
+            cbar();
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 7);
-        quantize_slice(c, S.hst, nks, S.bfh, &S.sh);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 19);
         {
+            // the block's down step: the chunk at the cursor (checked above); a piece's
+            // step: the next one
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-            for (;;) {
-                const uint8_t *w = take(c, cur, DOWN);
+            for (int ks = 0; ks < nks; ks++) {
+                const uint8_t *w = ks == 0 ? S.ring[cur.k % kSlots] : take(c, cur, DOWN);
                 if (!w) return drain(c, cur);
                 stamp(a, cta, c.ct, 2 + l * kTraceLayer + 20);
-                const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
                 const uint8_t *frag = w + sizeof(ChunkHdr);
                 const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
-                down_step(c, frag, sw, S.bfh[hd.first], pacc);
+                down_step(c, frag, sw, S.bfh[ks], S.sh[ks], pacc);
                 stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
-                const bool last = hd.first + 1 == hd.count;
-                if (last) {
+                if (ks + 1 == nks) {
                     // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
                     const int t0 = kDownTiles * c.cw / kConsumerWarps;
                     const int n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
                     const int g = c.lane >> 2;
-                    const float f = S.sh;
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         if (i < n && (c.lane & 3) == 0) {
                             const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
-                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0] * f);
-                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1] * f);
+                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0]);
+                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1]);
                         }
                     }
                 }
                 give_back(c, cur);
                 remaining--;
-                if (last) break;
             }
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
