@@ -131,6 +131,7 @@ struct Smem {
     // pointers the layer loop needs, copied from global memory once: a pointer load from
     // global memory feeding a second load puts two L2 round trips on the path
     const float *gain[2][LAYERS];  // RMSNorm gains: [0] attention, [1] FFN
+    const float *final_gain;       // the final norm's
     const uint8_t *ofrag;          // the plan's O-by-head fragments and scales
     const float *oscale;
     unsigned long long full[kSlots];
@@ -399,38 +400,51 @@ MB_DEV float4 load_gain(int ct, const float *gain)
                     : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// RMSNorm of S.xs with the gain g (this thread's four columns, from load_gain), in the
-// reference's form ((x * s) * g, s = 1/sqrt(sum x^2 / DIM + eps)) with s from the
-// hardware reciprocal square root (within 2 ulp of the rounded 1/sqrtf), quantized
-// straight into S.bf / S.sxs; with keep the normalised vector also goes to S.ns.
-// Consumer threads ct < 256 (warps 0..7) work; every consumer thread calls it (two
-// consumer barriers).
-MB_DEV void norm_quantize(Smem *Sp, int ct, float4 g, int keep)
+// RMSNorm with the gain g, in the reference's form ((x * s) * g, s = 1/sqrt(sum x^2 /
+// DIM + eps)) with s from the hardware reciprocal square root (within 2 ulp of the
+// rounded 1/sqrtf), quantized straight into S.bf / S.sxs.  Thread ct < 224 (warps 0..6)
+// owns columns quant_col(ct) .. + 3 of x and g (g from load_gain).  In two halves around
+// a consumer barrier, so that the first can be fused into the reduction that produces x.
+
+// First half: the warp sums of x^2 into S.red and pm = the 16-lane group max of |x * g|.
+// Warps 0..6, all lanes.
+MB_DEV void norm_sums(Smem &S, int ct, float4 g, float4 x, float &pm)
 {
-    Smem &S = *Sp;
-    const int t = min(ct, 223), col = quant_col(t), lane = ct & 31;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    float pm = 0.f;
-    if (ct < 256) {
-        x = *reinterpret_cast<const float4 *>(S.xs + col);
-        float ss = 0.f;
-        if (ct < 224) ss = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
-        pm = fmaxf(fmaxf(fabsf(x.x * g.x), fabsf(x.y * g.y)), fmaxf(fabsf(x.z * g.z), fabsf(x.w * g.w)));
-        ss = mb::warp_sum(ss);
-        pm = group_max16(pm);
-        if (lane == 0 && ct < 224) S.red[ct >> 5][0] = ss;
-    }
-    cbar();
-    if (ct < 224) {
+    float ss = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
+    pm = fmaxf(fmaxf(fabsf(x.x * g.x), fabsf(x.y * g.y)), fmaxf(fabsf(x.z * g.z), fabsf(x.w * g.w)));
+    ss = mb::warp_sum(ss);
+    pm = group_max16(pm);
+    if ((ct & 31) == 0) S.red[ct >> 5][0] = ss;
+}
+
+// Second half, after the barrier: s from the seven warp sums, the limbs of (x * s) * g
+// (with keep also the values into S.ns); every consumer thread calls it (one barrier).
+MB_DEV void norm_finish(Smem &S, int ct, float4 g, float4 x, float pm, int keep)
+{
+    if (ct < DIM / 4) {
         float sum = 0.f;
 #pragma unroll
         for (int w = 0; w < 7; w++) sum += S.red[w][0];
         const float s = rsqrtf(sum * (1.0f / DIM) + RMS_EPS);
         const float n[4] = {(x.x * s) * g.x, (x.y * s) * g.y, (x.z * s) * g.z, (x.w * s) * g.w};
-        if (keep) *reinterpret_cast<float4 *>(S.ns + col) = make_float4(n[0], n[1], n[2], n[3]);
-        put_limbs(S, t, n, pm * s);
+        if (keep) *reinterpret_cast<float4 *>(S.ns + quant_col(ct)) = make_float4(n[0], n[1], n[2], n[3]);
+        put_limbs(S, ct, n, pm * s);
     }
     cbar();
+}
+
+// The whole norm of S.xs; every consumer thread calls it (two barriers).
+MB_DEV void norm_quantize(Smem *Sp, int ct, float4 g, int keep)
+{
+    Smem &S = *Sp;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    float pm = 0.f;
+    if (ct < DIM / 4) {
+        x = *reinterpret_cast<const float4 *>(S.xs + quant_col(ct));
+        norm_sums(S, ct, g, x, pm);
+    }
+    cbar();
+    norm_finish(S, ct, g, x, pm, keep);
 }
 
 // D fragments of one group -> the limb combination (254 D0 + D1 + D2/254) of rows g
@@ -613,6 +627,104 @@ struct Cursor {
     uint32_t k;  // chunks consumed
 };
 
+// add_sums for the reductions that feed a norm: thread t < 224 polls the words of its
+// norm columns quant_col(t) .. + 3 (32 bytes per copy), adds them to S.xs and to x, and
+// runs the norm's first half on x (pm as norm_sums gives it) before the barrier that the
+// reduction ends with anyway; meanwhile the issuer thread, idle here, runs check() (the
+// next phase's chunks: landed, headers valid), whose verdict joins the barrier's.  The
+// caller finishes with norm_finish.
+template <typename Check>
+MB_DEV bool add_sums_norm(Ctx &c, const unsigned long long *acc, unsigned count, float4 g, float4 &x, float &pm,
+                          Check check)
+{
+    int ok = 1;
+    x = make_float4(0.f, 0.f, 0.f, 0.f);
+    pm = 0.f;
+    if (c.ct < DIM / 4) {
+        const int col = quant_col(c.ct);
+        unsigned long long v[kAccRep][4];
+        unsigned need[kAccRep];
+#pragma unroll
+        for (int r = 0; r < kAccRep; r++) {
+            need[r] = (count + kAccRep - 1 - r) / kAccRep;
+            dw_load4(acc + r * DIM + col, v[r]);
+        }
+        long long t0 = 0;
+        for (;;) {
+            bool done = true;
+#pragma unroll
+            for (int r = 0; r < kAccRep; r++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) done = done && (unsigned)(v[r][j] & 0xFFu) == need[r];
+            if (done) break;
+            if (t0 == 0) {
+                t0 = clock64();
+            } else if (give_up(c.sy, c.host_error, clock64() - t0, 1)) {
+                ok = 0;
+                break;
+            }
+#pragma unroll
+            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * DIM + col, v[r]);
+        }
+        long long s4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int r = 0; r < kAccRep; r++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) s4[j] += (long long)v[r][j] >> 8;
+        x = *reinterpret_cast<const float4 *>(c.S.xs + col);
+        x.x += __ll2float_rn(s4[0]) * kFixInv;
+        x.y += __ll2float_rn(s4[1]) * kFixInv;
+        x.z += __ll2float_rn(s4[2]) * kFixInv;
+        x.w += __ll2float_rn(s4[3]) * kFixInv;
+        *reinterpret_cast<float4 *>(c.S.xs + col) = x;
+        norm_sums(c.S, c.ct, g, x, pm);
+    }
+    if (c.ct == kIssuer && !check()) ok = 0;
+    return cbar_and(ok) != 0;
+}
+
+// Issuer-side checks of the chunks the next phase reads without waiting.  The QKV job of
+// layer l at the cursor: landed, a QKV header of layer l with 1..4 pairs.
+MB_DEV bool qkv_ready(Ctx &c, const Cursor &cur, int remaining, int l)
+{
+    const uint32_t slot = cur.k % kSlots;
+    if (remaining < 1) {
+        fail(c.sy, c.host_error, 4);
+        return false;
+    }
+    if (!mbar_wait(&c.S.full[slot], (cur.k / kSlots) & 1, c.sy, c.host_error)) return false;
+    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(c.S.ring[slot]);
+    if (h->kind != QKV || h->layer != (uint32_t)l || h->count < 1 || h->count > 4) {
+        fail(c.sy, c.host_error, 4);
+        return false;
+    }
+    return true;
+}
+
+// Layer l's FFN chunks from the cursor: ngu gate/up chunks (two of 16 units, then the
+// 8-unit piece if the CTA has one) and the first down chunk after them (ngu + 1 <=
+// kSlots: all resident together).
+MB_DEV bool ffn_ready(Ctx &c, const Cursor &cur, int remaining, int l, int ngu, int nks)
+{
+    if (remaining < ngu + 1) {
+        fail(c.sy, c.host_error, 4);
+        return false;
+    }
+    bool ok = true;
+    for (int i = 0; i <= ngu; i++) {
+        const uint32_t k = cur.k + (uint32_t)i;
+        if (!mbar_wait(&c.S.full[k % kSlots], (k / kSlots) & 1, c.sy, c.host_error)) return false;
+        const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(c.S.ring[k % kSlots]);
+        if (i < ngu)
+            ok = ok && h->kind == GATEUP && h->layer == (uint32_t)l && h->count == (i < 2 ? 16u : 8u);
+        else
+            ok = ok && h->kind == DOWN && h->layer == (uint32_t)l && h->first == 0 && h->count == (uint32_t)nks;
+    }
+    if (!ok) fail(c.sy, c.host_error, 4);
+    return ok;
+}
+
+
 // Wait for the next chunk; returns the slot (header first) or null on failure.
 // Every chunk's range is checked against the bounds its consumers assume.
 MB_DEV const uint8_t *take(Ctx &c, Cursor &cur, uint32_t kind)
@@ -766,6 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     if (threadIdx.x == 2 * LAYERS) {
         S.ofrag = a.P->ofrag;
         S.oscale = a.P->oscale;
+        S.final_gain = a.M->final_norm;
     }
     __syncthreads();
     Ctx c{S,
@@ -863,10 +976,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         // ---- QKV + bias + RoPE + KV write
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
-            norm_quantize(&S, c.ct, g_attn, 0);
+            // layer 0's norm here; every later layer's ran inside the previous layer's
+            // x_out reduction, which also checked this QKV chunk
+            if (l == 0) norm_quantize(&S, c.ct, g_attn, 0);
             g_attn = load_gain(c.ct, S.gain[0][min(l + 1, LAYERS - 1)]);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 12);
-            const uint8_t *w = take(c, cur, QKV);
+            const uint8_t *w = l == 0 ? take(c, cur, QKV) : S.ring[cur.k % kSlots];
             if (!w) return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 11);
             const ChunkHdr hd = *reinterpret_cast<const ChunkHdr *>(w);
@@ -1150,48 +1265,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 2);
 
         // ---- x_mid = x_in + the attention block, all-reduced over the attention CTAs
-        if (!add_sums(c, xacc + (size_t)kAccRep * l * DIM, (unsigned)(HEADS * splits))) return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
+        // (with the FFN norm's first half, and the issuer checking the FFN chunks)
+        const int ngu = has_spare(cta) ? 3 : 2, T = has_spare(cta) ? 5 : 4;  // gate/up chunks, tiles
+        {
+            float4 x;
+            float pm;
+            if (!add_sums_norm(c, xacc + (size_t)kAccRep * l * DIM, (unsigned)(HEADS * splits), g_ffn, x, pm,
+                               [&]() { return ffn_ready(c, cur, remaining, l, ngu, nks); }))
+                return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
+            norm_finish(S, c.ct, g_ffn, x, pm, 0);
+        }
 
         // ---- RMSNorm -> gate/up -> SwiGLU
         {
-            norm_quantize(&S, c.ct, g_ffn, 0);
-            g_ffn = load_gain(c.ct, S.gain[1][min(l + 1, LAYERS - 1)]);
+            // (after the last layer: the final norm's gain, for the head)
+            g_ffn = load_gain(c.ct, l + 1 < LAYERS ? S.gain[1][l + 1] : S.final_gain);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 10);
-            // this layer's gate/up chunks, all resident in the ring together in slots
-            // cur.k .. cur.k + ngu - 1 -- the plan gives every CTA two 16-unit chunks, then
-            // its 8-unit piece if it has one -- and the first down chunk after them (ngu
-            // + 1 <= kSlots): their barriers are tested together (the waits overlap), then
-            // their headers checked
-            const int ngu = has_spare(cta) ? 3 : 2;
-            int T = 0;
-            {
-                bool landed = ngu + 1 <= remaining;
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    if (i <= ngu) landed = mbar_test(&S.full[(cur.k + i) % kSlots], ((cur.k + i) / kSlots) & 1) && landed;
-                if (!landed)
-                    for (int i = 0; i <= ngu; i++)
-                        if (i >= remaining || !peek(c, cur, i)) {
-                            if (c.ct == 0 && i >= remaining) fail(c.sy, c.host_error, 4);
-                            return drain(c, cur);
-                        }
-                bool ok = true;
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const ChunkHdr *h = reinterpret_cast<const ChunkHdr *>(S.ring[(cur.k + i) % kSlots]);
-                    if (i < ngu) {
-                        ok = ok && h->kind == GATEUP && h->layer == (uint32_t)l && h->count == (i < 2 ? 16u : 8u);
-                        T += (int)h->count / 8;
-                    } else if (i == ngu) {
-                        ok = ok && h->kind == DOWN && h->layer == (uint32_t)l && h->first == 0 && h->count == (uint32_t)nks;
-                    }
-                }
-                if (!ok) {
-                    if (c.ct == 0) fail(c.sy, c.host_error, 4);
-                    return drain(c, cur);
-                }
-            }
+            // this layer's gate/up chunks, resident together in slots cur.k .. cur.k + ngu - 1,
+            // and the first down chunk after them: checked during the x_mid reduction
             const uint32_t s0 = cur.k % kSlots, s1 = (cur.k + 1) % kSlots, s2 = (cur.k + (ngu > 2 ? 2 : 0)) % kSlots;
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 9);
             Tiles tl{{S.ring[s0] + sizeof(ChunkHdr), S.ring[s1] + sizeof(ChunkHdr), S.ring[s2] + sizeof(ChunkHdr)},
@@ -1280,9 +1372,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
         // all-reduce: once all 148 CTAs' additions are complete every CTA adds the sums
-        // to its x_mid -- the next layer's input
-        if (!add_sums(c, dacc + (size_t)kAccRep * l * DIM, kCTAs)) return drain(c, cur);
-        stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
+        // to its x_mid -- the next layer's input -- fused with that layer's QKV norm (first
+        // half) while the issuer checks its QKV chunk
+        if (l + 1 < LAYERS) {
+            float4 x;
+            float pm;
+            if (!add_sums_norm(c, dacc + (size_t)kAccRep * l * DIM, kCTAs, g_attn, x, pm,
+                               [&]() { return qkv_ready(c, cur, remaining, l + 1); }))
+                return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
+            norm_finish(S, c.ct, g_attn, x, pm, 0);
+        } else {
+            if (!add_sums(c, dacc + (size_t)kAccRep * l * DIM, kCTAs)) return drain(c, cur);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
+        }
     }
 
     if (project) {
@@ -1298,7 +1401,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         }
         if (c.ct == 0)
             for (int i = 0; i < kSlots; i++) S.slot_fill[(cur.k + i) % kSlots] = (int)(cur.k + i);
-        norm_quantize(&S, c.ct, load_gain(c.ct, M->final_norm), cta == 0);
+        norm_quantize(&S, c.ct, g_ffn, cta == 0);
         if (cta == 0)
             for (int i = c.ct; i < DIM; i += kNT) a.b.hidden[i] = S.ns[i];
         // Warp w takes tiles w, w + 16, ... in order (tile t = tile t & 1 of chunk t >> 1),
