@@ -123,7 +123,7 @@ struct Smem {
     float att_m, att_l, att_w;           // this split's max and sum of weights; its weight in the head
     float gp[5 * 16][kGpStride];   // per-group partial row sums of the current job (<= 5 tiles)
     float sxs[kGroups];            // input scale / 254 per group
-    __align__(16) float hst[2][32];  // this CTA's SwiGLU outputs at their column in each down step
+    __align__(16) float hst[2][32];  // SwiGLU outputs: the block's at column unit % 32, the piece's at 0..7
     float sh[2];                   // their scale / 254, per down step
     __align__(16) float red[kConsumerWarps][8];  // also read as 64-bit keys (block_max)
     float rc[HEAD_DIM / 2], rs[HEAD_DIM / 2];  // RoPE cos/sin at pos
@@ -146,12 +146,20 @@ static_assert(sizeof(Smem) <= 232448, "shared memory per CTA");
 // Hidden units whose gate/up rows and down-projection columns CTA c owns: the
 // 32-unit block [32c, 32c + 32) and, for the last 16 CTAs, an 8-unit piece of the four
 // spare blocks, [4736 + 8j, 4736 + 8j + 8) for CTA 132 + j (4864 = 148 * 32 + 16 * 8).
-// Down-projection step 0 covers the CTA's block, step 1 the spare block holding its
-// piece (the other 24 columns enter as zeros).
+// Down-projection step 0 covers the CTA's block (its own chunk); the piece's 8 down
+// columns ride in the piece's gate/up chunk, after its tile, so the CTA never waits
+// for a second down chunk: its three gate/up chunks and its down chunk fill the ring
+// together.
 constexpr int kSpareFirst = kCTAs - (HIDDEN - 32 * kCTAs) / 8;  // 132
 static_assert(32 * kCTAs + 8 * (kCTAs - kSpareFirst) == HIDDEN, "hidden slices");
 __host__ __device__ inline bool has_spare(int c) { return c >= kSpareFirst; }
 __host__ __device__ inline int spare_lo(int c) { return 32 * kCTAs + 8 * (c - kSpareFirst); }
+// The piece's down columns in its gate/up chunk, after the tile and the tile rows'
+// scales: [kDownTiles][16][8 B] -- registers a0 and a1 of lanes 4 g + tig, tig < 2, of a
+// 32-column step whose columns 0..7 are the piece's units (the rest zero) -- then the
+// 896 rows' scales of the piece's 64-column group.
+constexpr int kSpareDownOff = kTileBytes + 16 * kGroups * 4;
+constexpr int kSpareDownBytes = kDownTiles * 16 * 8;
 
 // ---- low-level primitives --------------------------------------------------
 
@@ -520,22 +528,34 @@ MB_DEV float row_sum(const Ctx &c, int row)
 }
 
 // Down projection, one 32-column step of this CTA's hidden units for all 896 rows
-// ([kDownTiles][32 lanes][16 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
+// ([kDownTiles][32 lanes][16 B], or with Piece the 8-column form of a spare piece,
+// [kDownTiles][16][8 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
 // partials (v * weight scale * input scale sx) are added to acc[tile][row g | row g + 8].
 // A warp with
 // three tiles also multiplies a fourth (the next warp's first) into an acc entry its
 // caller ignores: no branch around the loads.
+template <bool Piece>
 MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float sx,
                       float (&acc)[4][2])
 {
     const int t0 = kDownTiles * c.cw / kConsumerWarps;
     const uint2 b = bfs[c.lane];
-    const int g = c.lane >> 2;
+    const int g = c.lane >> 2, tig = c.lane & 3;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int t = min(t0 + i, kDownTiles - 1);
         int d[4] = {0, 0, 0, 0};
-        mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16), b);
+        uint4 a = make_uint4(0u, 0u, 0u, 0u);
+        if (!Piece) {
+            a = *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16);
+        } else {
+            const uint2 v = *reinterpret_cast<const uint2 *>(frag + ((size_t)t * 16 + 2 * g + (tig & 1)) * 8);
+            if (tig < 2) {
+                a.x = v.x;
+                a.y = v.y;
+            }
+        }
+        mma_s8(d, a, b);
         float v0, v1;
         combine(d, v0, v1);
         const int r0 = 16 * t + g;
@@ -704,7 +724,7 @@ MB_DEV bool qkv_ready(Ctx &c, const Cursor &cur, int remaining, int l)
 // Layer l's FFN chunks from the cursor: ngu gate/up chunks (two of 16 units, then the
 // 8-unit piece if the CTA has one) and the first down chunk after them (ngu + 1 <=
 // kSlots: all resident together).
-MB_DEV bool ffn_ready(Ctx &c, const Cursor &cur, int remaining, int l, int ngu, int nks)
+MB_DEV bool ffn_ready(Ctx &c, const Cursor &cur, int remaining, int l, int ngu)
 {
     if (remaining < ngu + 1) {
         fail(c.sy, c.host_error, 4);
@@ -718,7 +738,7 @@ MB_DEV bool ffn_ready(Ctx &c, const Cursor &cur, int remaining, int l, int ngu, 
         if (i < ngu)
             ok = ok && h->kind == GATEUP && h->layer == (uint32_t)l && h->count == (i < 2 ? 16u : 8u);
         else
-            ok = ok && h->kind == DOWN && h->layer == (uint32_t)l && h->first == 0 && h->count == (uint32_t)nks;
+            ok = ok && h->kind == DOWN && h->layer == (uint32_t)l && h->first == 0 && h->count == 1;
     }
     if (!ok) fail(c.sy, c.host_error, 4);
     return ok;
@@ -737,7 +757,7 @@ MB_DEV const uint8_t *take(Ctx &c, Cursor &cur, uint32_t kind)
     if (kind == QKV) ok = ok && h->count <= 4;
     if (kind == GATEUP) ok = ok && (h->count == 8 || h->count == (uint32_t)kGateupPerChunk);
     if (kind == HEAD) ok = ok && h->count <= (uint32_t)kHeadPerChunk;
-    if (kind == DOWN) ok = ok && h->count <= 2 && h->first < h->count;
+    if (kind == DOWN) ok = ok && h->count == 1 && h->first == 0;
     if (!ok) {
         if (c.ct == 0) fail(c.sy, c.host_error, 4);
         return nullptr;
@@ -922,7 +942,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     for (int i = c.ct; i < kSteps * 32; i += kNT) S.bf[i >> 5][i & 31] = make_uint2(0u, 0u);
     for (int i = c.ct; i < 2 * 32; i += kNT) {
         S.bfh[i >> 5][i & 31] = make_uint2(0u, 0u);
-        S.hst[i >> 5][i & 31] = 0.f;  // columns of the spare step owned by other CTAs stay zero
+        S.hst[i >> 5][i & 31] = 0.f;  // columns 8..31 of the piece's step stay zero
     }
     stamp(a, cta, c.ct, 0);
 
@@ -1271,7 +1291,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             float4 x;
             float pm;
             if (!add_sums_norm(c, xacc + (size_t)kAccRep * l * DIM, (unsigned)(HEADS * splits), g_ffn, x, pm,
-                               [&]() { return ffn_ready(c, cur, remaining, l, ngu, nks); }))
+                               [&]() { return ffn_ready(c, cur, remaining, l, ngu); }))
                 return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
             norm_finish(S, c.ct, g_ffn, x, pm, 0);
@@ -1300,20 +1320,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 gemv_mma<4>(&S, c.cw, c.lane, tl);
             cbar();
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 18);
-            // the products are in S.gp: the gate/up chunks go back at once
+            // the products are in S.gp: the block's gate/up chunks go back at once; a
+            // piece's chunk stays at the cursor until its down columns have been used
             if (c.ct == kIssuer)
-                for (int i = 0; i < ngu; i++) issue(c, cur.k + i + kSlots);
-            cur.k += ngu;
-            remaining -= ngu;
+                for (int i = 0; i < 2; i++) issue(c, cur.k + i + kSlots);
+            cur.k += 2;
+            remaining -= 2;
             // h = silu(gate) * up, each down step's 32 columns in one warp, quantized there
             // with the step's own scale (no block barrier between SwiGLU and limbs): warp 0
             // the CTA's block, unit 32 cta + lane at column lane (tile lane / 8 holds its
             // gate row 16 t + lane % 8 and its up row 8 below); warp 1, for a CTA with a
-            // piece, the piece's 8 units from tile 4 at their columns of the spare block
+            // piece, the piece's 8 units from tile 4 at columns 0..7 of its step
             if (c.cw < nks) {
                 const int t = c.cw == 0 ? c.lane >> 3 : 4, j = c.lane & 7;
                 const bool live = c.cw == 0 || c.lane < 8;
-                const int col = c.cw == 0 ? c.lane : (spare_lo(cta) & 31) + j;
+                const int col = c.cw == 0 ? c.lane : j;
                 float hv = 0.f;
                 if (live) {
                     const float g = row_sum(c, 16 * t + j), u = row_sum(c, 16 * t + 8 + j);
@@ -1341,34 +1362,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 7);
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 19);
         {
-            // the block's down step: the chunk at the cursor (checked above); a piece's
-            // step: the next one
+            // the block's down step (checked with the gate/up chunks; after a kept piece
+            // chunk), then the piece's 8 columns from that chunk
+            const int keep = nks - 1;
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-            for (int ks = 0; ks < nks; ks++) {
-                const uint8_t *w = ks == 0 ? S.ring[cur.k % kSlots] : take(c, cur, DOWN);
-                if (!w) return drain(c, cur);
-                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 20);
-                const uint8_t *frag = w + sizeof(ChunkHdr);
-                const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
-                down_step(c, frag, sw, S.bfh[ks], S.sh[ks], pacc);
-                stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
-                if (ks + 1 == nks) {
-                    // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
-                    const int t0 = kDownTiles * c.cw / kConsumerWarps;
-                    const int n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
-                    const int g = c.lane >> 2;
+            const uint8_t *frag = S.ring[(cur.k + keep) % kSlots] + sizeof(ChunkHdr);
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 20);
+            down_step<false>(c, frag, reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512), S.bfh[0],
+                             S.sh[0], pacc);
+            if (keep) {
+                const uint8_t *pf = S.ring[cur.k % kSlots] + sizeof(ChunkHdr) + kSpareDownOff;
+                down_step<true>(c, pf, reinterpret_cast<const float *>(pf + kSpareDownBytes), S.bfh[1], S.sh[1], pacc);
+            }
+            stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
+            // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
+            {
+                const int t0 = kDownTiles * c.cw / kConsumerWarps;
+                const int n = kDownTiles * (c.cw + 1) / kConsumerWarps - t0;
+                const int g = c.lane >> 2;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        if (i < n && (c.lane & 3) == 0) {
-                            const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
-                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0]);
-                            fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1]);
-                        }
+                for (int i = 0; i < 4; i++) {
+                    if (i < n && (c.lane & 3) == 0) {
+                        const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
+                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0]);
+                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1]);
                     }
                 }
-                give_back(c, cur);
-                remaining--;
             }
+            cbar();
+            if (c.ct == kIssuer)
+                for (int i = 0; i <= keep; i++) issue(c, cur.k + i + kSlots);
+            cur.k += 1 + keep;
+            remaining -= 1 + keep;
         }
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 6);
         // all-reduce: once all 148 CTAs' additions are complete every CTA adds the sums
@@ -1702,9 +1727,10 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
         return true;
     };
     // A chunk of 896-wide rows: tiles of 16 rows (tile_rows.size() a multiple of 16, or 8
-    // for a half tile), then the tile rows' 14 scales each, then extras.
+    // for a half tile), then the tile rows' 14 scales each, then extra bytes and floats.
     auto emit896 = [&](uint32_t kind, uint32_t layer, uint32_t first, uint32_t count,
-                       const std::vector<Row> &tile_rows, const std::vector<float> &extra, uint32_t gain_off) {
+                       const std::vector<Row> &tile_rows, const std::vector<uint8_t> &extra_bytes,
+                       const std::vector<float> &extra, uint32_t gain_off) {
         const bool half = tile_rows.size() == 8;
         if (!half && tile_rows.size() % 16) return false;
         Chunk ch = begin(kind, layer, first, count);
@@ -1718,6 +1744,7 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
         for (const Row &r : tile_rows)
             for (int g = 0; g < kGroups; g++) sc.push_back(scale(r, g));
         put_floats(sc);
+        stream.insert(stream.end(), extra_bytes.begin(), extra_bytes.end());
         put_floats(extra);
         return finish(ch, gain_off);
     };
@@ -1745,9 +1772,12 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
                 bias[2 * j] = bv[r0];
                 bias[2 * j + 1] = bv[r0 + 32];
             }
-            if (!emit896(QKV, l, lo, hi - lo, rows, bias, lt[ATTN_NORM].data)) return 1;
+            if (!emit896(QKV, l, lo, hi - lo, rows, {}, bias, lt[ATTN_NORM].data)) return 1;
             // gate/up: tiles of 8 gate rows then the 8 up rows of the same hidden units;
-            // the CTA's block in two chunks, then its spare piece (one tile)
+            // the CTA's block in two chunks, then its spare piece (one tile, followed by
+            // the piece's 8 down-projection columns and their scales)
+            const FileTensor *wd = &lt[WDOWN];
+            const int8_t *dw = reinterpret_cast<const int8_t *>(hfile + wd->data);
             std::vector<std::pair<int, int>> pieces = {{32 * c, 16}, {32 * c + 16, 16}};
             if (has_spare(c)) pieces.push_back({spare_lo(c), 8});
             for (size_t i = 0; i < pieces.size(); i++) {
@@ -1757,18 +1787,29 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
                     for (int j = 0; j < 8; j++) rows.push_back({&lt[WGATE], h0 + 8 * ti + j});
                     for (int j = 0; j < 8; j++) rows.push_back({&lt[WUP], h0 + 8 * ti + j});
                 }
-                if (!emit896(GATEUP, l, h0, n, rows, {}, i == 0 ? lt[FFN_NORM].data : 0)) return 1;
+                std::vector<uint8_t> pb;
+                std::vector<float> psc;
+                if (i == 2) {
+                    // entry e = 2 g + tig (tig < 2) of tile ti: rows 16 ti + g and 16 ti + g + 8,
+                    // columns h0 + 4 tig .. h0 + 4 tig + 3 (registers a0, a1)
+                    for (int ti = 0; ti < kDownTiles; ti++)
+                        for (int e = 0; e < 16; e++) {
+                            const int g = e >> 1, tig = e & 1;
+                            for (int rr = 0; rr < 2; rr++)
+                                for (int j = 0; j < 4; j++)
+                                    pb.push_back((uint8_t)dw[(size_t)(16 * ti + g + 8 * rr) * HIDDEN + h0 + 4 * tig + j]);
+                        }
+                    for (int r = 0; r < DIM; r++) psc.push_back(scale({wd, r}, h0 / GROUP));
+                    if (pb.size() != (size_t)kSpareDownBytes) return 1;
+                }
+                if (!emit896(GATEUP, l, h0, n, rows, pb, psc, i == 0 ? lt[FFN_NORM].data : 0)) return 1;
             }
-            // down: step 0 = columns of the CTA's block, step 1 = the spare block holding
-            // its piece; each 32-column step lies in one scale group
-            const FileTensor *wd = &lt[WDOWN];
-            const int8_t *dw = reinterpret_cast<const int8_t *>(hfile + wd->data);
-            const int nks = has_spare(c) ? 2 : 1;
-            for (int ks = 0; ks < nks; ks++) {
-                const int k0 = ks == 0 ? 32 * c : spare_lo(c) / 32 * 32;
+            // down: the 32 columns of the CTA's block (one scale group)
+            {
+                const int k0 = 32 * c;
                 std::vector<float> dsc(DIM);
                 for (int r = 0; r < DIM; r++) dsc[r] = scale({wd, r}, k0 / GROUP);
-                Chunk ch = begin(DOWN, l, ks, nks);
+                Chunk ch = begin(DOWN, l, 0, 1);
                 for (int ti = 0; ti < kDownTiles; ti++) {
                     const int8_t *rr[16];
                     for (int j = 0; j < 16; j++) rr[j] = dw + (size_t)(16 * ti + j) * HIDDEN;
@@ -1788,7 +1829,7 @@ int build_plan(const FileHeader *hdr, const unsigned char *hfile, const unsigned
             const int n = r1 - r0, padded = n <= 8 ? 8 : (n + 15) / 16 * 16;
             std::vector<Row> rows(padded, none);
             for (int r = r0; r < r1; r++) rows[r - r0] = {&t[0], r};
-            if (!emit896(HEAD, LAYERS, r0, n, rows, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
+            if (!emit896(HEAD, LAYERS, r0, n, rows, {}, {}, r0 == lo ? t[TENSORS - 1].data : 0)) return 1;
         }
     }
     // O by head, read by the attention CTAs (not streamed per CTA): for layer l and head
