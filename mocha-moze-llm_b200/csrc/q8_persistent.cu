@@ -102,6 +102,16 @@ constexpr float kFixInv = 1.0f / 4294967296.0f;
 // result does not depend on the split).  Two copies measured best: each further copy
 // costs the 148 readers one more 32-byte poll per round.
 constexpr int kAccRep = 2;
+// Each 32-byte sector of four accumulator words gets its own 128-byte line
+// (kSecPerLine sectors per line): the red operations on a line are served one by one,
+// and a reader's poll is one sector either way.
+constexpr int kSecPerLine = 1;
+constexpr int kAccCopyWords = (DIM / 4 / kSecPerLine) * 16;  // one copy of DIM sums, padded
+__host__ __device__ inline int acc_word(int row)
+{
+    const int sec = row >> 2;
+    return (sec / kSecPerLine) * 16 + (sec % kSecPerLine) * 4 + (row & 3);
+}
 
 struct Smem {
     uint8_t ring[kSlots][kSlotBytes];
@@ -570,7 +580,7 @@ MB_DEV size_t kv_index(int layer, int kvh, int pos)
 }
 
 // S.xs += the 896 counted fixed-point sums at acc once they hold `count` additions in
-// all: writer w adds to copy w % kAccRep (copies DIM words apart), so copy r waits for
+// all: writer w adds to copy w % kAccRep (copies kAccCopyWords apart), so copy r waits for
 // ceil((count - r) / kAccRep) of them.  Thread t < 224 polls its four words of every
 // copy (one 32-byte request per copy and round).  Every consumer thread returns the
 // same verdict (ends with a barrier).
@@ -583,7 +593,7 @@ MB_DEV bool add_sums(Ctx &c, const unsigned long long *acc, unsigned count)
 #pragma unroll
         for (int r = 0; r < kAccRep; r++) {
             need[r] = (count + kAccRep - 1 - r) / kAccRep;
-            dw_load4(acc + r * DIM + 4 * c.ct, v[r]);
+            dw_load4(acc + r * kAccCopyWords + acc_word(4 * c.ct), v[r]);
         }
         long long t0 = 0;
         for (;;) {
@@ -600,7 +610,7 @@ MB_DEV bool add_sums(Ctx &c, const unsigned long long *acc, unsigned count)
                 break;
             }
 #pragma unroll
-            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * DIM + 4 * c.ct, v[r]);
+            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * kAccCopyWords + acc_word(4 * c.ct), v[r]);
         }
         long long s[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -667,7 +677,7 @@ MB_DEV bool add_sums_norm(Ctx &c, const unsigned long long *acc, unsigned count,
 #pragma unroll
         for (int r = 0; r < kAccRep; r++) {
             need[r] = (count + kAccRep - 1 - r) / kAccRep;
-            dw_load4(acc + r * DIM + col, v[r]);
+            dw_load4(acc + r * kAccCopyWords + acc_word(col), v[r]);
         }
         long long t0 = 0;
         for (;;) {
@@ -684,7 +694,7 @@ MB_DEV bool add_sums_norm(Ctx &c, const unsigned long long *acc, unsigned count,
                 break;
             }
 #pragma unroll
-            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * DIM + col, v[r]);
+            for (int r = 0; r < kAccRep; r++) dw_load4(acc + r * kAccCopyWords + acc_word(col), v[r]);
         }
         long long s4[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -927,15 +937,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     // share of the other set, which the next step uses (the last step that used it has
     // finished: it was the previous launch on this stream)
     const int set = (int)(epoch & 1u);
-    unsigned long long *dacc = scr.dacc + (size_t)set * kAccRep * LAYERS * DIM;
-    unsigned long long *xacc = scr.xacc + (size_t)set * kAccRep * LAYERS * DIM;
+    unsigned long long *dacc = scr.dacc + (size_t)set * kAccRep * LAYERS * kAccCopyWords;
+    unsigned long long *xacc = scr.xacc + (size_t)set * kAccRep * LAYERS * kAccCopyWords;
     {
-        unsigned long long *od = scr.dacc + (size_t)(set ^ 1) * kAccRep * LAYERS * DIM;
-        unsigned long long *ox = scr.xacc + (size_t)(set ^ 1) * kAccRep * LAYERS * DIM;
+        unsigned long long *od = scr.dacc + (size_t)(set ^ 1) * kAccRep * LAYERS * kAccCopyWords;
+        unsigned long long *ox = scr.xacc + (size_t)(set ^ 1) * kAccRep * LAYERS * kAccCopyWords;
         const int lo = kAccRep * LAYERS * DIM * cta / kCTAs, hi = kAccRep * LAYERS * DIM * (cta + 1) / kCTAs;
         for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) {
-            od[i] = 0ull;
-            ox[i] = 0ull;
+            const size_t w = (size_t)(i / DIM) * kAccCopyWords + acc_word(i % DIM);  // (copy, row) -> word
+            od[w] = 0ull;
+            ox[w] = 0ull;
         }
     }
     // B-fragment columns 3..7 stay zero; columns 0..2 are rewritten by every quantize
@@ -1275,8 +1286,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 for (int i = 0; i < 4; i++) {
                     if (i < otn && (c.lane & 3) == 0) {
                         const int r0 = 16 * (ot0 + i) + g, r1 = r0 + 8;
-                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0] * f);
-                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1] * f);
+                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * kAccCopyWords + acc_word(r0), pacc[i][0] * f);
+                        fix_add(xacc + (size_t)(kAccRep * l + cta % kAccRep) * kAccCopyWords + acc_word(r1), pacc[i][1] * f);
                     }
                 }
             }
@@ -1290,7 +1301,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         {
             float4 x;
             float pm;
-            if (!add_sums_norm(c, xacc + (size_t)kAccRep * l * DIM, (unsigned)(HEADS * splits), g_ffn, x, pm,
+            if (!add_sums_norm(c, xacc + (size_t)kAccRep * l * kAccCopyWords, (unsigned)(HEADS * splits), g_ffn, x, pm,
                                [&]() { return ffn_ready(c, cur, remaining, l, ngu); }))
                 return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
@@ -1384,8 +1395,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 for (int i = 0; i < 4; i++) {
                     if (i < n && (c.lane & 3) == 0) {
                         const int r0 = 16 * (t0 + i) + g, r1 = r0 + 8;
-                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r0, pacc[i][0]);
-                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * DIM + r1, pacc[i][1]);
+                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * kAccCopyWords + acc_word(r0), pacc[i][0]);
+                        fix_add(dacc + (size_t)(kAccRep * l + cta % kAccRep) * kAccCopyWords + acc_word(r1), pacc[i][1]);
                     }
                 }
             }
@@ -1402,13 +1413,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
         if (l + 1 < LAYERS) {
             float4 x;
             float pm;
-            if (!add_sums_norm(c, dacc + (size_t)kAccRep * l * DIM, kCTAs, g_attn, x, pm,
+            if (!add_sums_norm(c, dacc + (size_t)kAccRep * l * kAccCopyWords, kCTAs, g_attn, x, pm,
                                [&]() { return qkv_ready(c, cur, remaining, l + 1); }))
                 return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
             norm_finish(S, c.ct, g_attn, x, pm, 0);
         } else {
-            if (!add_sums(c, dacc + (size_t)kAccRep * l * DIM, kCTAs)) return drain(c, cur);
+            if (!add_sums(c, dacc + (size_t)kAccRep * l * kAccCopyWords, kCTAs)) return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
         }
     }
@@ -1634,7 +1645,7 @@ size_t smem_bytes() { return sizeof(Smem); }
 
 size_t scratch_words()
 {
-    return (size_t)DIM + (size_t)kReplicas * kStrideKv + kPartWords + 4 * (size_t)kAccRep * LAYERS * DIM;
+    return (size_t)DIM + (size_t)kReplicas * kStrideKv + kPartWords + 4 * (size_t)kAccRep * LAYERS * kAccCopyWords;
 }
 
 void carve_scratch(unsigned long long *base, Scratch *scr)
@@ -1643,7 +1654,7 @@ void carve_scratch(unsigned long long *base, Scratch *scr)
     scr->kv = scr->q + DIM;
     scr->part = scr->kv + kReplicas * kStrideKv;
     scr->dacc = scr->part + kPartWords;
-    scr->xacc = scr->dacc + 2 * (size_t)kAccRep * LAYERS * DIM;
+    scr->xacc = scr->dacc + 2 * (size_t)kAccRep * LAYERS * kAccCopyWords;
 
 }
 

@@ -66,10 +66,10 @@ struct Scratch {
     unsigned long long *q;        // [DIM] rotated queries
     unsigned long long *kv;       // [kReplicas][KV_HEADS][2][HEAD_DIM] this position's K (rotated) and V
     unsigned long long *part;     // [HEADS][kMaxSplit][2] (max, sum of weights) of every attention split
-    unsigned long long *dacc;     // [2][LAYERS][2][DIM] down-projection sums: fixed point (value * 2^32) in
+    unsigned long long *dacc;     // [2][LAYERS][2][DIM, padded] down-projection sums: fixed point (value * 2^32) in
                                   // bits 8..63, additions counted in bits 0..7; two sets used by
                                   // alternating steps (epoch & 1), two copies per layer (writer parity)
-    unsigned long long *xacc;     // [2][LAYERS][2][DIM] attention block (O of every head) sums, the same form
+    unsigned long long *xacc;     // [2][LAYERS][2][DIM, padded] attention block (O of every head) sums, the same form
     unsigned long long *cand;     // [kCTAs][64] per-CTA candidate keys (plain)
 };
 
