@@ -660,12 +660,13 @@ struct Cursor {
 // add_sums for the reductions that feed a norm: thread t < 224 polls the words of its
 // norm columns quant_col(t) .. + 3 (32 bytes per copy), adds them to S.xs and to x, and
 // runs the norm's first half on x (pm as norm_sums gives it) before the barrier that the
-// reduction ends with anyway; meanwhile the issuer thread, idle here, runs check() (the
-// next phase's chunks: landed, headers valid), whose verdict joins the barrier's.  The
-// caller finishes with norm_finish.
-template <typename Check>
+// reduction ends with anyway; meanwhile the threads t >= 224, idle here, run side()
+// and the issuer thread (one of them) check() -- the next phase's chunks: landed,
+// headers valid -- whose verdict joins the barrier's.  The caller finishes with
+// norm_finish.
+template <typename Check, typename Side>
 MB_DEV bool add_sums_norm(Ctx &c, const unsigned long long *acc, unsigned count, float4 g, float4 &x, float &pm,
-                          Check check)
+                          Check check, Side side)
 {
     int ok = 1;
     x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -710,7 +711,37 @@ MB_DEV bool add_sums_norm(Ctx &c, const unsigned long long *acc, unsigned count,
         norm_sums(c.S, c.ct, g, x, pm);
     }
     if (c.ct == kIssuer && !check()) ok = 0;
+    if (c.ct >= DIM / 4) side();
     return cbar_and(ok) != 0;
+}
+
+// attention split of one query head: positions [p0, p0+np)
+struct AttnUnit {
+    int head, split, p0, np;
+};
+
+// Threads [t0, t0 + nt): start the asynchronous copy of the past K/V rows of layer l for
+// this CTA's attention split into shared memory (they do not depend on this step), and
+// (thread t0) the L2 prefetch of the head's O columns and scales, wanted after the
+// attention.
+MB_DEV void attn_prefetch(Ctx &c, const Args &a, const AttnUnit &unit, int l, int pos, int t0, int nt)
+{
+    const int kvh = unit.head / GQA;
+    const int past = min(unit.np, pos - unit.p0);  // rows < pos
+    const float *kb = a.b.kc + kv_index(l, kvh, unit.p0);
+    const float *vb = a.b.vc + kv_index(l, kvh, unit.p0);
+    for (int i = c.ct - t0; i < past * (HEAD_DIM / 4); i += nt) {
+        const int p = i / (HEAD_DIM / 4), q4 = i % (HEAD_DIM / 4);
+        cp_async16(&c.S.u.att.k[p][q4 * 4], kb + p * HEAD_DIM + q4 * 4);
+        cp_async16(&c.S.u.att.v[p][q4 * 4], vb + p * HEAD_DIM + q4 * 4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (c.ct == t0) {
+        const uint8_t *of = c.S.ofrag + (size_t)(l * HEADS + unit.head) * kOHeadBytes;
+        const float *os = c.S.oscale + (size_t)(l * HEADS + unit.head) * DIM;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(of), "r"(kOHeadBytes) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(os), "r"(DIM * 4) : "memory");
+    }
 }
 
 // Issuer-side checks of the chunks the next phase reads without waiting.  The QKV job of
@@ -862,11 +893,6 @@ MB_DEV unsigned long long block_max(Ctx &c, unsigned long long v)
     return best;
 }
 
-// attention split of one query head: positions [p0, p0+np)
-struct AttnUnit {
-    int head, split, p0, np;
-};
-
 __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -983,27 +1009,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
     // next to its use would put two dependent L2 round trips on the critical path)
     float4 g_attn = load_gain(c.ct, S.gain[0][0]), g_ffn = load_gain(c.ct, S.gain[1][0]);
     for (int l = 0; l < LAYERS; l++) {
-        // K/V of past positions for this CTA's attention split: no dependency on this
-        // step, copied asynchronously while the QKV phase runs
-        if (unit.head >= 0) {
-            const int kvh = unit.head / GQA;
-            const int past = min(unit.np, pos - unit.p0);  // rows < pos
-            const float *kb = a.b.kc + kv_index(l, kvh, unit.p0);
-            const float *vb = a.b.vc + kv_index(l, kvh, unit.p0);
-            for (int i = c.ct; i < past * (HEAD_DIM / 4); i += kNT) {
-                const int p = i / (HEAD_DIM / 4), q4 = i % (HEAD_DIM / 4);
-                cp_async16(&S.u.att.k[p][q4 * 4], kb + p * HEAD_DIM + q4 * 4);
-                cp_async16(&S.u.att.v[p][q4 * 4], vb + p * HEAD_DIM + q4 * 4);
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-            // this head's O columns and scales, wanted after the attention: into L2 now
-            if (c.ct == 0) {
-                const uint8_t *of = S.ofrag + (size_t)(l * HEADS + unit.head) * kOHeadBytes;
-                const float *os = S.oscale + (size_t)(l * HEADS + unit.head) * DIM;
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(of), "r"(kOHeadBytes) : "memory");
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(os), "r"(DIM * 4) : "memory");
-            }
-        }
+        // layer 0's past K/V for this CTA's attention split (every later layer's were
+        // started by the idle threads of the previous layer's x_out reduction)
+        if (l == 0 && unit.head >= 0) attn_prefetch(c, a, unit, 0, pos, 0, kNT);
         // ---- QKV + bias + RoPE + KV write
         stamp(a, cta, c.ct, 2 + l * kTraceLayer + 0);
         {
@@ -1302,7 +1310,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             float4 x;
             float pm;
             if (!add_sums_norm(c, xacc + (size_t)kAccRep * l * kAccCopyWords, (unsigned)(HEADS * splits), g_ffn, x, pm,
-                               [&]() { return ffn_ready(c, cur, remaining, l, ngu); }))
+                               [&]() { return ffn_ready(c, cur, remaining, l, ngu); }, []() {}))
                 return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 5);
             norm_finish(S, c.ct, g_ffn, x, pm, 0);
@@ -1414,7 +1422,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             float4 x;
             float pm;
             if (!add_sums_norm(c, dacc + (size_t)kAccRep * l * kAccCopyWords, kCTAs, g_attn, x, pm,
-                               [&]() { return qkv_ready(c, cur, remaining, l + 1); }))
+                               [&]() { return qkv_ready(c, cur, remaining, l + 1); },
+                               [&]() {
+                                   if (unit.head >= 0) attn_prefetch(c, a, unit, l + 1, pos, DIM / 4, kNT - DIM / 4);
+                               }))
                 return drain(c, cur);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 8);
             norm_finish(S, c.ct, g_attn, x, pm, 0);
