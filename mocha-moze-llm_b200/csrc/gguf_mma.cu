@@ -624,7 +624,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
         float tot = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; w++) tot += red[w];
-        sc = 1.0f / sqrtf(tot / g.cols + g.eps);
+        sc = rsqrtf(tot / g.cols + g.eps);
     }
 #pragma unroll
     for (int e = 0; e < kMaxUnits; e++) {
@@ -638,8 +638,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
             float4 x = xv[e][h];
             if (g.up) {  // h = silu(gate) * up, as the reference's FFN
                 const float4 u = uv[e][h];
-                x = make_float4((x.x / (1.0f + expf(-x.x))) * u.x, (x.y / (1.0f + expf(-x.y))) * u.y,
-                                (x.z / (1.0f + expf(-x.z))) * u.z, (x.w / (1.0f + expf(-x.w))) * u.w);
+                x = make_float4(__fdividef(x.x, 1.0f + expf(-x.x)) * u.x, __fdividef(x.y, 1.0f + expf(-x.y)) * u.y,
+                                __fdividef(x.z, 1.0f + expf(-x.z)) * u.z, __fdividef(x.w, 1.0f + expf(-x.w)) * u.w);
             }
             if (g.gain) {
                 const float4 gn = gv[h];
@@ -653,11 +653,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
             sum += (x.x + x.y) + (x.z + x.w);
         }
         // block max over the warp; step sum over its 4 threads
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        m = mb::warp_max(m);
 #pragma unroll
         for (int o = 1; o < 4; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        const float inv = m > 0.f ? 127.f / m : 0.f;
+        const float inv = m > 0.f ? __fdividef(127.f, m) : 0.f;
         uint32_t *bw = reinterpret_cast<uint32_t *>(&bf[s * 32]);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
@@ -697,7 +696,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_mma(const Gemv g)
             }
         }
         if (tq == 0) {
-            sx[s] = m / (127.f * 254.f);
+            sx[s] = m * (1.0f / (127.f * 254.f));
             x32[s] = sum;
         }
     }
