@@ -33,7 +33,7 @@ WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per toke
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 ONE_THREAD_TOKENS = 16         # bounded 1-thread sample of the reference engine
 SERVE_REF_SEQS = 2             # sequences of the batched job timed on the reference engine
-TRAFFIC_PER_TOKEN = 545_005_568  # DRAM read + write per k_step launch (544.58 + 0.43 MB), ncu, positions 40-42
+TRAFFIC_PER_TOKEN = 539_433_216  # DRAM read + write per k_step launch (538.78 + 0.65 MB), ncu, positions 40-42
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
@@ -411,10 +411,11 @@ def batched_cpu_baseline(model_path):
 
 # phase boundaries of the persistent step's trace stamps (offset within a layer, name),
 # in the order a CTA reaches them; see mocha_q8_trace_step in include/mocha_b200.h
-TRACE_PHASES = [(0, "x_in"), (12, "qkv norm+limbs"), (11, "qkv chunk"), (13, "qkv products"), (1, "qkv stored"),
-                (14, "att q/k/v in"), (15, "att past K/V"), (16, "att softmax+PV"), (2, "attention + O added"),
+TRACE_PHASES = [(0, "x_in"), (12, "qkv input ready"), (11, "qkv chunk"), (13, "qkv products"), (1, "qkv stored"),
+                (14, "att q/k/v in"), (15, "att past K/V"), (16, "att softmax+PV"), (3, "att merged+limbs"),
+                (4, "att O products"), (23, "att split weight"), (2, "attention + O added"),
                 (5, "x_mid"), (10, "ffn norm+limbs"), (9, "gate/up chunks"), (18, "gate/up products"),
-                (7, "swiglu"), (19, "h limbs"), (20, "down chunk"), (21, "down products"), (6, "down added"),
+                (7, "swiglu+limbs"), (20, "down chunk"), (21, "down products"), (6, "down added"),
                 (8, "x_out")]
 
 
