@@ -1151,8 +1151,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
                 const float sc = valid ? z * 0.125f : -INFINITY;
                 const float m = mb::warp_max(sc);
                 const float e = valid ? expf(sc - m) : 0.f;
-                const float lw = mb::warp_sum(qd == 0 ? e : 0.f);  // each position sits in four lanes
-                float a0 = 0.f, a1 = 0.f;
+                // the warp's sum of weights comes with the P.V shuffles (every lane sees
+                // the 8 weights in order)
+                float lw = 0.f, a0 = 0.f, a1 = 0.f;
                 const float *vb = S.u.att.v[8 * c.cw];
                 // rows past np read the next rows of the buffer (or, for row 8 * 12 + 7 =
                 // kAttnLenMax, the query after it) and enter as zeros: no branch around
@@ -1160,6 +1161,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     const float ej = __shfl_sync(0xffffffffu, e, j);  // lane j holds position 8 cw + j
+                    lw += ej;
                     const bool in = 8 * c.cw + j < np;
                     const float x0 = vb[j * HEAD_DIM + c.lane], x1 = vb[j * HEAD_DIM + 32 + c.lane];
                     a0 = fmaf(ej, in ? x0 : 0.f, a0);
