@@ -538,39 +538,46 @@ MB_DEV float row_sum(const Ctx &c, int row)
 }
 
 // Down projection, one 32-column step of this CTA's hidden units for all 896 rows
-// ([kDownTiles][32 lanes][16 B], or with Piece the 8-column form of a spare piece,
-// [kDownTiles][16][8 B]): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the step's
-// partials (v * weight scale * input scale sx) are added to acc[tile][row g | row g + 8].
-// A warp with
-// three tiles also multiplies a fourth (the next warp's first) into an acc entry its
-// caller ignores: no branch around the loads.
-template <bool Piece>
-MB_DEV void down_step(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bfs)[32], float sx,
-                      float (&acc)[4][2])
+// ([kDownTiles][32 lanes][16 B]; a spare piece's 8-column form [kDownTiles][16][8 B]:
+// registers a0, a1 of lanes with tig < 2): warp cw's tiles [56 cw/16, 56 (cw+1)/16); the
+// step's partials (v * weight scale * input scale sx) are added to acc[tile][row g |
+// row g + 8].  A warp with three tiles also multiplies a fourth (the next warp's first)
+// into an acc entry its caller ignores: no branch around the loads.
+// The block's down step and, WithPiece, the piece's step in one pass over the warp's
+// tiles (the two MMAs of a tile are independent): each acc entry adds the block's
+// product, then the piece's (the order of two separate passes).
+template <bool WithPiece>
+MB_DEV void down_steps(Ctx &c, const uint8_t *frag, const float *sw, const uint2 (&bf0)[32], float sx0,
+                       const uint8_t *pfrag, const float *psw, const uint2 (&bf1)[32], float sx1, float (&acc)[4][2])
 {
     const int t0 = kDownTiles * c.cw / kConsumerWarps;
-    const uint2 b = bfs[c.lane];
+    const uint2 b0 = bf0[c.lane], b1 = bf1[c.lane];
     const int g = c.lane >> 2, tig = c.lane & 3;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int t = min(t0 + i, kDownTiles - 1);
-        int d[4] = {0, 0, 0, 0};
-        uint4 a = make_uint4(0u, 0u, 0u, 0u);
-        if (!Piece) {
-            a = *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16);
-        } else {
-            const uint2 v = *reinterpret_cast<const uint2 *>(frag + ((size_t)t * 16 + 2 * g + (tig & 1)) * 8);
+        int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
+        mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16), b0);
+        if (WithPiece) {
+            uint4 a = make_uint4(0u, 0u, 0u, 0u);
+            const uint2 v = *reinterpret_cast<const uint2 *>(pfrag + ((size_t)t * 16 + 2 * g + (tig & 1)) * 8);
             if (tig < 2) {
                 a.x = v.x;
                 a.y = v.y;
             }
+            mma_s8(e, a, b1);
         }
-        mma_s8(d, a, b);
         float v0, v1;
         combine(d, v0, v1);
         const int r0 = 16 * t + g;
-        acc[i][0] = fmaf(v0, sw[r0] * sx, acc[i][0]);
-        acc[i][1] = fmaf(v1, sw[r0 + 8] * sx, acc[i][1]);
+        acc[i][0] = fmaf(v0, sw[r0] * sx0, acc[i][0]);
+        acc[i][1] = fmaf(v1, sw[r0 + 8] * sx0, acc[i][1]);
+        if (WithPiece) {
+            float w0, w1;
+            combine(e, w0, w1);
+            acc[i][0] = fmaf(w0, psw[r0] * sx1, acc[i][0]);
+            acc[i][1] = fmaf(w1, psw[r0 + 8] * sx1, acc[i][1]);
+        }
     }
 }
 
@@ -1389,12 +1396,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
             const uint8_t *frag = S.ring[(cur.k + keep) % kSlots] + sizeof(ChunkHdr);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 20);
-            down_step<false>(c, frag, reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512), S.bfh[0],
-                             S.sh[0], pacc);
-            if (keep) {
-                const uint8_t *pf = S.ring[cur.k % kSlots] + sizeof(ChunkHdr) + kSpareDownOff;
-                down_step<true>(c, pf, reinterpret_cast<const float *>(pf + kSpareDownBytes), S.bfh[1], S.sh[1], pacc);
-            }
+            const float *sw = reinterpret_cast<const float *>(frag + (size_t)kDownTiles * 512);
+            const uint8_t *pf = S.ring[cur.k % kSlots] + sizeof(ChunkHdr) + kSpareDownOff;
+            const float *psw = reinterpret_cast<const float *>(pf + kSpareDownBytes);
+            if (keep)
+                down_steps<true>(c, frag, sw, S.bfh[0], S.sh[0], pf, psw, S.bfh[1], S.sh[1], pacc);
+            else
+                down_steps<false>(c, frag, sw, S.bfh[0], S.sh[0], pf, psw, S.bfh[1], S.sh[1], pacc);
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 21);
             // rows 16 t + g and 16 t + g + 8 of the warp's tiles: this CTA's partial
             {
