@@ -90,8 +90,7 @@ constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: v + kMagic rounds 
 static_assert(DIM % 64 == 0 && kCTAs % 4 == 0, "layout");
 
 enum Phase { PH_QKV = 0, PH_ATTN = 1 };
-constexpr float kFixScale = 4294967296.0f;     // 2^32: partial sums as fixed point ...
-constexpr float kFixInv = 1.0f / 4294967296.0f;
+constexpr float kFixInv = 1.0f / 4294967296.0f;  // partial sums as fixed point, scaled by 2^32 ...
 // ... in bits 8..63 of an accumulator word; bits 0..7 count the additions (< 256), so a
 // reader sees from the word alone when every contributor's addition has landed.  Each
 // addition is (q << 8) + 1, q = rint(v * 2^32): the low byte only ever gains the +1s,
