@@ -496,26 +496,34 @@ MB_DEV void gemv_mma(Smem *Sp, int cw, int lane, Tiles tl)
     const int g = lane >> 2, tig = lane & 3, grp = cw;
     const uint2 b0 = S.bf[2 * grp][lane], b1 = S.bf[2 * grp + 1][lane];
     const float f = S.sxs[grp];
+    // every tile's first MMA, then every second one, then the combines: each tile's
+    // MMA -> MMA -> shuffle -> convert chain is about 90 cycles, paid once, not per tile
+    int d[MAXT][4];
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+#pragma unroll
+        for (int i = 0; i < MAXT; i++) {
+            const int t = min(i, tl.T - 1), ch = t >> 1;
+            const uint8_t *fr = (ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2]) + (t & 1) * kTileBytes;
+            uint4 a;
+            if (tl.half) {
+                const uint2 x = *reinterpret_cast<const uint2 *>(fr + ((size_t)(2 * grp + k) * 32 + lane) * 8);
+                a = make_uint4(x.x, 0u, x.y, 0u);
+            } else {
+                a = *reinterpret_cast<const uint4 *>(fr + ((size_t)(2 * grp + k) * 32 + lane) * 16);
+            }
+            if (k == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) d[i][j] = 0;
+            }
+            mma_s8(d[i], a, k == 0 ? b0 : b1);
+        }
 #pragma unroll
     for (int i = 0; i < MAXT; i++) {
         const int t = min(i, tl.T - 1), ch = t >> 1;
-        const uint8_t *fr = (ch == 0 ? tl.frag[0] : ch == 1 ? tl.frag[1] : tl.frag[2]) + (t & 1) * kTileBytes;
         const float *sc = (ch == 0 ? tl.sc[0] : ch == 1 ? tl.sc[1] : tl.sc[2]) + (t & 1) * 16 * kGroups;
-        uint4 a0, a1;
-        if (tl.half) {
-            const uint2 x0 = *reinterpret_cast<const uint2 *>(fr + ((size_t)(2 * grp) * 32 + lane) * 8);
-            const uint2 x1 = *reinterpret_cast<const uint2 *>(fr + ((size_t)(2 * grp + 1) * 32 + lane) * 8);
-            a0 = make_uint4(x0.x, 0u, x0.y, 0u);
-            a1 = make_uint4(x1.x, 0u, x1.y, 0u);
-        } else {
-            a0 = *reinterpret_cast<const uint4 *>(fr + ((size_t)(2 * grp) * 32 + lane) * 16);
-            a1 = *reinterpret_cast<const uint4 *>(fr + ((size_t)(2 * grp + 1) * 32 + lane) * 16);
-        }
-        int d[4] = {0, 0, 0, 0};
-        mma_s8(d, a0, b0);
-        mma_s8(d, a1, b1);
         float v0, v1;
-        combine(d, v0, v1);
+        combine(d[i], v0, v1);
         // (a half tile has 8 rows of scales: row g stands in for the absent row g + 8)
         const float s0 = sc[g * kGroups + grp], s1 = sc[(tl.half ? g : g + 8) * kGroups + grp];
         if (tig == 0 && i < tl.T) {
@@ -552,11 +560,15 @@ MB_DEV void down_steps(Ctx &c, const uint8_t *frag, const float *sw, const uint2
     const int t0 = kDownTiles * c.cw / kConsumerWarps;
     const uint2 b0 = bf0[c.lane], b1 = bf1[c.lane];
     const int g = c.lane >> 2, tig = c.lane & 3;
+    // every MMA of the warp is issued before the first combine: a tile's MMA -> shuffle
+    // -> convert chain is about 70 cycles, and tile after tile it would be paid four times
+    int d[4][4], e[4][4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int t = min(t0 + i, kDownTiles - 1);
-        int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
-        mma_s8(d, *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16), b0);
+#pragma unroll
+        for (int j = 0; j < 4; j++) d[i][j] = e[i][j] = 0;
+        mma_s8(d[i], *reinterpret_cast<const uint4 *>(frag + ((size_t)t * 32 + c.lane) * 16), b0);
         if (WithPiece) {
             uint4 a = make_uint4(0u, 0u, 0u, 0u);
             const uint2 v = *reinterpret_cast<const uint2 *>(pfrag + ((size_t)t * 16 + 2 * g + (tig & 1)) * 8);
@@ -564,16 +576,20 @@ MB_DEV void down_steps(Ctx &c, const uint8_t *frag, const float *sw, const uint2
                 a.x = v.x;
                 a.y = v.y;
             }
-            mma_s8(e, a, b1);
+            mma_s8(e[i], a, b1);
         }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int t = min(t0 + i, kDownTiles - 1);
         float v0, v1;
-        combine(d, v0, v1);
+        combine(d[i], v0, v1);
         const int r0 = 16 * t + g;
         acc[i][0] = fmaf(v0, sw[r0] * sx0, acc[i][0]);
         acc[i][1] = fmaf(v1, sw[r0 + 8] * sx0, acc[i][1]);
         if (WithPiece) {
             float w0, w1;
-            combine(e, w0, w1);
+            combine(e[i], w0, w1);
             acc[i][0] = fmaf(w0, psw[r0] * sx1, acc[i][0]);
             acc[i][1] = fmaf(w1, psw[r0 + 8] * sx1, acc[i][1]);
         }
@@ -1255,17 +1271,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             // (a warp with three tiles also multiplies a copy of its last; unused)
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
             const uint2 bo[2] = {S.bfo[0][c.lane], S.bfo[1][c.lane]};
+            {
+                // all eight MMAs first, then the combines (as in down_steps)
+                int d[4][2][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
+                for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    int d[4] = {0, 0, 0, 0};
-                    mma_s8(d, ofr[ks][i], bo[ks]);
-                    float v0, v1;
-                    combine(d, v0, v1);
-                    pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
-                    pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
-                }
+                    for (int ks = 0; ks < 2; ks++) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++) d[i][ks][j] = 0;
+                        mma_s8(d[i][ks], ofr[ks][i], bo[ks]);
+                    }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int ks = 0; ks < 2; ks++) {
+                        float v0, v1;
+                        combine(d[i][ks], v0, v1);
+                        pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
+                        pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
+                    }
             }
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
             // this split's weight in the head's softmax: exp(m - M) / L over the splits
