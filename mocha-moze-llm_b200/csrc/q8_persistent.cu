@@ -1272,25 +1272,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(Args a)
             float pacc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
             const uint2 bo[2] = {S.bfo[0][c.lane], S.bfo[1][c.lane]};
             {
-                // all eight MMAs first, then the combines (as in down_steps)
-                int d[4][2][4];
+                // The head's 64 columns are one scale group of O's rows and one
+                // quantization of the output: both 32-column steps add into one int32 sum
+                // per tile (|D| <= 2 * 32 * 128 * 127), combined once.  Every tile's first
+                // MMA, then every second one, then the combines (as in gemv_mma).
+                int d[4][4];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int ks = 0; ks < 2; ks++)
 #pragma unroll
-                    for (int ks = 0; ks < 2; ks++) {
+                    for (int i = 0; i < 4; i++) {
+                        if (ks == 0) {
 #pragma unroll
-                        for (int j = 0; j < 4; j++) d[i][ks][j] = 0;
-                        mma_s8(d[i][ks], ofr[ks][i], bo[ks]);
+                            for (int j = 0; j < 4; j++) d[i][j] = 0;
+                        }
+                        mma_s8(d[i], ofr[ks][i], bo[ks]);
                     }
 #pragma unroll
-                for (int i = 0; i < 4; i++)
-#pragma unroll
-                    for (int ks = 0; ks < 2; ks++) {
-                        float v0, v1;
-                        combine(d[i][ks], v0, v1);
-                        pacc[i][0] = fmaf(v0, osc[i][0], pacc[i][0]);
-                        pacc[i][1] = fmaf(v1, osc[i][1], pacc[i][1]);
-                    }
+                for (int i = 0; i < 4; i++) {
+                    float v0, v1;
+                    combine(d[i], v0, v1);
+                    pacc[i][0] = v0 * osc[i][0];
+                    pacc[i][1] = v1 * osc[i][1];
+                }
             }
             stamp(a, cta, c.ct, 2 + l * kTraceLayer + 4);
             // this split's weight in the head's softmax: exp(m - M) / L over the splits
