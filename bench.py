@@ -33,7 +33,7 @@ WEIGHT_BYTES = 525_120_000     # int8 + fp32 scales + fp32 norms/biases per toke
 KV_BYTES_PER_POS = 24_576      # 24 layers x (K+V) x 128 x fp32
 ONE_THREAD_TOKENS = 16         # bounded 1-thread sample of the reference engine
 SERVE_REF_SEQS = 2             # sequences of the batched job timed on the reference engine
-TRAFFIC_PER_TOKEN = 539_433_216  # DRAM read + write per k_step launch (538.78 + 0.65 MB), ncu, positions 40-42
+TRAFFIC_PER_TOKEN = 539_311_872  # DRAM read + write per k_step launch (538.71 + 0.60 MB), ncu, positions 40-42
 # prefill workload: one 1024-token prompt, head on the last position
 PREFILL_LEN = 1024
 PREFILL_FLOP = 2 * 357_826_560 * 1024 + 45.1e9 + 2 * 136_134_656   # algorithmic FLOP per prompt
