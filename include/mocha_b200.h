@@ -197,12 +197,6 @@ int mocha_tc_gemm_check(int device, int rows, int n, int cols, const signed char
 int mocha_tq_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
                         const float *x, float *y, int splits);
 
-/* The same product through the converted-weight tcgen05 GEMM: int8 weights widened to
- * bf16 pairs on chip, x as bf16 pairs, one fp32 accumulator over K.
- * rows % 128 == 0, cols % 64 == 0, 1 <= n <= 1024.  No reference counterpart. */
-int mocha_tw_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
-                        const float *x, float *y, int splits);
-
 #ifdef __cplusplus
 }
 #endif

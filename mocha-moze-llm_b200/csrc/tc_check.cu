@@ -8,7 +8,6 @@
 #include "mocha_b200.h"
 #include "tc_gemm.cuh"
 #include "tc_q8gemm.cuh"
-#include "tc_w8gemm.cuh"
 
 namespace {
 
@@ -131,54 +130,6 @@ extern "C" int mocha_tq_gemm_check(int device, int rows, int n, int cols, const 
     MB_CHECK(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
     if (herr) {
         fprintf(stderr, "mocha_tq_gemm_check: kernel reported error %d\n", herr);
-        return 1;
-    }
-    std::vector<float> part((size_t)sp.splits * n * rows);
-    MB_CHECK(cudaMemcpy(part.data(), dp, part.size() * 4, cudaMemcpyDeviceToHost));
-    for (size_t i = 0; i < (size_t)n * rows; i++) {
-        float acc = 0.f;
-        for (int s = 0; s < sp.splits; s++) acc += part[(size_t)s * n * rows + i];
-        y[i] = acc;
-    }
-    return 0;
-}
-
-extern "C" int mocha_tw_gemm_check(int device, int rows, int n, int cols, const signed char *q, const float *scales,
-                                   const float *x, float *y, int splits)
-{
-    if (rows <= 0 || rows % 128 || cols <= 0 || cols % 64 || n <= 0 || n > 1024 || !q || !scales || !x || !y) {
-        fprintf(stderr, "mocha_tw_gemm_check: bad arguments\n");
-        return 1;
-    }
-    MB_CHECK(cudaSetDevice(device));
-    Buffers b;
-    const size_t wn = (size_t)rows * cols, xn = (size_t)n * cols;
-    int8_t *dq = b.alloc<int8_t>(wn);
-    float *ds = b.alloc<float>(wn / 64), *dx = b.alloc<float>(xn);
-    __nv_bfloat16 *xhi = b.alloc<__nv_bfloat16>(xn), *xlo = b.alloc<__nv_bfloat16>(xn);
-    int *err = b.alloc<int>(1);
-    if (!dq || !ds || !dx || !xhi || !xlo || !err) {
-        fprintf(stderr, "mocha_tw_gemm_check: out of device memory\n");
-        return 1;
-    }
-    MB_CHECK(cudaMemcpy(dq, q, wn, cudaMemcpyHostToDevice));
-    MB_CHECK(cudaMemcpy(ds, scales, wn / 64 * 4, cudaMemcpyHostToDevice));
-    MB_CHECK(cudaMemcpy(dx, x, xn * 4, cudaMemcpyHostToDevice));
-    MB_CHECK(cudaMemset(err, 0, sizeof(int)));
-    k_split_rows<<<148 * 4, 256>>>(dx, xn, xhi, xlo);
-    MB_CHECK(cudaGetLastError());
-    mb::tw::Gemm g;
-    if (mb::tw::plan(&g, dq, ds, rows, cols, xhi, xlo, n, nullptr, rows, splits, err)) return 1;
-    const mb::tc::Split sp = mb::tw::split_for(g, n);
-    float *dp = b.alloc<float>((size_t)sp.splits * n * rows);
-    if (!dp) return 1;
-    g.p.d = dp;
-    if (mb::tw::launch(g, n, 0)) return 1;
-    MB_CHECK(cudaDeviceSynchronize());
-    int herr = 0;
-    MB_CHECK(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (herr) {
-        fprintf(stderr, "mocha_tw_gemm_check: kernel reported error %d\n", herr);
         return 1;
     }
     std::vector<float> part((size_t)sp.splits * n * rows);

@@ -88,8 +88,6 @@ _SIGS = {
                                          C.POINTER(MochaSampling), C.c_void_p, C.c_void_p]),
     "mocha_tq_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
-    "mocha_tw_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
-                                      C.c_void_p, C.c_int]),
     "mocha_tc_gemm_check": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
 }

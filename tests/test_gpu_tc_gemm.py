@@ -50,18 +50,3 @@ def test_int8_limb_gemm_matches_fp64(native, rows, n, cols, splits):
     assert np.all(np.isfinite(y))
     assert np.all(err <= 2e-5 * bound + 1e-30), float((err / bound).max())
 
-
-@pytest.mark.parametrize("rows,n,cols,splits", [
-    (128, 64, 64, 1),       # one tile, one stage
-    (1152, 64, 896, 0),     # fused q/k/v rows, decode batch, K split by the plan
-    (896, 37, 4864, 0),     # down projection, ragged batch
-    (384, 200, 896, 2),     # 256-row N tile, ragged
-    (9728, 1024, 896, 1),   # gate|up rows of a 1024-token prompt
-    (256, 100, 128, 1),     # 128-row N tile
-])
-def test_converted_weight_gemm_matches_fp64(native, rows, n, cols, splits):
-    """int8 weights widened to bf16 pairs on chip against bf16-pair activations."""
-    y, ref, bound = run(native, rows, n, cols, splits, seed=2, entry="mocha_tw_gemm_check")
-    err = np.abs(y - ref)
-    assert np.all(np.isfinite(y))
-    assert np.all(err <= 2e-5 * bound + 1e-30), float((err / bound).max())
