@@ -95,6 +95,10 @@ struct mocha_q8 {
     bool stream_done = true;
     cudaGraphExec_t g_forward[2] = {nullptr, nullptr};
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
+    // kStepsPerGraph consecutive prompt / decode steps in one graph: each step reads the
+    // token and position the previous one wrote, as with separate launches, and the
+    // steps follow each other as kernel nodes of one graph instead of graph launches
+    cudaGraphExec_t g_prefill_n = nullptr, g_decode_n = nullptr;
     cudaEvent_t ev[4] = {};
     // persistent one-launch-per-token path (default) and its state
     bool persistent = true;
@@ -147,10 +151,40 @@ q8::Mat mat_of(const unsigned char *base, const q8::FileTensor &t)
     return q8::Mat{(const int8_t *)(base + t.data), (const float *)(base + t.scales)};
 }
 
-int capture(mocha_q8 *h, cudaGraphExec_t *out, int kind)
+constexpr int kStepsPerGraph = 8;
+int enqueue_one(mocha_q8 *h, int kind);
+
+int capture(mocha_q8 *h, cudaGraphExec_t *out, int kind, int steps = 1)
 {
     cudaGraph_t g = nullptr;
     TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = 0;
+    for (int i = 0; i < steps && !rc; i++) rc = enqueue_one(h, kind);
+    const cudaError_t end = cudaStreamEndCapture(h->stream, &g);
+    if (rc || end != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        fprintf(stderr, "CUDA graph capture failed: %s\n", cudaGetErrorString(end));
+        return 1;
+    }
+    const cudaError_t inst = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    TRY(inst);
+    return 0;
+}
+
+// Launch `count` prompt (kind 2) or decode (kind 3) steps: whole graphs of
+// kStepsPerGraph, then single steps.
+int launch_steps(mocha_q8 *h, int kind, int count)
+{
+    cudaGraphExec_t one = kind == 2 ? h->g_prefill : h->g_decode, many = kind == 2 ? h->g_prefill_n : h->g_decode_n;
+    for (; count >= kStepsPerGraph; count -= kStepsPerGraph) TRY(cudaGraphLaunch(many, h->stream));
+    for (; count > 0; count--) TRY(cudaGraphLaunch(one, h->stream));
+    return 0;
+}
+
+// One step of `kind` into the stream being captured.
+int enqueue_one(mocha_q8 *h, int kind)
+{
     int rc = 0;
     if (h->persistent) {
         static const int modes[4] = {q8p::FORWARD, q8p::FORWARD_PROJECT, q8p::PREFILL, q8p::DECODE};
@@ -172,16 +206,7 @@ int capture(mocha_q8 *h, cudaGraphExec_t *out, int kind)
             rc = sampling::enqueue_sample(h->d_keys, h->d_params, h->d_seq, &h->b.st->token, &h->b.st->pos,
                                           h->d_out, h->d_out_count, h->stream);
     }
-    const cudaError_t end = cudaStreamEndCapture(h->stream, &g);
-    if (rc || end != cudaSuccess) {
-        if (g) cudaGraphDestroy(g);
-        fprintf(stderr, "CUDA graph capture failed: %s\n", cudaGetErrorString(end));
-        return 1;
-    }
-    const cudaError_t inst = cudaGraphInstantiate(out, g, 0);
-    cudaGraphDestroy(g);
-    TRY(inst);
-    return 0;
+    return rc;
 }
 
 int alloc_common(mocha_q8 *h)
@@ -289,7 +314,8 @@ int open_full(mocha_q8 *h, int device, const void *file, size_t bytes)
     TRY(cudaHostGetDevicePointer(&h->d_err, h->h_err, 0));
     *h->h_err = 0;
     if (capture(h, &h->g_forward[0], 0) || capture(h, &h->g_forward[1], 1) || capture(h, &h->g_prefill, 2) ||
-        capture(h, &h->g_decode, 3))
+        capture(h, &h->g_decode, 3) || capture(h, &h->g_prefill_n, 2, kStepsPerGraph) ||
+        capture(h, &h->g_decode_n, 3, kStepsPerGraph))
         return 1;
     TRY(cudaStreamSynchronize(h->stream));
     return 0;
@@ -304,6 +330,8 @@ void release(mocha_q8 *h)
         if (g) cudaGraphExecDestroy(g);
     if (h->g_prefill) cudaGraphExecDestroy(h->g_prefill);
     if (h->g_decode) cudaGraphExecDestroy(h->g_decode);
+    if (h->g_prefill_n) cudaGraphExecDestroy(h->g_prefill_n);
+    if (h->g_decode_n) cudaGraphExecDestroy(h->g_decode_n);
     for (auto e : h->ev)
         if (e) cudaEventDestroy(e);
     void *dev[] = {h->d_file, h->dm, h->b.x, h->b.q, h->b.kc, h->b.vc, h->b.partial, h->b.h, h->b.logits,
@@ -663,11 +691,11 @@ extern "C" int mocha_q8_generate(mocha_q8 *h, const int *prompt, int n_prompt, i
     }
     if (begin_sequence(h, prompt, n_prompt, s)) return 1;
     TRY(cudaEventRecord(h->ev[0], h->stream));
-    for (int p = 0; p + 1 < n_prompt; p++) TRY(cudaGraphLaunch(h->g_prefill, h->stream));
+    if (launch_steps(h, 2, n_prompt - 1)) return 1;
     TRY(cudaEventRecord(h->ev[1], h->stream));
     TRY(cudaGraphLaunch(h->g_decode, h->stream));  // first sampled token (not in DECODE_TPS)
     TRY(cudaEventRecord(h->ev[2], h->stream));
-    for (int i = 1; i < n_new; i++) TRY(cudaGraphLaunch(h->g_decode, h->stream));
+    if (launch_steps(h, 3, n_new - 1)) return 1;
     TRY(cudaEventRecord(h->ev[3], h->stream));
     TRY(cudaStreamSynchronize(h->stream));
     if (check_device_error(h)) return 1;
@@ -698,7 +726,7 @@ extern "C" int mocha_q8_stream_begin(mocha_q8 *h, const int *prompt, int n_promp
         return 1;
     }
     if (begin_sequence(h, prompt, n_prompt, s)) return 1;
-    for (int p = 0; p + 1 < n_prompt; p++) TRY(cudaGraphLaunch(h->g_prefill, h->stream));
+    if (launch_steps(h, 2, n_prompt - 1)) return 1;
     h->stream_total = n_new;
     h->stream_read = 0;
     h->stream_enqueued = 0;
