@@ -92,8 +92,9 @@ int mocha_q8_trace_step(mocha_q8 *h, int token, int pos, unsigned long long *sta
  * set to -1e30 (it only touches rows past 151643).  All device buffers live in one
  * fixed ~672 KiB __device__ array, so 1 <= k <= min(64, rows) and rows <= 151936;
  * other requests fail with a message.  The first call on a device looks the array's
- * address up (make it before any stream capture on that device); calls that overlap
- * on the GPU share the array and race. */
+ * address up (make it before any stream capture on that device); a call on a stream
+ * that is being captured fails with a message; calls that overlap on the GPU share
+ * the array and race. */
 int mocha_topk_static(const float *logits, int rows, const int *history, int count, float penalty, int k,
                       float *values, int *ids, void *stream);
 

@@ -95,9 +95,16 @@ extern "C" int mocha_topk_static(const float *logits, int rows, const int *histo
         fprintf(stderr, "mocha_topk_static: k=%d exceeds rows=%d\n", k, rows);
         return 1;
     }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // the call copies to and from host stack buffers and waits for the stream: inside a
+    // capture it would invalidate the capture, so it refuses instead
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess || capturing != cudaStreamCaptureStatusNone) {
+        fprintf(stderr, "mocha_topk_static: the stream is being captured (the call waits for it); call it outside a capture\n");
+        return 1;
+    }
     unsigned char *base = scratch_for_current_device();
     if (!base) return 1;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     float *d_logits = reinterpret_cast<float *>(base + kLogitsOff);
     int *d_hist = reinterpret_cast<int *>(base + kHistOff);
     sampling::Params *d_params = reinterpret_cast<sampling::Params *>(base + kParamsOff);

@@ -64,3 +64,30 @@ def test_static_topk_matches_collect(native, q8_model_bytes, golden_q8):
                                      ids.ctypes.data, None) == 1
     finally:
         assert lib.gpu_finish() == 0
+
+
+def test_static_topk_refuses_a_capturing_stream(native):
+    """A call on a stream that is being captured fails with a message instead of
+    synchronising the stream and invalidating the capture."""
+    import ctypes
+
+    import torch
+    lib = native.load()
+    logits = np.zeros(1000, np.float32)
+    vals = np.empty(4, np.float32)
+    ids = np.empty(4, np.int32)
+    x = torch.zeros(4, device="cuda")
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        g.capture_begin()
+        try:
+            x.add_(1.0)  # the captured graph is not empty
+            rc = lib.mocha_topk_static(logits.ctypes.data, 1000, None, 0, 1.0, 4, vals.ctypes.data,
+                                       ids.ctypes.data, ctypes.c_void_p(s.cuda_stream))
+        finally:
+            g.capture_end()
+    assert rc == 1
+    g.replay()
+    torch.cuda.synchronize()
+    assert x.tolist() == [1.0, 1.0, 1.0, 1.0]
