@@ -238,27 +238,48 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_post(const float *__restric
     }
 }
 
-// Combine the chunks of one (row, head) into the attention output, as limbs for the O
-// GEMM (one warp, two dims per lane: the head is one 64-group).
-__global__ void __launch_bounds__(32) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out, int per)
+// Combine the key spans of (row, head) pairs into the attention output, as limbs for
+// the O GEMM: one warp per pair, two dims per lane (the head is one 64-group), kCombWarps
+// pairs per CTA (one-warp CTAs left the SMs at half their warps: an SM holds at most 32
+// CTAs), the spans' partials loaded before the first use (at most kCombSpans of `per`
+// keys each).
+constexpr int kCombWarps = 8;
+template <int kCombSpans>
+__global__ void __launch_bounds__(32 * kCombWarps) k_attn_combine(const float *__restrict__ part, Rows rows, Limbs out,
+                                                                   int per, int n)
 {
     pdl_enter();
-    const int h = blockIdx.x, t = blockIdx.y, d = 2 * threadIdx.x;
+    const int pair = blockIdx.x * kCombWarps + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (pair >= n * HEADS) return;  // whole warps
+    const int t = pair / HEADS, h = pair % HEADS, d = 2 * lane;
     if (rows.pos[t] < per) return;  // one span: k_attn_tc wrote the row's limbs
-    const int nc = rows.pos[t] / per + 1;  // partials of `per` keys each
+    const int nc = min(rows.pos[t] / per + 1, kCombSpans);  // partials of `per` keys each
     const float *p = part + ((size_t)t * HEADS + h) * NCHUNK * PART;
-    float m = -INFINITY;
-    for (int c = 0; c < nc; c++) m = fmaxf(m, p[c * PART]);
-    float l = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int c = 0; c < nc; c++) {
-        const float w = expf(p[c * PART] - m);
-        l += p[c * PART + 1] * w;
-        a0 += p[c * PART + 2 + d] * w;
-        a1 += p[c * PART + 3 + d] * w;
+    float pm[kCombSpans], pl[kCombSpans], pa[kCombSpans], pb[kCombSpans];
+#pragma unroll
+    for (int c = 0; c < kCombSpans; c++) {
+        const bool in = c < nc;
+        pm[c] = in ? p[c * PART] : -INFINITY;
+        pl[c] = in ? p[c * PART + 1] : 0.f;
+        pa[c] = in ? p[c * PART + 2 + d] : 0.f;
+        pb[c] = in ? p[c * PART + 3 + d] : 0.f;
     }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kCombSpans; c++)
+        if (c < nc) m = fmaxf(m, pm[c]);
+    float l = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < kCombSpans; c++)
+        if (c < nc) {
+            const float w = expf(pm[c] - m);
+            l += pl[c] * w;
+            a0 += pa[c] * w;
+            a1 += pb[c] * w;
+        }
     const float v[2] = {a0 / l, a1 / l};
     mb::tq::store_limbs<2, 32>(v, out.q + (size_t)t * 3 * DIM, DIM, h * HEAD_DIM + d,
-                               out.s + (size_t)t * (DIM / GROUP) + h, threadIdx.x);
+                               out.s + (size_t)t * (DIM / GROUP) + h, lane);
 }
 
 // Rows of any shape: the attention of one row (one query position) for one KV head
@@ -1214,7 +1235,8 @@ int enqueue_attention(mocha_q8b *h, Rows rows, int n, int layer, int block, int 
             return 1;
         // rows at positions < TSPAN were finished by k_attn_tc (their block needs one span)
         if (max_pos < TSPAN) return 0;
-        return pdl(k_attn_combine, dim3(HEADS, n), 32, 0, h->stream, h->apart, rows, h->la, TSPAN);
+        return pdl(k_attn_combine<TSPLIT>, dim3((HEADS * n + kCombWarps - 1) / kCombWarps), 32 * kCombWarps, 0,
+                   h->stream, h->apart, rows, h->la, TSPAN, n);
     }
     if (block) {
         if (!attr_done[h->device & 63]) {
