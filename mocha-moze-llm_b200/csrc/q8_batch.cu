@@ -499,7 +499,8 @@ constexpr int TSPLIT = CONTEXT / TSPAN;
 constexpr uint32_t kTileQ = TQ * HEAD_DIM * 2;   // 16 KiB: one bf16 [128][64] tile
 constexpr uint32_t kTileK = TK * HEAD_DIM * 2;   // 8 KiB: one bf16 [64][64] tile
 constexpr uint32_t kStageKV = 4 * kTileK;        // K hi, K lo, Vt hi, Vt lo
-constexpr size_t TC_SMEM = 1024 + 2 * kTileQ /*Q*/ + 2 * kStageKV + 2 * kTileQ /*P*/ + 128;
+constexpr int kAttnStages = 1;                   // key chunks in flight per CTA
+constexpr size_t TC_SMEM = 1024 + 2 * kTileQ /*Q*/ + kAttnStages * kStageKV + 2 * kTileQ /*P*/ + 128;
 
 struct AttnMaps {
     CUtensorMap k_hi, k_lo;    // [slot*LAYERS*KV_HEADS*CONTEXT][64], box {64, 64}
@@ -531,8 +532,8 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *q_hi = sm, *q_lo = q_hi + kTileQ, *kv = q_lo + kTileQ;
-    uint8_t *p_hi = kv + 2 * kStageKV, *p_lo = p_hi + kTileQ;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(p_lo + kTileQ);  // [0,1] stage full, [2] S, [3] O, [4] drain
+    uint8_t *p_hi = kv + kAttnStages * kStageKV, *p_lo = p_hi + kTileQ;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(p_lo + kTileQ);  // [0, stages) stage full, [2] S, [3] O, [4] drain
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 5);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -540,9 +541,9 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
     const int krow0 = (((slot * LAYERS + layer) * KV_HEADS + g) * CONTEXT);  // K map row of key 0
     const int vrow0 = (((slot * LAYERS + layer) * KV_HEADS + g) * HEAD_DIM);  // Vt map row of dim 0
     int issued = 0, landed_n = 0;  // thread 0: chunks whose copies were issued / have landed
-    auto issue = [&](int c) {  // TMA of chunk c into stage c & 1 (thread 0)
+    auto issue = [&](int c) {  // TMA of chunk c into stage c % kAttnStages (thread 0)
         issued = c + 1;
-        const int st = c & 1, k0 = key_begin + c * TK;
+        const int st = c % kAttnStages, k0 = key_begin + c * TK;
         uint8_t *b = kv + st * kStageKV;
         mb::as::mbar_expect_tx(&bar[st], kStageKV);
         mb::as::tma_load_2d(b, &maps.k_hi, 0, krow0 + k0, &bar[st]);
@@ -554,8 +555,7 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         for (int i = 0; i < 5; i++) mb::as::mbar_init(&bar[i], 1);
         *abort = 0;
         mb::as::fence_barrier_init();
-        issue(0);
-        if (nch > 1) issue(1);
+        for (int c = 0; c < kAttnStages && c < nch; c++) issue(c);
     }
     if (warp == 0) mb::as::tmem_alloc(tmem_slot, 128);
     for (int ci = tid; ci < TQ * 8; ci += TQ) {
@@ -579,10 +579,10 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int c = 0; c < nch; c++) {
-        const int st = c & 1, k0 = key_begin + c * TK;
+        const int st = c % kAttnStages, k0 = key_begin + c * TK;
         uint8_t *kvs = kv + st * kStageKV;
         if (tid == 0) {
-            const bool landed = mb::as::mbar_wait(&bar[st], (c >> 1) & 1, abort);
+            const bool landed = mb::as::mbar_wait(&bar[st], (c / kAttnStages) & 1, abort);
             if (landed) {
                 landed_n = c + 1;
                 mb::as::tc_fence_after();
@@ -674,7 +674,7 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         }
         mb::as::tc_fence_before();
         __syncthreads();  // stage st, S and P are free again
-        if (tid == 0 && c + 2 < nch) issue(c + 2);
+        if (tid == 0 && c + kAttnStages < nch) issue(c + kAttnStages);
     }
     if (!ok && tid == 0) {
         // every MMA issued so far has finished, and the copies in flight have landed,
@@ -682,7 +682,7 @@ __global__ void __launch_bounds__(TQ, 1) k_attn_tc(const float *__restrict__ q, 
         mb::as::mma_commit(&bar[4]);
         const volatile int never = 0;
         mb::as::mbar_wait(&bar[4], 0, &never);
-        for (int k = landed_n; k < issued; k++) mb::as::mbar_wait(&bar[k & 1], (k >> 1) & 1, &never);
+        for (int k = landed_n; k < issued; k++) mb::as::mbar_wait(&bar[k % kAttnStages], (k / kAttnStages) & 1, &never);
     }
     if (ok && p0 + TQ <= TSPAN) {
         // the block's keys lie in this one span: the row is finished here, as the span
