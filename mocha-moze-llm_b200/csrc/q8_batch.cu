@@ -162,8 +162,9 @@ __global__ void __launch_bounds__(NT) k_embed_norm(Mat embed, Rows rows, const f
 }
 
 // x[t] += sum_s part[s][t]; then the norm of the new x into row dst_row[t] (or t).
-// B: partial loads in flight per thread (8 for the many-split decode GEMMs; 1 keeps
-// the register count, and the occupancy of the prompt passes' thousands of rows, low).
+// B: partial loads in flight per thread (20 for the many-split decode GEMMs: every
+// partial of the down projection's 19 in one round of loads; 1 keeps the register
+// count, and the occupancy of the prompt passes' thousands of rows, low).
 template <int B>
 __global__ void __launch_bounds__(NT) k_residual_norm(float *x, const float *__restrict__ part, int splits,
                                                       long long sstride, const float *__restrict__ gain, Limbs out,
@@ -1302,7 +1303,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
             if (enqueue_attention(h, rows, n, l, block_attention, max_pos)) return 1;
         }
         if (mb::tq::launch(ps.o[l], n, s, &sp)) return 1;
-        if (pdl(sp.splits > 2 ? k_residual_norm<8> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
+        if (pdl(sp.splits > 2 ? k_residual_norm<20> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
                 sp.split_stride, L.ffn_norm, h->lx, nullptr))
             return 1;
         if (mb::tq::launch(ps.gu[l], n, s, &sp)) return 1;  // prompt passes: writes the SwiGLU limbs
@@ -1311,7 +1312,7 @@ int enqueue_forward(mocha_q8b *h, Rows rows, int n, bool decode_set, const int *
             return 1;
         if (mb::tq::launch(ps.down[l], n, s, &sp)) return 1;
         const bool last = l + 1 == LAYERS;
-        if (pdl(sp.splits > 2 ? k_residual_norm<8> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
+        if (pdl(sp.splits > 2 ? k_residual_norm<20> : k_residual_norm<1>, n, NT, 0, s, h->x, h->part, sp.splits,
                 sp.split_stride, last ? h->m.final_norm : h->m.layer[l + 1].attn_norm, last ? h->lhead : h->lx,
                 last ? proj_dst : nullptr))
             return 1;
